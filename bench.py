@@ -1,0 +1,359 @@
+#!/usr/bin/env python
+"""BaseLM per-token decode benchmark (one JSON line on rank 0).
+
+Workloads (seeded synthetic models):
+  cfg2 (default)  28 layers, H=2048, 16x128 heads, 2 KV heads, F=6144, Q8_0; one stream per GPU,
+                  KV prefilled to 1023 positions, decoding towards a 4096 context
+  cfg3            cfg2 with F16 projections
+  cfg1            24 layers at H=1024 (config[0]'s layer), F16 token table, 128-token prefill
+
+A step is one decode token of one stream. `value` is the whole-job aggregate tok/s over all
+GPUs (independent replicas, weights replicated, no collectives on the data path), device-timed
+with CUDA events on the engine's stream, max over ranks. `e2e` is the same metric through the
+C ABI with host buffers: every step copies its token from pinned host memory and reads the
+output hidden state back to the host.
+
+`--impl reference` times the reference's CPU path: the C restatement of the reference shaders
+(oracle/) on all host cores, on the same workload. The reference itself (Rust + Vulkan GLSL)
+cannot be built or run here.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+WORKLOADS = {
+    "cfg2": dict(preset="cfg2", prefill=1023, ctx=4096, desc="BaseLM 28L H2048 16x128 GQA 2 KV F6144 Q8_0"),
+    "cfg3": dict(preset="cfg3", prefill=1023, ctx=4096, desc="BaseLM 28L H2048 16x128 GQA 2 KV F6144 F16"),
+    "cfg1": dict(preset="cfg1", prefill=128, ctx=512, desc="BaseLM 24L H1024 16x64 GQA 2 KV F4096 Q8_0"),
+}
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="cfg2", choices=sorted(WORKLOADS))
+    ap.add_argument("--e2e-steps", type=int, default=None)
+    ap.add_argument("--cpu-seconds", type=float, default=15.0, help="bounded CPU-baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-profile", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", str(rank)))
+    return rank, world, local
+
+
+def model_cache() -> Path:
+    return Path(os.environ.get("VOXGEN_MODEL_CACHE", "/tmp/voxgen_b200_models"))
+
+
+def ensure_model(spec, rank, world, pg_barrier):
+    from voxgen_b200 import synth
+    if rank == 0:
+        p = synth.model_path(spec, model_cache())
+    pg_barrier()
+    if rank != 0:
+        p = synth.model_path(spec, model_cache())
+    return p
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.proc = None
+        self.dev = device_index
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={device_index}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (FileNotFoundError, OSError):
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        rows = [r.split(",") for r in out.strip().splitlines() if r.count(",") >= 8]
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.strip() == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def algorithmic_bytes(info, positions):
+    """Weights + norm weights + KV rows read + KV row written, per token (embedding row added
+    separately). positions: decode positions of the steps."""
+    kv = info["block_count"] * info["kv_dim"] * 2 * 2  # K+V fp16 per position per token
+    base = info["layer_weight_bytes"] + info["norm_weight_bytes"]
+    return [base + kv * (p + 1) + kv for p in positions]
+
+
+def run_reference(args, rank, world):
+    """CPU path of the reference (oracle port) on this host's cores."""
+    if rank != 0:
+        return
+    from oracle import oracle as O
+    from voxgen_b200 import synth
+    wl = WORKLOADS[args.workload]
+    spec = synth.preset(wl["preset"])
+    path = synth.model_path(spec, model_cache())
+    m = O.OracleModel(path)
+    st = O.OracleState(m, wl["ctx"])
+    k, v = synth.kv_prefill(spec, wl["prefill"])
+    toks = synth.token_ids(spec, args.warmup + args.steps)
+    cores = O.threads()
+    # each bench step is one decode token; the run is bounded so that K+W steps end in minutes
+    budget = float(os.environ.get("VOXGEN_REF_SECONDS", "120"))
+    st.write_kv(k, v)
+    for t in toks[: min(args.warmup, 3)]:
+        st.decode_token(int(t))
+    st.write_kv(k, v)
+    t0 = time.perf_counter()
+    n = 0
+    for t in toks[: args.steps]:
+        st.decode_token(int(t))
+        n += 1
+        if time.perf_counter() - t0 > budget:
+            break
+    el = time.perf_counter() - t0
+    val = n / el
+    line = {
+        "metric": "decode tok/s", "value": val, "unit": "tok/s", "n_gpus": world, "steps": n,
+        "warmup": min(args.warmup, 3), "ms_per_step": 1000 * el / n, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
+        "config": {"workload": f"{args.workload}: {wl['desc']}", "positions": [wl["prefill"], wl["prefill"] + n - 1],
+                   "streams_per_gpu": 1, "parallelism": "cpu"},
+        "cpu_baseline": {"value": val, "unit": "tok/s", "cores": cores, "kind": "port",
+                         "sample": f"{n} decode steps from position {wl['prefill']} (C restatement of the "
+                                   f"reference shaders, OpenMP, {cores} threads)"},
+        "e2e": {"value": val, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def cpu_baseline_sample(args, spec, path, wl):
+    """The oracle on the host cores, bounded to about args.cpu_seconds of work."""
+    from oracle import oracle as O
+    from voxgen_b200 import synth
+    m = O.OracleModel(path)
+    st = O.OracleState(m, wl["ctx"])
+    k, v = synth.kv_prefill(spec, wl["prefill"])
+    st.write_kv(k, v)
+    toks = synth.token_ids(spec, 64)
+    st.decode_token(int(toks[0]))  # warm caches
+    t0 = time.perf_counter()
+    n = 0
+    while n < 63 and (n < 2 or time.perf_counter() - t0 < args.cpu_seconds):
+        st.decode_token(int(toks[n + 1]))
+        n += 1
+    el = time.perf_counter() - t0
+    return {"value": n / el, "unit": "tok/s", "cores": O.threads(), "kind": "port",
+            "sample": f"{n} decode steps from position {wl['prefill'] + 1} of {args.workload} "
+                      f"({el:.1f} s, C restatement of the reference shaders, OpenMP)"}
+
+
+def main():
+    args = parse()
+    rank, world, local = dist_env()
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+
+    import torch
+    import torch.distributed as dist
+
+    from voxgen_b200 import api, synth
+
+    torch.cuda.set_device(local)
+    pg = None
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
+        pg = dist.group.WORLD
+
+    def barrier():
+        if pg is not None:
+            dist.barrier()
+
+    wl = WORKLOADS[args.workload]
+    spec = synth.preset(wl["preset"])
+    path = ensure_model(spec, rank, world, barrier)
+    K, W = args.steps, args.warmup
+    need = wl["prefill"] + W + K
+    max_ctx = max(wl["ctx"], need)
+
+    ctx = api.Context(local)
+    model = api.Model(ctx, path)
+    info = model.info
+    eng = api.BaseLmEngine(model, max_ctx)
+    kpre, vpre = synth.kv_prefill(spec, wl["prefill"])
+    toks = synth.token_ids(spec, W + K, seed_index=3000 + rank)
+    stream = torch.cuda.ExternalStream(eng.cuda_stream, device=torch.device("cuda", local))
+
+    # ---- device-timed decode: W warm-up + K timed steps from the prefilled position ----
+    eng.write_kv(kpre, vpre)
+    for t in toks[:W]:
+        eng.decode_token_gpu_only(int(t))
+    eng.sync()
+    p0 = eng.position
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    start.record(stream)
+    for t in toks[W:W + K]:
+        eng.decode_token_gpu_only(int(t))
+    end.record(stream)
+    eng.sync(timeout_s=600)
+    torch.cuda.synchronize()
+    barrier()
+    clk = clocks.stop()
+    ms = start.elapsed_time(end)
+    t_max = torch.tensor([ms], dtype=torch.float64, device="cuda")
+    if pg is not None:
+        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
+    ms_max = float(t_max.item())
+    positions = list(range(p0, p0 + K))
+
+    # ---- e2e through the C ABI with host buffers ----
+    KE = args.e2e_steps or min(K, 500)
+    eng.write_kv(kpre, vpre)
+    host_out = np.empty(info["embedding_length"], np.float32)
+    for t in toks[:min(W, 5)]:
+        eng.decode_token_gpu_only(int(t))
+        eng.output()
+    barrier()
+    torch.cuda.synchronize()
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record(stream)
+    for t in toks[W:W + KE]:
+        eng.decode_token_gpu_only(int(t))          # token id copied from pinned host memory
+        host_out[:] = eng.output()                  # D2H of the final hidden state + sync
+    e_end.record(stream)
+    torch.cuda.synchronize()
+    barrier()
+    e_ms = e_start.elapsed_time(e_end)
+    t_e = torch.tensor([e_ms], dtype=torch.float64, device="cuda")
+    if pg is not None:
+        dist.all_reduce(t_e, op=dist.ReduceOp.MAX)
+    e_ms_max = float(t_e.item())
+
+    # ---- per-kernel roofline: one instrumented step (events around every launch) ----
+    roof = None
+    peak, peak_kind = measured_peaks()
+    prof = None
+    if not args.no_profile:
+        eng.write_kv(kpre, vpre)
+        for t in toks[:3]:
+            eng.profile_step(int(t))       # warm
+        eng.write_kv(kpre, vpre)
+        prof = [eng.profile_step(int(t)) for t in toks[3:8]]
+        rows = [r for step in prof for r in step if r["name"] == "gate_up"]
+        avg_ms = sum(r["ms"] for r in rows) / len(rows)
+        byt = rows[0]["bytes"]
+        ach = byt / (avg_ms * 1e-3) / 1e9
+        roof = {"kernel": "gate_up (fused gate/up matvec + SwiGLU)", "bound": "hbm", "achieved": round(ach, 1),
+                "peak": peak, "unit": "GB/s", "frac": round(ach / peak, 4), "traffic": None,
+                "bytes_per_launch": byt, "avg_launch_ms": round(avg_ms, 5),
+                "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)" if peak_kind == "measured"
+                else "fallback 6650 GB/s"}
+        tr = ROOT / "profiles" / "traffic.json"
+        if tr.exists():
+            t = json.loads(tr.read_text()).get(args.workload, {}).get("gate_up")
+            if t:
+                roof["traffic"] = t
+
+    # ---- whole-step numbers ----
+    bytes_tok = algorithmic_bytes(info, positions)
+    emb_row = info["embedding_length"] * 2
+    avg_bytes = (sum(bytes_tok) / K) + emb_row
+    step_ms = ms_max / K
+    value = world * K / (ms_max / 1e3)
+    e2e_val = world * KE / (e_ms_max / 1e3)
+    line = {
+        "metric": "decode tok/s", "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": K,
+        "warmup": W, "ms_per_step": round(step_ms, 5), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {
+            "workload": f"{args.workload}: {wl['desc']}",
+            "weights": "Q8_0" if info["format"] == 8 else "F16",
+            "compute": "int8/fp16 weights dequantised in registers, fp32 accumulation",
+            "streams_per_gpu": 1, "positions": [positions[0], positions[-1]],
+            "parallelism": f"replicas x{world} (weights replicated, no collectives)",
+            "l2": f"inputs larger than L2: {info['layer_weight_bytes'] / 1e9:.2f} GB of weights per step",
+            "input": "seeded token ids",
+        },
+        "per_stream_tok_s": round(K / (ms_max / 1e3), 2),
+        "step_roofline": {"bound": "hbm", "bytes_per_token": int(avg_bytes),
+                          "achieved": round(avg_bytes / (step_ms * 1e-3) / 1e9, 1), "peak": peak, "unit": "GB/s",
+                          "frac": round(avg_bytes / (step_ms * 1e-3) / 1e9 / peak, 4)},
+        "roofline": roof,
+        "e2e": {"value": round(e2e_val, 2), "unit": "tok/s", "steps": KE, "h2d_bytes_per_step": 4,
+                "d2h_bytes_per_step": info["embedding_length"] * 4 + 64},
+        "gpu_launches": K * (5 * info["block_count"] + 2),
+        "clocks": clk,
+    }
+    if prof:
+        agg = {}
+        for step in prof:
+            for r in step:
+                a = agg.setdefault(r["name"], [0.0, 0, 0])
+                a[0] += r["ms"]
+                a[1] += 1
+                a[2] = r["bytes"]
+        line["kernels"] = {n: {"avg_ms": round(a[0] / a[1], 5), "launches_per_step": a[1] // len(prof),
+                               "gbs": round(a[2] / (a[0] / a[1] * 1e-3) / 1e9, 1)} for n, a in agg.items()}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline_sample(args, spec, path, wl)
+    eng.close()
+    model.close()
+    ctx.close()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if pg is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,64 @@
+"""Builds the native library ``voxgen_b200/libvoxgen_b200.so`` with nvcc for sm_100a.
+
+The library is built in-tree so that it travels with the repository snapshot; there is no
+JIT cache and no CPU fallback. ``build()`` is idempotent: it rebuilds only when a source is
+newer than the library.
+"""
+from __future__ import annotations
+
+import os
+import shutil
+import subprocess
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+ROOT = PKG.parent
+CSRC = PKG / "csrc"
+LIB = PKG / "libvoxgen_b200.so"
+SOURCES = [CSRC / "engine.cu", CSRC / "gguf_loader.cpp"]
+HEADERS = [CSRC / "kernels.cuh", CSRC / "ptx.cuh", CSRC / "gguf_loader.h", ROOT / "include" / "voxgen_cuda.h"]
+
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "--expt-relaxed-constexpr", "-Xcompiler", "-fPIC",
+              "-Xcompiler", "-Wall", "-Xptxas", "-warn-spills"]
+
+
+def nvcc() -> str:
+    for cand in (os.environ.get("NVCC"), shutil.which("nvcc"), "/usr/local/cuda/bin/nvcc"):
+        if cand and Path(cand).exists():
+            return cand
+    raise FileNotFoundError("nvcc not found")
+
+
+def needs_build() -> bool:
+    if not LIB.exists():
+        return True
+    t = LIB.stat().st_mtime
+    return any(p.stat().st_mtime > t for p in SOURCES + HEADERS)
+
+
+def build(force: bool = False, verbose: bool = False) -> Path:
+    if not force and not needs_build():
+        return LIB
+    objdir = PKG / "_build"
+    objdir.mkdir(exist_ok=True)
+    objs = []
+    for src in SOURCES:
+        obj = objdir / (src.name + ".o")
+        cmd = [nvcc(), *ARCH, *NVCC_FLAGS, "-I", str(ROOT / "include"), "-c", str(src), "-o", str(obj)]
+        if verbose:
+            print(" ".join(cmd))
+        subprocess.run(cmd, check=True)
+        objs.append(str(obj))
+    tmp = LIB.with_name(f"libvoxgen_b200.tmp{os.getpid()}.so")
+    cmd = [nvcc(), *ARCH, "-shared", "-o", str(tmp), *objs]
+    if verbose:
+        print(" ".join(cmd))
+    subprocess.run(cmd, check=True)
+    tmp.replace(LIB)
+    return LIB
+
+
+if __name__ == "__main__":
+    import sys
+    print(build(force="--force" in sys.argv, verbose=True))

@@ -1,0 +1,1290 @@
+// C ABI of the B200 BaseLM decode step (include/voxgen_cuda.h).
+//
+// Host side of the hot path: replaces BaseLmEngine (src/baselm.rs:429-1232)
+// and the Vulkan dispatch it records into (src/vulkan.rs). One decode step is
+// one CUDA graph of 5 kernels per layer plus the final norm, all launched with
+// programmatic dependent launch so each kernel's weight stream starts while
+// its predecessor finishes. Position and token live in device memory, so one
+// instantiated graph replays every step.
+#include <cuda_runtime.h>
+#include <sys/mman.h>
+#include <fcntl.h>
+#include <unistd.h>
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstdarg>
+#include <cstring>
+#include <functional>
+#include <map>
+#include <mutex>
+#include <set>
+#include <string>
+#include <thread>
+#include <vector>
+
+#include "../../include/voxgen_cuda.h"
+#include "gguf_loader.h"
+#include "kernels.cuh"
+
+using namespace vg;
+
+// ---------------------------------------------------------------------------
+// handles
+// ---------------------------------------------------------------------------
+struct vg_ctx {
+  int device = 0;
+  int sms = 0;
+  std::string err;
+  std::mutex mu;
+};
+
+namespace {
+
+struct DevMat {
+  uint8_t *w = nullptr;
+  uint32_t rows = 0, cols = 0, row_bytes = 0, type = GGML_Q8_0;
+};
+
+struct Layer {
+  DevMat qkv, o, gateup, down;
+  float *attn_norm = nullptr, *ffn_norm = nullptr;
+};
+
+struct Launch {
+  std::function<cudaError_t(cudaStream_t, bool)> fn;
+  const char *name = "";
+  uint32_t layer = 0;
+  uint64_t bytes = 0;    // algorithmic HBM bytes (attention: per KV row, scaled at run time)
+  bool per_position = false;
+};
+
+constexpr uint32_t kStagingSlots = 16;
+constexpr uint32_t kSmemBudget = 112 * 1024;  // per matvec CTA: two kernels share an SM under PDL
+constexpr uint32_t kSmemMax = 227 * 1024;
+
+std::mutex g_live_mu;
+std::set<const void *> g_live;
+
+void live_add(const void *p) {
+  std::lock_guard<std::mutex> l(g_live_mu);
+  g_live.insert(p);
+}
+void live_del(const void *p) {
+  std::lock_guard<std::mutex> l(g_live_mu);
+  g_live.erase(p);
+}
+bool live(const void *p) {
+  std::lock_guard<std::mutex> l(g_live_mu);
+  return p && g_live.count(p);
+}
+
+std::string strf(const char *f, ...) __attribute__((format(printf, 1, 2)));
+std::string strf(const char *f, ...) {
+  char buf[1024];
+  va_list ap;
+  va_start(ap, f);
+  vsnprintf(buf, sizeof buf, f, ap);
+  va_end(ap);
+  return buf;
+}
+
+[[noreturn]] void fail(int code, const std::string &m) { throw Error{code, m}; }
+
+#define CK(call)                                                                               \
+  do {                                                                                         \
+    cudaError_t e_ = (call);                                                                   \
+    if (e_ != cudaSuccess)                                                                     \
+      fail(e_ == cudaErrorMemoryAllocation ? VG_ENOMEM : VG_ECUDA,                             \
+           strf("%s failed: %s (%s:%d)", #call, cudaGetErrorString(e_), __FILE__, __LINE__)); \
+  } while (0)
+
+uint32_t round_up(uint32_t x, uint32_t a) { return (x + a - 1) / a * a; }
+size_t round_up_sz(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+uint32_t row_bytes_of(uint32_t type, uint32_t cols) {
+  return type == GGML_Q8_0 ? q8_row_bytes(cols) : f16_row_bytes(cols);
+}
+
+// Bounded host wait on an event: spin briefly, then poll with short sleeps.
+int host_wait(cudaEvent_t ev, uint64_t timeout_ns) {
+  const auto t0 = std::chrono::steady_clock::now();
+  for (uint64_t it = 0;; ++it) {
+    cudaError_t e = cudaEventQuery(ev);
+    if (e == cudaSuccess) return VG_OK;
+    if (e != cudaErrorNotReady) fail(VG_ECUDA, strf("cudaEventQuery failed: %s", cudaGetErrorString(e)));
+    const uint64_t el = (uint64_t)std::chrono::duration_cast<std::chrono::nanoseconds>(
+                            std::chrono::steady_clock::now() - t0).count();
+    if (el > timeout_ns) return VG_ETIMEDOUT;
+    if (el > 2000000) std::this_thread::sleep_for(std::chrono::microseconds(20));
+  }
+}
+
+template <class K, class... Args>
+cudaError_t launch_ex(K kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = pdl ? attr : nullptr;
+  cfg.numAttrs = pdl ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, args...);
+}
+
+// ---- matvec planning --------------------------------------------------------
+using MvFn = void (*)(MvParams);
+
+template <Mode M, Pro P>
+MvFn pick_matvec(uint32_t type, uint32_t cols, uint32_t &rw) {
+  const bool big = cols > 4096;
+  rw = big ? 2 : 4;
+  if (type == GGML_Q8_0)
+    return big ? matvec_kernel<WFmt::Q8, M, P, 2> : matvec_kernel<WFmt::Q8, M, P, 4>;
+  return big ? matvec_kernel<WFmt::F16, M, P, 2> : matvec_kernel<WFmt::F16, M, P, 4>;
+}
+
+std::mutex g_attr_mu;
+std::map<std::pair<int, const void *>, int> g_smem_attr;  // (device, fn) -> bytes set
+
+void ensure_smem(const void *fn, int device, uint32_t bytes) {
+  std::lock_guard<std::mutex> l(g_attr_mu);
+  int &cur = g_smem_attr[{device, fn}];
+  if ((int)bytes > cur) {
+    CK(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes));
+    cur = (int)bytes;
+  }
+}
+
+struct MvPlan {
+  MvFn fn = nullptr;
+  dim3 grid;
+  uint32_t smem = 0;
+  MvParams p{};
+};
+
+template <Mode M, Pro P>
+MvPlan plan_matvec(const DevMat &m, int device, uint32_t sms) {
+  MvPlan pl;
+  uint32_t rw = 4;
+  pl.fn = pick_matvec<M, P>(m.type, m.cols, rw);
+  const bool q8 = m.type == GGML_Q8_0;
+  const uint32_t xpad = q8 ? Fmt<WFmt::Q8>::xpad(m.cols) : Fmt<WFmt::F16>::xpad(m.cols);
+  const uint32_t x_bytes = round_up(xpad * 4u, 128u);
+  const uint32_t units = (m.rows + rw - 1) / rw;
+  const uint32_t grid = std::min<uint32_t>(sms, units);
+  const uint32_t per_cta = (units + grid - 1) / grid;
+  const uint32_t slot = rw * m.row_bytes;
+  uint32_t budget = kSmemBudget > x_bytes + 1024 ? kSmemBudget - x_bytes - 1024 : 0;
+  uint32_t slots = std::max<uint32_t>(1u, std::min<uint32_t>(budget / slot, per_cta));
+  uint32_t smem = matvec_smem_bytes(x_bytes, slots, slot);
+  while (smem > kSmemMax && slots > 1) smem = matvec_smem_bytes(x_bytes, --slots, slot);
+  if (smem > kSmemMax) fail(VG_EUNSUPPORTED, strf("matrix rows of %u columns do not fit in shared memory", m.cols));
+  pl.grid = dim3(grid);
+  pl.smem = smem;
+  pl.p.w = m.w;
+  pl.p.rows = m.rows;
+  pl.p.cols = m.cols;
+  pl.p.row_bytes = m.row_bytes;
+  pl.p.units = units;
+  pl.p.slots = slots;
+  pl.p.x_bytes = x_bytes;
+  ensure_smem((const void *)pl.fn, device, smem);
+  return pl;
+}
+
+cudaError_t run_matvec(const MvPlan &pl, cudaStream_t st, bool pdl) {
+  return launch_ex(pl.fn, pl.grid, dim3(kMatvecThreads), pl.smem, st, pdl, pl.p);
+}
+
+using AttnFn = void (*)(AttnParams);
+AttnFn pick_attention(uint32_t head_dim) {
+  switch (head_dim) {
+    case 32: return attention_kernel<1>;
+    case 64: return attention_kernel<2>;
+    case 128: return attention_kernel<4>;
+    default: return attention_kernel<8>;
+  }
+}
+
+}  // namespace
+
+struct vg_model {
+  vg_ctx *ctx = nullptr;
+  BaseLmConfig cfg;
+  GgufSummary summary;
+  uint8_t *arena = nullptr;
+  size_t arena_bytes = 0;
+  std::vector<Layer> layers;
+  DevMat tok, out;
+  float *out_norm = nullptr, *inv_freq = nullptr, *ext = nullptr;
+  bool rope_ok = true;
+  vg_model_info info{};
+  int streams = 0;
+};
+
+struct vg_stream {
+  vg_model *m = nullptr;
+  uint32_t max_ctx = 0, pos = 0, nsplit = 0, chunk_cap = 0;
+  cudaStream_t st = nullptr;
+  __half *kc = nullptr, *vc = nullptr;  // [layer][kv_head][max_ctx][head_dim]
+  float *hid_a = nullptr, *hid_b = nullptr, *q = nullptr, *attn = nullptr, *gate = nullptr;
+  float *out_norm = nullptr, *logits = nullptr, *part = nullptr;
+  uint32_t *tickets = nullptr, *ctrl = nullptr;
+  void *dev_block = nullptr;
+  // pinned staging: kStagingSlots x (token + H floats), and the output block
+  uint8_t *pin_in = nullptr;
+  size_t pin_in_stride = 0;
+  cudaEvent_t pin_ev[kStagingSlots] = {};
+  uint32_t pin_next = 0;
+  uint8_t *pin_out = nullptr;
+  cudaEvent_t ev_done = nullptr;
+  cudaGraphExec_t graphs[2][2] = {{nullptr, nullptr}, {nullptr, nullptr}};  // [token_input][logits]
+  bool logits_valid = false;
+};
+
+namespace {
+
+void set_err(vg_ctx *c, const std::string &msg) {
+  if (!c) return;
+  std::lock_guard<std::mutex> l(c->mu);
+  c->err = msg;
+}
+
+template <class F>
+int guard(vg_ctx *c, F &&f) {
+  try {
+    return f();
+  } catch (const Error &e) {
+    set_err(c, e.msg);
+    return e.code;
+  } catch (const std::bad_alloc &) {
+    set_err(c, "host allocation failed");
+    return VG_ENOMEM;
+  } catch (const std::exception &e) {
+    set_err(c, e.what());
+    return VG_EINVAL;
+  }
+}
+
+void fill_info(vg_model *m) {
+  const BaseLmConfig &c = m->cfg;
+  vg_model_info &i = m->info;
+  i.context_length = c.context_length;
+  i.embedding_length = c.embedding_length;
+  i.block_count = c.block_count;
+  i.feed_forward_length = c.feed_forward_length;
+  i.vocab_size = c.vocab_size;
+  i.head_count = c.head_count;
+  i.head_count_kv = c.head_count_kv;
+  i.head_dim = c.head_dim;
+  i.kv_dim = c.kv_dim;
+  i.rope_original_context_length = c.rope_original_context_length;
+  i.rms_epsilon = c.rms_epsilon;
+  i.rope_theta = c.rope_theta;
+  i.rope_scaling_factor = c.rope_scaling_factor();
+  i.embedding_scale = c.embedding_scale;
+  i.residual_scale = c.residual_scale;
+  i.logit_scale = c.logit_scale;
+  i.format = (int32_t)c.format;
+  i.tied_output = c.tied_output;
+  i.rope_long_factors = c.rope_scaling_type == "longrope" && c.rope_long();
+  i.gguf_data_bytes = m->summary.file_bytes - m->summary.data_offset;
+  uint64_t lw = 0;
+  for (uint32_t l = 0; l < c.block_count; ++l)
+    for (const char *s : {"attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up", "ffn_down"})
+      lw += m->summary.find(strf("blk.%u.%s.weight", l, s))->bytes;
+  i.layer_weight_bytes = lw;
+  i.norm_weight_bytes = (uint64_t)(2 * c.block_count + 1) * c.embedding_length * 4;
+  i.device_weight_bytes = m->arena_bytes;
+}
+
+float eff_scale(float v) { return v == 0.0f ? 1.0f : v; }  // effective_scale, src/baselm.rs:1262-1264
+
+void load_model(vg_model *m, const std::string &path, uint32_t requested) {
+  m->summary = load_summary(path);
+  m->cfg = config_from_gguf(m->summary, requested);
+  check_kernel_support(m->summary, m->cfg);
+  const BaseLmConfig &c = m->cfg;
+  const GgufSummary &S = m->summary;
+  const uint32_t H = c.embedding_length, F = c.feed_forward_length, KV = c.kv_dim;
+
+  // ---- arena layout ----
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    size_t o = off;
+    off = round_up_sz(off + bytes, 256);
+    return o;
+  };
+  struct Pending {
+    DevMat *mat;
+    size_t off;
+  };
+  std::vector<Pending> mats;
+  std::vector<std::pair<float **, size_t>> vecs;
+  m->layers.resize(c.block_count);
+  auto tensor = [&](const std::string &n) -> const TensorInfo & { return *S.find(n); };
+  for (uint32_t l = 0; l < c.block_count; ++l) {
+    Layer &L = m->layers[l];
+    auto nm = [&](const char *s) { return strf("blk.%u.%s.weight", l, s); };
+    const uint32_t tq = tensor(nm("attn_q")).type, to = tensor(nm("attn_output")).type;
+    const uint32_t tg = tensor(nm("ffn_gate")).type, td = tensor(nm("ffn_down")).type;
+    L.qkv = {nullptr, H + 2 * KV, H, row_bytes_of(tq, H), tq};
+    L.o = {nullptr, H, H, row_bytes_of(to, H), to};
+    L.gateup = {nullptr, 2 * F, H, row_bytes_of(tg, H), tg};
+    L.down = {nullptr, H, F, row_bytes_of(td, F), td};
+    for (DevMat *d : {&L.qkv, &L.o, &L.gateup, &L.down}) mats.push_back({d, take((size_t)d->rows * d->row_bytes)});
+    vecs.push_back({&L.attn_norm, take((size_t)H * 4)});
+    vecs.push_back({&L.ffn_norm, take((size_t)H * 4)});
+  }
+  const TensorInfo &tok = tensor("token_embd.weight");
+  m->tok = {nullptr, c.vocab_size, H, row_bytes_of(tok.type, H), tok.type};
+  mats.push_back({&m->tok, take((size_t)m->tok.rows * m->tok.row_bytes)});
+  if (!c.tied_output) {
+    const TensorInfo &o = tensor("output.weight");
+    m->out = {nullptr, c.vocab_size, H, row_bytes_of(o.type, H), o.type};
+    mats.push_back({&m->out, take((size_t)m->out.rows * m->out.row_bytes)});
+  }
+  vecs.push_back({&m->out_norm, take((size_t)H * 4)});
+  vecs.push_back({&m->inv_freq, take((size_t)c.head_dim / 2 * 4)});
+  vecs.push_back({&m->ext, take((size_t)c.head_dim / 2 * 4)});
+  m->arena_bytes = off;
+  CK(cudaMalloc(&m->arena, m->arena_bytes));
+  for (auto &p : mats) p.mat->w = m->arena + p.off;
+  for (auto &v : vecs) *v.first = reinterpret_cast<float *>(m->arena + v.second);
+  if (c.tied_output) m->out = m->tok;
+
+  // ---- upload + repack ----
+  int fd = ::open(path.c_str(), O_RDONLY);
+  if (fd < 0) fail(VG_EIO, "open " + path + " failed");
+  void *map = mmap(nullptr, S.file_bytes, PROT_READ, MAP_PRIVATE, fd, 0);
+  ::close(fd);
+  if (map == MAP_FAILED) fail(VG_EIO, "mmap " + path + " failed");
+  const uint8_t *data = static_cast<const uint8_t *>(map) + S.data_offset;
+  size_t max_raw = 0;
+  for (const auto &t : S.tensors) max_raw = std::max<size_t>(max_raw, t.bytes);
+  uint8_t *staging = nullptr;
+  cudaStream_t st = nullptr;
+  try {
+    CK(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+    CK(cudaMalloc(&staging, max_raw));
+    auto repack = [&](const std::string &name, const DevMat &dst, size_t row0, uint32_t stride, uint32_t offset,
+                      uint32_t pair_group) {
+      const TensorInfo &t = tensor(name);
+      CK(cudaMemcpyAsync(staging, data + t.offset, t.bytes, cudaMemcpyHostToDevice, st));
+      const uint32_t rows = (uint32_t)t.dims[1], cols = (uint32_t)t.dims[0];
+      repack_kernel<<<std::min<uint32_t>(rows, 65535u), 256, 0, st>>>(
+          staging, t.type == GGML_Q8_0, rows, cols, dst.w + row0 * dst.row_bytes, dst.row_bytes, stride, offset,
+          pair_group);
+      CK(cudaGetLastError());
+      CK(cudaStreamSynchronize(st));
+    };
+    auto upload_vec = [&](const std::string &name, float *dst) {
+      const TensorInfo &t = tensor(name);
+      CK(cudaMemcpy(dst, data + t.offset, t.bytes, cudaMemcpyHostToDevice));
+    };
+    for (uint32_t l = 0; l < c.block_count; ++l) {
+      Layer &L = m->layers[l];
+      auto nm = [&](const char *s) { return strf("blk.%u.%s.weight", l, s); };
+      repack(nm("attn_q"), L.qkv, 0, 1, 0, c.head_dim);
+      repack(nm("attn_k"), L.qkv, H, 1, 0, c.head_dim);
+      repack(nm("attn_v"), L.qkv, H + KV, 1, 0, 0);
+      repack(nm("attn_output"), L.o, 0, 1, 0, 0);
+      repack(nm("ffn_gate"), L.gateup, 0, 2, 0, 0);
+      repack(nm("ffn_up"), L.gateup, 0, 2, 1, 0);
+      repack(nm("ffn_down"), L.down, 0, 1, 0, 0);
+      upload_vec(nm("attn_norm"), L.attn_norm);
+      upload_vec(nm("ffn_norm"), L.ffn_norm);
+    }
+    repack("token_embd.weight", m->tok, 0, 1, 0, 0);
+    if (!c.tied_output) repack("output.weight", m->out, 0, 1, 0, 0);
+    upload_vec("output_norm.weight", m->out_norm);
+    // RoPE tables: inv_freq as rope.comp:29-30 computes it, evaluated once on
+    // the host; ext = the factor set record_transformer picks (baselm.rs:902-913).
+    std::vector<float> inv(c.head_dim / 2), ext(c.head_dim / 2, 1.0f);
+    for (uint32_t i = 0; i < c.head_dim / 2; ++i)
+      inv[i] = 1.0f / powf(c.rope_theta, (float)(i * 2u) / (float)c.head_dim);
+    m->rope_ok = c.rope_scaling_type == "longrope";
+    if (m->rope_ok) {
+      const TensorInfo &f = tensor(c.rope_long() ? "rope_factors_long.weight" : "rope_factors_short.weight");
+      std::memcpy(ext.data(), data + f.offset, ext.size() * 4);
+    }
+    CK(cudaMemcpy(m->inv_freq, inv.data(), inv.size() * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(m->ext, ext.data(), ext.size() * 4, cudaMemcpyHostToDevice));
+  } catch (...) {
+    munmap(map, S.file_bytes);
+    if (staging) cudaFree(staging);
+    if (st) cudaStreamDestroy(st);
+    throw;
+  }
+  munmap(map, S.file_bytes);
+  cudaFree(staging);
+  cudaStreamDestroy(st);
+  fill_info(m);
+}
+
+// ---- step recording ---------------------------------------------------------
+// GGUF bytes of one matrix row of `cols` columns (the algorithmic bytes read).
+uint64_t gguf_bytes(uint32_t type, uint32_t cols) {
+  return type == GGML_Q8_0 ? (uint64_t)cols / 32 * 34 : (uint64_t)cols * 2;
+}
+
+void build_program(vg_stream *s, bool token_input, bool logits, std::vector<Launch> &prog) {
+  vg_model *m = s->m;
+  const BaseLmConfig &c = m->cfg;
+  const int dev = m->ctx->device;
+  const uint32_t sms = (uint32_t)m->ctx->sms;
+  const uint32_t H = c.embedding_length, D = c.head_dim, G = c.head_count / c.head_count_kv;
+  const float rs = eff_scale(c.residual_scale);
+  uint32_t *ctrl = s->ctrl;
+  if (token_input) {
+    const DevMat tok = m->tok;
+    const float alpha = eff_scale(c.embedding_scale);
+    float *out = s->hid_a;
+    prog.push_back({[=](cudaStream_t st, bool pdl) {
+      return launch_ex(embedding_kernel, dim3((H + 255) / 256), dim3(256), 0, st, pdl, (const uint8_t *)tok.w,
+                       (int)(tok.type == GGML_Q8_0), tok.rows, tok.cols, tok.row_bytes,
+                       (const uint32_t *)(ctrl + kCtrlToken), 0u, alpha, out, ctrl + kCtrlErr);
+    }, "embedding", 0, gguf_bytes(tok.type, H) + (uint64_t)H * 4});
+  }
+  const AttnFn afn = pick_attention(D);
+  const uint32_t asmem = attention_smem_bytes(G, D, s->chunk_cap, s->nsplit);
+  ensure_smem((const void *)afn, dev, asmem);
+  for (uint32_t l = 0; l < c.block_count; ++l) {
+    const Layer &L = m->layers[l];
+    __half *kc = s->kc + (size_t)l * c.head_count_kv * s->max_ctx * D;
+    __half *vc = s->vc + (size_t)l * c.head_count_kv * s->max_ctx * D;
+    MvPlan qkv = plan_matvec<Mode::QKV, Pro::RMSNORM>(L.qkv, dev, sms);
+    qkv.p.xsrc = s->hid_a;
+    qkv.p.normw = L.attn_norm;
+    qkv.p.eps = c.rms_epsilon;
+    qkv.p.out = s->q;
+    qkv.p.q_rows = H;
+    qkv.p.kv_rows = c.kv_dim;
+    qkv.p.head_dim = D;
+    qkv.p.ctx = s->max_ctx;
+    qkv.p.kc = kc;
+    qkv.p.vc = vc;
+    qkv.p.inv_freq = m->inv_freq;
+    qkv.p.ext = m->ext;
+    qkv.p.rope_scaling = c.rope_scaling_factor();
+    qkv.p.ctrl = ctrl;
+    prog.push_back({[=](cudaStream_t st, bool pdl) { return run_matvec(qkv, st, pdl); }, "qkv", l,
+                    gguf_bytes(L.qkv.type, H) * L.qkv.rows + (uint64_t)H * 4 + 2ull * c.kv_dim * 2});
+
+    AttnParams ap{};
+    ap.q = s->q;
+    ap.kc = kc;
+    ap.vc = vc;
+    ap.out = s->attn;
+    ap.part = s->part;
+    ap.tickets = s->tickets;
+    ap.heads = c.head_count;
+    ap.kv_heads = c.head_count_kv;
+    ap.ctx = s->max_ctx;
+    ap.nsplit = s->nsplit;
+    ap.chunk_cap = s->chunk_cap;
+    ap.scale = 1.0f / sqrtf((float)D);
+    ap.fixed_pos = 0xFFFFFFFFu;
+    ap.ctrl = ctrl;
+    prog.push_back({[=](cudaStream_t st, bool pdl) {
+      return launch_ex(afn, dim3(ap.nsplit, ap.kv_heads), dim3(256), asmem, st, pdl, ap);
+    }, "attention", l, 2ull * c.kv_dim * 2, true});
+
+    MvPlan o = plan_matvec<Mode::RESID, Pro::COPY>(L.o, dev, sms);
+    o.p.xsrc = s->attn;
+    o.p.out = s->hid_b;
+    o.p.resid = s->hid_a;
+    o.p.alpha = rs;
+    o.p.ctrl = ctrl;
+    prog.push_back({[=](cudaStream_t st, bool pdl) { return run_matvec(o, st, pdl); }, "o_proj", l,
+                    gguf_bytes(L.o.type, H) * L.o.rows});
+
+    MvPlan gu = plan_matvec<Mode::SWIGLU, Pro::RMSNORM>(L.gateup, dev, sms);
+    gu.p.xsrc = s->hid_b;
+    gu.p.normw = L.ffn_norm;
+    gu.p.eps = c.rms_epsilon;
+    gu.p.out = s->gate;
+    gu.p.ctrl = ctrl;
+    prog.push_back({[=](cudaStream_t st, bool pdl) { return run_matvec(gu, st, pdl); }, "gate_up", l,
+                    gguf_bytes(L.gateup.type, H) * L.gateup.rows + (uint64_t)H * 4});
+
+    MvPlan dn = plan_matvec<Mode::RESID, Pro::COPY>(L.down, dev, sms);
+    dn.p.xsrc = s->gate;
+    dn.p.out = s->hid_a;
+    dn.p.resid = s->hid_b;
+    dn.p.alpha = rs;
+    dn.p.ctrl = ctrl;
+    prog.push_back({[=](cudaStream_t st, bool pdl) { return run_matvec(dn, st, pdl); }, "down", l,
+                    gguf_bytes(L.down.type, c.feed_forward_length) * L.down.rows});
+  }
+  {
+    float *hid = s->hid_a, *y = s->out_norm;
+    const float *w = m->out_norm;
+    const float eps = c.rms_epsilon;
+    prog.push_back({[=](cudaStream_t st, bool pdl) {
+      return launch_ex(residual_rmsnorm_kernel, dim3(1), dim3(std::min<uint32_t>(1024u, round_up(H, 32))), 0, st,
+                       pdl, hid, (const float *)nullptr, w, H, eps, 1.0f, y, ctrl, 1);
+    }, "final_norm", c.block_count, (uint64_t)H * 4});
+  }
+  if (logits) {
+    MvPlan lg = plan_matvec<Mode::PLAIN, Pro::COPY>(m->out, dev, sms);
+    lg.p.xsrc = s->out_norm;
+    lg.p.out = s->logits;
+    lg.p.alpha = eff_scale(c.logit_scale);
+    lg.p.ctrl = ctrl;
+    prog.push_back({[=](cudaStream_t st, bool pdl) { return run_matvec(lg, st, pdl); }, "logits", c.block_count,
+                    gguf_bytes(m->out.type, H) * m->out.rows});
+  }
+}
+
+cudaGraphExec_t get_graph(vg_stream *s, bool token_input, bool logits) {
+  cudaGraphExec_t &g = s->graphs[token_input][logits];
+  if (g) return g;
+  std::vector<Launch> prog;
+  build_program(s, token_input, logits, prog);
+  cudaGraph_t graph = nullptr;
+  CK(cudaStreamBeginCapture(s->st, cudaStreamCaptureModeThreadLocal));
+  cudaError_t e = cudaSuccess;
+  for (size_t i = 0; i < prog.size() && e == cudaSuccess; ++i) e = prog[i].fn(s->st, i > 0);
+  cudaError_t e2 = cudaStreamEndCapture(s->st, &graph);
+  if (e != cudaSuccess) {
+    if (graph) cudaGraphDestroy(graph);
+    fail(VG_ECUDA, strf("kernel launch during capture failed: %s", cudaGetErrorString(e)));
+  }
+  CK(e2);
+  e = cudaGraphInstantiate(&g, graph, 0);
+  cudaGraphDestroy(graph);
+  CK(e);
+  return g;
+}
+
+void check_step(vg_stream *s) {
+  if (s->pos >= s->max_ctx)
+    fail(VG_EFULL, strf("BaseLM KV cache is full at %u tokens; reset or increase --max-context", s->max_ctx));
+  if (!s->m->rope_ok) fail(VG_EUNSUPPORTED, "MiniCPM4 BaseLM without LongRoPE factors is not enabled");
+}
+
+uint8_t *staging_slot(vg_stream *s) {
+  const uint32_t i = s->pin_next;
+  s->pin_next = (s->pin_next + 1) % kStagingSlots;
+  int rc = host_wait(s->pin_ev[i], 10ull * 1000000000ull);
+  if (rc) fail(rc, "timed out waiting for a staging buffer");
+  return s->pin_in + (size_t)i * s->pin_in_stride;
+}
+cudaEvent_t staging_event(vg_stream *s) { return s->pin_ev[(s->pin_next + kStagingSlots - 1) % kStagingSlots]; }
+
+void launch_step(vg_stream *s, bool token_input, bool logits) {
+  cudaGraphExec_t g = get_graph(s, token_input, logits);
+  CK(cudaGraphLaunch(g, s->st));
+  s->pos += 1;
+  s->logits_valid = logits;
+}
+
+int sync_stream(vg_stream *s, uint64_t timeout_ns, bool check_flag) {
+  CK(cudaEventRecord(s->ev_done, s->st));
+  int rc = host_wait(s->ev_done, timeout_ns);
+  if (rc) fail(rc, "stream did not finish within the timeout");
+  if (check_flag) {
+    uint32_t flag = 0;
+    CK(cudaMemcpy(&flag, s->ctrl + kCtrlErr, 4, cudaMemcpyDeviceToHost));
+    if (flag) {
+      CK(cudaMemset(s->ctrl + kCtrlErr, 0, 4));
+      fail(VG_EDEVICE, strf("a kernel raised device error flag 0x%x", flag));
+    }
+  }
+  return VG_OK;
+}
+
+void destroy_stream(vg_stream *s) {
+  for (auto &row : s->graphs)
+    for (auto &g : row)
+      if (g) cudaGraphExecDestroy(g);
+  for (auto &e : s->pin_ev)
+    if (e) cudaEventDestroy(e);
+  if (s->ev_done) cudaEventDestroy(s->ev_done);
+  if (s->st) cudaStreamDestroy(s->st);
+  if (s->kc) cudaFree(s->kc);
+  if (s->dev_block) cudaFree(s->dev_block);
+  if (s->pin_in) cudaFreeHost(s->pin_in);
+  if (s->pin_out) cudaFreeHost(s->pin_out);
+}
+
+}  // namespace
+
+// ===========================================================================
+// ABI
+// ===========================================================================
+extern "C" {
+
+int vg_ctx_create(int device, vg_ctx **out) {
+  if (!out) return VG_EINVAL;
+  *out = nullptr;
+  vg_ctx *c = new vg_ctx();
+  c->device = device;
+  int rc = guard(c, [&] {
+    int n = 0;
+    CK(cudaGetDeviceCount(&n));
+    if (device < 0 || device >= n) fail(VG_EINVAL, strf("device %d out of range (%d devices)", device, n));
+    CK(cudaSetDevice(device));
+    CK(cudaDeviceGetAttribute(&c->sms, cudaDevAttrMultiProcessorCount, device));
+    return VG_OK;
+  });
+  if (rc) {
+    delete c;
+    return rc;
+  }
+  live_add(c);
+  *out = c;
+  return VG_OK;
+}
+
+int vg_ctx_destroy(vg_ctx *c) {
+  if (!live(c)) return VG_ESTATE;
+  live_del(c);
+  delete c;
+  return VG_OK;
+}
+
+const char *vg_last_error(const vg_ctx *c) {
+  if (!live(c)) return "invalid or destroyed context";
+  return c->err.c_str();
+}
+
+int vg_ctx_sm_count(const vg_ctx *c, int *out) {
+  if (!live(c) || !out) return live(c) ? VG_EINVAL : VG_ESTATE;
+  *out = c->sms;
+  return VG_OK;
+}
+
+int vg_gguf_inspect(const char *path, int format, vg_model_info *info, char *err, size_t err_len) {
+  if (err && err_len) err[0] = 0;
+  if (!path || !info) return VG_EINVAL;
+  if (format != VG_FORMAT_AUTO && format != VG_FORMAT_Q8_0 && format != VG_FORMAT_F16) return VG_EINVAL;
+  try {
+    vg_model tmp;
+    tmp.summary = load_summary(path);
+    tmp.cfg = config_from_gguf(tmp.summary, (uint32_t)format);
+    check_kernel_support(tmp.summary, tmp.cfg);
+    // device bytes the repack would take (same layout as load_model)
+    const BaseLmConfig &c = tmp.cfg;
+    size_t bytes = 0;
+    auto add = [&](size_t b) { bytes = round_up_sz(bytes + b, 256); };
+    for (uint32_t l = 0; l < c.block_count; ++l) {
+      auto t = [&](const char *s) { return tmp.summary.find(strf("blk.%u.%s.weight", l, s))->type; };
+      add((size_t)(c.embedding_length + 2 * c.kv_dim) * row_bytes_of(t("attn_q"), c.embedding_length));
+      add((size_t)c.embedding_length * row_bytes_of(t("attn_output"), c.embedding_length));
+      add((size_t)2 * c.feed_forward_length * row_bytes_of(t("ffn_gate"), c.embedding_length));
+      add((size_t)c.embedding_length * row_bytes_of(t("ffn_down"), c.feed_forward_length));
+      add((size_t)c.embedding_length * 4);
+      add((size_t)c.embedding_length * 4);
+    }
+    add((size_t)c.vocab_size * row_bytes_of(tmp.summary.find("token_embd.weight")->type, c.embedding_length));
+    if (!c.tied_output)
+      add((size_t)c.vocab_size * row_bytes_of(tmp.summary.find("output.weight")->type, c.embedding_length));
+    add((size_t)c.embedding_length * 4);
+    add((size_t)c.head_dim / 2 * 4);
+    add((size_t)c.head_dim / 2 * 4);
+    tmp.arena_bytes = bytes;
+    fill_info(&tmp);
+    *info = tmp.info;
+    return VG_OK;
+  } catch (const Error &e) {
+    if (err && err_len) snprintf(err, err_len, "%s", e.msg.c_str());
+    return e.code;
+  } catch (const std::exception &e) {
+    if (err && err_len) snprintf(err, err_len, "%s", e.what());
+    return VG_EINVAL;
+  }
+}
+
+int vg_kv_cache_bytes(const vg_model_info *info, uint32_t max_context, uint64_t *bytes) {
+  if (!info || !bytes) return VG_EINVAL;
+  *bytes = (uint64_t)info->block_count * max_context * info->kv_dim * 2 /* fp16 */ * 2 /* K + V */;
+  return VG_OK;
+}
+
+int vg_top_k_logits(const float *logits, uint32_t n, uint32_t k, vg_top_logit *out, uint32_t *n_out) {
+  if ((!logits && n) || (!out && k) || !n_out) return VG_EINVAL;
+  // finite values only, descending; equal values keep index order
+  std::vector<uint32_t> idx;
+  idx.reserve(n);
+  for (uint32_t i = 0; i < n; ++i)
+    if (std::isfinite(logits[i])) idx.push_back(i);
+  const size_t kk = std::min<size_t>(k, idx.size());
+  std::partial_sort(idx.begin(), idx.begin() + kk, idx.end(), [&](uint32_t a, uint32_t b) {
+    return logits[a] > logits[b] || (logits[a] == logits[b] && a < b);
+  });
+  for (size_t i = 0; i < kk; ++i) out[i] = {idx[i], logits[idx[i]]};
+  *n_out = (uint32_t)kk;
+  return VG_OK;
+}
+
+int vg_model_load_gguf(vg_ctx *ctx, const char *path, int format, vg_model **out) {
+  if (!live(ctx)) return VG_ESTATE;
+  if (!path || !out) return VG_EINVAL;
+  *out = nullptr;
+  if (format != VG_FORMAT_AUTO && format != VG_FORMAT_Q8_0 && format != VG_FORMAT_F16) return VG_EINVAL;
+  vg_model *m = new vg_model();
+  m->ctx = ctx;
+  int rc = guard(ctx, [&] {
+    CK(cudaSetDevice(ctx->device));
+    load_model(m, path, (uint32_t)format);
+    return VG_OK;
+  });
+  if (rc) {
+    if (m->arena) cudaFree(m->arena);
+    delete m;
+    return rc;
+  }
+  live_add(m);
+  *out = m;
+  return VG_OK;
+}
+
+int vg_model_info_get(const vg_model *m, vg_model_info *info) {
+  if (!live(m)) return VG_ESTATE;
+  if (!info) return VG_EINVAL;
+  *info = m->info;
+  return VG_OK;
+}
+
+int vg_model_destroy(vg_model *m) {
+  if (!live(m)) return VG_ESTATE;
+  if (m->streams > 0) {
+    set_err(m->ctx, "model still has live streams");
+    return VG_ESTATE;
+  }
+  live_del(m);
+  cudaSetDevice(m->ctx->device);
+  if (m->arena) cudaFree(m->arena);
+  delete m;
+  return VG_OK;
+}
+
+int vg_stream_create(vg_model *m, uint32_t max_context, vg_stream **out) {
+  if (!live(m)) return VG_ESTATE;
+  if (!out) return VG_EINVAL;
+  *out = nullptr;
+  vg_stream *s = new vg_stream();
+  s->m = m;
+  int rc = guard(m->ctx, [&] {
+    const BaseLmConfig &c = m->cfg;
+    // BaseLmConfig::from_gguf, src/baselm.rs:68-72
+    if (max_context == 0 || max_context > c.context_length)
+      fail(VG_EINVAL, strf("--max-context must be in 1..=%u, got %u", c.context_length, max_context));
+    CK(cudaSetDevice(m->ctx->device));
+    s->max_ctx = max_context;
+    const uint32_t H = c.embedding_length, D = c.head_dim, G = c.head_count / c.head_count_kv;
+    s->nsplit = std::max<uint32_t>(16u, (max_context + 2047u) / 2048u);
+    s->chunk_cap = (max_context + s->nsplit - 1) / s->nsplit;
+    const size_t kv_elems = (size_t)c.block_count * c.head_count_kv * max_context * D;
+    CK(cudaMalloc(&s->kc, kv_elems * 2 * sizeof(__half)));
+    s->vc = s->kc + kv_elems;
+    // activations + scratch + control, one allocation
+    size_t off = 0;
+    auto take = [&](size_t b) {
+      size_t o = off;
+      off = round_up_sz(off + b, 256);
+      return o;
+    };
+    const size_t o_out = take((size_t)H * 4), o_ctrl = take(kCtrlWords * 4);
+    const size_t o_a = take((size_t)H * 4), o_b = take((size_t)H * 4), o_q = take((size_t)H * 4),
+                 o_att = take((size_t)H * 4), o_g = take((size_t)c.feed_forward_length * 4),
+                 o_lg = take((size_t)c.vocab_size * 4),
+                 o_part = take((size_t)c.head_count_kv * s->nsplit * G * (D + 2) * 4),
+                 o_tk = take((size_t)c.head_count_kv * 4);
+    CK(cudaMalloc(&s->dev_block, off));
+    CK(cudaMemset(s->dev_block, 0, off));
+    uint8_t *b = static_cast<uint8_t *>(s->dev_block);
+    s->out_norm = (float *)(b + o_out);
+    s->ctrl = (uint32_t *)(b + o_ctrl);
+    s->hid_a = (float *)(b + o_a);
+    s->hid_b = (float *)(b + o_b);
+    s->q = (float *)(b + o_q);
+    s->attn = (float *)(b + o_att);
+    s->gate = (float *)(b + o_g);
+    s->logits = (float *)(b + o_lg);
+    s->part = (float *)(b + o_part);
+    s->tickets = (uint32_t *)(b + o_tk);
+    CK(cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking));
+    CK(cudaEventCreateWithFlags(&s->ev_done, cudaEventDisableTiming));
+    s->pin_in_stride = round_up_sz(16 + (size_t)H * 4, 256);
+    CK(cudaMallocHost(&s->pin_in, s->pin_in_stride * kStagingSlots));
+    for (auto &e : s->pin_ev) {
+      CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+      CK(cudaEventRecord(e, s->st));
+    }
+    CK(cudaMallocHost(&s->pin_out, round_up_sz((size_t)std::max(H, c.vocab_size) * 4, 256) + 256));
+    CK(cudaStreamSynchronize(s->st));
+    return VG_OK;
+  });
+  if (rc) {
+    destroy_stream(s);
+    delete s;
+    return rc;
+  }
+  m->streams += 1;
+  live_add(s);
+  *out = s;
+  return VG_OK;
+}
+
+int vg_stream_destroy(vg_stream *s) {
+  if (!live(s)) return VG_ESTATE;
+  live_del(s);
+  cudaSetDevice(s->m->ctx->device);
+  cudaStreamSynchronize(s->st);
+  s->m->streams -= 1;
+  destroy_stream(s);
+  delete s;
+  return VG_OK;
+}
+
+int vg_stream_reset(vg_stream *s) {
+  if (!live(s)) return VG_ESTATE;
+  return guard(s->m->ctx, [&] {
+    CK(cudaSetDevice(s->m->ctx->device));
+    // Cache contents stay; they are unreachable once the position is 0 (src/baselm.rs:616-620).
+    CK(cudaMemsetAsync(s->ctrl + kCtrlPos, 0, 4, s->st));
+    s->pos = 0;
+    return VG_OK;
+  });
+}
+
+int vg_stream_position(const vg_stream *s, uint32_t *position) {
+  if (!live(s)) return VG_ESTATE;
+  if (!position) return VG_EINVAL;
+  *position = s->pos;
+  return VG_OK;
+}
+
+int vg_stream_cuda_stream(const vg_stream *s, void **cuda_stream) {
+  if (!live(s)) return VG_ESTATE;
+  if (!cuda_stream) return VG_EINVAL;
+  *cuda_stream = (void *)s->st;
+  return VG_OK;
+}
+
+int vg_stream_write_kv(vg_stream *s, const uint16_t *k, const uint16_t *v, uint32_t n) {
+  if (!live(s)) return VG_ESTATE;
+  if ((!k || !v) && n) return VG_EINVAL;
+  return guard(s->m->ctx, [&] {
+    const BaseLmConfig &c = s->m->cfg;
+    if (n > s->max_ctx) fail(VG_EFULL, strf("%u positions exceed the KV cache of %u", n, s->max_ctx));
+    CK(cudaSetDevice(s->m->ctx->device));
+    CK(cudaStreamSynchronize(s->st));
+    const uint32_t D = c.head_dim;
+    for (uint32_t l = 0; l < c.block_count && n; ++l)
+      for (uint32_t h = 0; h < c.head_count_kv; ++h) {
+        const size_t dst = ((size_t)l * c.head_count_kv + h) * s->max_ctx * D;
+        const size_t src = (size_t)l * n * c.kv_dim + (size_t)h * D;
+        CK(cudaMemcpy2D(s->kc + dst, D * 2, k + src, c.kv_dim * 2, D * 2, n, cudaMemcpyHostToDevice));
+        CK(cudaMemcpy2D(s->vc + dst, D * 2, v + src, c.kv_dim * 2, D * 2, n, cudaMemcpyHostToDevice));
+      }
+    CK(cudaMemcpy(s->ctrl + kCtrlPos, &n, 4, cudaMemcpyHostToDevice));
+    s->pos = n;
+    return VG_OK;
+  });
+}
+
+int vg_stream_read_kv(vg_stream *s, uint16_t *k, uint16_t *v, uint32_t n) {
+  if (!live(s)) return VG_ESTATE;
+  if ((!k || !v) && n) return VG_EINVAL;
+  return guard(s->m->ctx, [&] {
+    const BaseLmConfig &c = s->m->cfg;
+    if (n > s->max_ctx) fail(VG_EINVAL, strf("%u positions exceed the KV cache of %u", n, s->max_ctx));
+    CK(cudaSetDevice(s->m->ctx->device));
+    sync_stream(s, 60ull * 1000000000ull, false);
+    const uint32_t D = c.head_dim;
+    for (uint32_t l = 0; l < c.block_count && n; ++l)
+      for (uint32_t h = 0; h < c.head_count_kv; ++h) {
+        const size_t src = ((size_t)l * c.head_count_kv + h) * s->max_ctx * D;
+        const size_t dst = (size_t)l * n * c.kv_dim + (size_t)h * D;
+        CK(cudaMemcpy2D(k + dst, c.kv_dim * 2, s->kc + src, D * 2, D * 2, n, cudaMemcpyDeviceToHost));
+        CK(cudaMemcpy2D(v + dst, c.kv_dim * 2, s->vc + src, D * 2, D * 2, n, cudaMemcpyDeviceToHost));
+      }
+    return VG_OK;
+  });
+}
+
+int vg_decode_token(vg_stream *s, uint32_t token, int want_logits) {
+  if (!live(s)) return VG_ESTATE;
+  return guard(s->m->ctx, [&] {
+    if (token >= s->m->cfg.vocab_size)
+      fail(VG_ERANGE, strf("token id %u is outside vocabulary 0..%u", token, s->m->cfg.vocab_size));
+    check_step(s);
+    CK(cudaSetDevice(s->m->ctx->device));
+    uint8_t *slot = staging_slot(s);
+    std::memcpy(slot, &token, 4);
+    CK(cudaMemcpyAsync(s->ctrl + kCtrlToken, slot, 4, cudaMemcpyHostToDevice, s->st));
+    CK(cudaEventRecord(staging_event(s), s->st));
+    launch_step(s, true, want_logits != 0);
+    return VG_OK;
+  });
+}
+
+int vg_decode_embedding(vg_stream *s, const float *host, int want_logits) {
+  if (!live(s)) return VG_ESTATE;
+  if (!host) return VG_EINVAL;
+  return guard(s->m->ctx, [&] {
+    check_step(s);
+    CK(cudaSetDevice(s->m->ctx->device));
+    const size_t bytes = (size_t)s->m->cfg.embedding_length * 4;
+    uint8_t *slot = staging_slot(s);
+    std::memcpy(slot + 16, host, bytes);
+    CK(cudaMemcpyAsync(s->hid_a, slot + 16, bytes, cudaMemcpyHostToDevice, s->st));
+    CK(cudaEventRecord(staging_event(s), s->st));
+    launch_step(s, false, want_logits != 0);
+    return VG_OK;
+  });
+}
+
+int vg_decode_embedding_device(vg_stream *s, const float *dev, int want_logits) {
+  if (!live(s)) return VG_ESTATE;
+  if (!dev) return VG_EINVAL;
+  return guard(s->m->ctx, [&] {
+    check_step(s);
+    CK(cudaSetDevice(s->m->ctx->device));
+    CK(cudaMemcpyAsync(s->hid_a, dev, (size_t)s->m->cfg.embedding_length * 4, cudaMemcpyDeviceToDevice, s->st));
+    launch_step(s, false, want_logits != 0);
+    return VG_OK;
+  });
+}
+
+int vg_prefill_tokens(vg_stream *s, const uint32_t *tokens, uint32_t n, int want_logits_last) {
+  if (!live(s)) return VG_ESTATE;
+  if (n == 0) {
+    set_err(s->m->ctx, "prefill token list is empty");
+    return VG_EINVAL;
+  }
+  if (!tokens) return VG_EINVAL;
+  for (uint32_t i = 0; i < n; ++i) {
+    int rc = vg_decode_token(s, tokens[i], (i + 1 == n) ? want_logits_last : 0);
+    if (rc) return rc;
+  }
+  return VG_OK;
+}
+
+int vg_stream_output(const vg_stream *s, const float **dev) {
+  if (!live(s)) return VG_ESTATE;
+  if (!dev) return VG_EINVAL;
+  *dev = s->out_norm;
+  return VG_OK;
+}
+
+int vg_stream_logits(const vg_stream *s, const float **dev) {
+  if (!live(s)) return VG_ESTATE;
+  if (!dev) return VG_EINVAL;
+  *dev = s->logits;
+  return VG_OK;
+}
+
+static int copy_out(vg_stream *s, const float *src, float *host, size_t n, size_t limit) {
+  return guard(s->m->ctx, [&] {
+    if (n > limit) fail(VG_EINVAL, strf("requested %zu floats, buffer holds %zu", n, limit));
+    CK(cudaSetDevice(s->m->ctx->device));
+    // output block = out_norm then ctrl: one copy brings back the flag too
+    const bool with_flag = src == s->out_norm;
+    const size_t bytes = with_flag ? (size_t)((uint8_t *)(s->ctrl + kCtrlWords) - (uint8_t *)s->out_norm) : n * 4;
+    CK(cudaMemcpyAsync(s->pin_out, src, bytes, cudaMemcpyDeviceToHost, s->st));
+    CK(cudaEventRecord(s->ev_done, s->st));
+    int rc = host_wait(s->ev_done, 30ull * 1000000000ull);
+    if (rc) fail(rc, "output copy did not finish within the timeout");
+    if (with_flag) {
+      uint32_t flag;
+      std::memcpy(&flag, s->pin_out + ((uint8_t *)(s->ctrl + kCtrlErr) - (uint8_t *)s->out_norm), 4);
+      if (flag) {
+        CK(cudaMemset(s->ctrl + kCtrlErr, 0, 4));
+        fail(VG_EDEVICE, strf("a kernel raised device error flag 0x%x", flag));
+      }
+    }
+    std::memcpy(host, s->pin_out, n * 4);
+    return VG_OK;
+  });
+}
+
+int vg_copy_output(vg_stream *s, float *host, size_t n) {
+  if (!live(s)) return VG_ESTATE;
+  if (!host && n) return VG_EINVAL;
+  return copy_out(s, s->out_norm, host, n, s->m->cfg.embedding_length);
+}
+
+int vg_copy_logits(vg_stream *s, float *host, size_t n) {
+  if (!live(s)) return VG_ESTATE;
+  if (!host && n) return VG_EINVAL;
+  return copy_out(s, s->logits, host, n, s->m->cfg.vocab_size);
+}
+
+int vg_stream_sync(vg_stream *s, uint64_t timeout_ns) {
+  if (!live(s)) return VG_ESTATE;
+  return guard(s->m->ctx, [&] {
+    CK(cudaSetDevice(s->m->ctx->device));
+    return sync_stream(s, timeout_ns, true);
+  });
+}
+
+int vg_step_result_get(vg_stream *s, uint32_t top_k, vg_step_result *res, vg_top_logit *top) {
+  if (!live(s)) return VG_ESTATE;
+  if (!res || (top_k && !top)) return VG_EINVAL;
+  const uint32_t H = s->m->cfg.embedding_length, V = s->m->cfg.vocab_size;
+  std::vector<float> h(H);
+  int rc = vg_copy_output(s, h.data(), H);
+  if (rc) return rc;
+  double sum = 0, sq = 0;
+  for (float x : h) {
+    sum += (double)x;
+    sq += (double)x * (double)x;
+  }
+  res->position = s->pos ? s->pos - 1 : 0;
+  res->final_hidden_checksum = sum;
+  res->final_hidden_l2 = std::sqrt(sq);
+  res->n_top = 0;
+  if (top_k) {
+    if (!s->logits_valid) {
+      set_err(s->m->ctx, "the last step did not compute logits");
+      return VG_ESTATE;
+    }
+    std::vector<float> lg(V);
+    rc = vg_copy_logits(s, lg.data(), V);
+    if (rc) return rc;
+    rc = vg_top_k_logits(lg.data(), V, top_k, top, &res->n_top);
+    if (rc) return rc;
+  }
+  return VG_OK;
+}
+
+int vg_benchmark(vg_stream *s, uint32_t token, uint32_t warmup, uint32_t iterations, int want_logits,
+                 vg_benchmark_result *res) {
+  if (!live(s)) return VG_ESTATE;
+  if (!res) return VG_EINVAL;
+  return guard(s->m->ctx, [&] {
+    if (iterations == 0) fail(VG_EINVAL, "benchmark iterations must be > 0");
+    const uint64_t needed = (uint64_t)warmup + iterations;
+    if (needed > s->max_ctx)
+      fail(VG_EFULL, strf("benchmark needs %llu context positions but --max-context is %u",
+                          (unsigned long long)needed, s->max_ctx));
+    int rc = vg_stream_reset(s);
+    if (rc) return rc;
+    for (uint32_t i = 0; i < warmup; ++i)
+      if ((rc = vg_decode_token(s, token, want_logits))) return rc;
+    std::vector<cudaEvent_t> ev(iterations + 1);
+    for (auto &e : ev) CK(cudaEventCreate(&e));
+    CK(cudaEventRecord(ev[0], s->st));
+    for (uint32_t i = 0; i < iterations; ++i) {
+      if ((rc = vg_decode_token(s, token, want_logits))) break;
+      CK(cudaEventRecord(ev[i + 1], s->st));
+    }
+    if (!rc) rc = sync_stream(s, 120ull * 1000000000ull, true);
+    double sum = 0, mn = 1e30, mx = 0;
+    if (!rc)
+      for (uint32_t i = 0; i < iterations; ++i) {
+        float ms = 0;
+        CK(cudaEventElapsedTime(&ms, ev[i], ev[i + 1]));
+        sum += ms;
+        mn = std::min<double>(mn, ms);
+        mx = std::max<double>(mx, ms);
+      }
+    for (auto &e : ev) cudaEventDestroy(e);
+    if (rc) return rc;
+    res->iterations = iterations;
+    res->token_id = token;
+    res->mean_ms = sum / iterations;
+    res->min_ms = mn;
+    res->max_ms = mx;
+    res->tokens_per_second = 1000.0 / res->mean_ms;
+    return VG_OK;
+  });
+}
+
+int vg_stream_profile_step(vg_stream *s, uint32_t token, int want_logits, vg_kernel_time *out, uint32_t capacity,
+                           uint32_t *n_out) {
+  if (!live(s)) return VG_ESTATE;
+  if (!n_out || (!out && capacity)) return VG_EINVAL;
+  return guard(s->m->ctx, [&] {
+    if (token >= s->m->cfg.vocab_size)
+      fail(VG_ERANGE, strf("token id %u is outside vocabulary 0..%u", token, s->m->cfg.vocab_size));
+    check_step(s);
+    CK(cudaSetDevice(s->m->ctx->device));
+    std::vector<Launch> prog;
+    build_program(s, true, want_logits != 0, prog);
+    uint8_t *slot = staging_slot(s);
+    std::memcpy(slot, &token, 4);
+    CK(cudaMemcpyAsync(s->ctrl + kCtrlToken, slot, 4, cudaMemcpyHostToDevice, s->st));
+    CK(cudaEventRecord(staging_event(s), s->st));
+    std::vector<cudaEvent_t> ev(prog.size() + 1);
+    for (auto &e : ev) CK(cudaEventCreate(&e));
+    cudaError_t err = cudaEventRecord(ev[0], s->st);
+    for (size_t i = 0; i < prog.size() && err == cudaSuccess; ++i) {
+      err = prog[i].fn(s->st, false);
+      if (err == cudaSuccess) err = cudaEventRecord(ev[i + 1], s->st);
+    }
+    const uint32_t pos = s->pos;
+    s->pos += 1;
+    s->logits_valid = want_logits != 0;
+    int rc = err == cudaSuccess ? sync_stream(s, 60ull * 1000000000ull, true) : VG_ECUDA;
+    uint32_t n = 0;
+    if (rc == VG_OK) {
+      for (size_t i = 0; i < prog.size() && n < capacity; ++i, ++n) {
+        float ms = 0;
+        CK(cudaEventElapsedTime(&ms, ev[i], ev[i + 1]));
+        vg_kernel_time &k = out[n];
+        std::memset(&k, 0, sizeof k);
+        snprintf(k.name, sizeof k.name, "%s", prog[i].name);
+        k.layer = prog[i].layer;
+        k.ms = ms;
+        k.bytes = prog[i].per_position ? prog[i].bytes * (uint64_t)(pos + 1) : prog[i].bytes;
+      }
+    }
+    for (auto &e : ev) cudaEventDestroy(e);
+    if (err != cudaSuccess) fail(VG_ECUDA, strf("kernel launch failed: %s", cudaGetErrorString(err)));
+    *n_out = n;
+    return rc;
+  });
+}
+
+int vg_decode_batch(vg_stream *const *streams, int n, const uint32_t *tokens) {
+  if (!streams || !tokens || n <= 0 || n > 16) return VG_EINVAL;
+  for (int i = 0; i < n; ++i)
+    if (!live(streams[i])) return VG_ESTATE;
+  set_err(streams[0]->m->ctx, "vg_decode_batch is not implemented yet");
+  return VG_EUNSUPPORTED;
+}
+
+// ---- kernel-level entry points --------------------------------------------
+static std::mutex g_kctrl_mu;
+static std::map<int, uint32_t *> g_kctrl;  // per-device control words for kernel-level calls
+
+static uint32_t *kernel_ctrl() {
+  int dev = 0;
+  CK(cudaGetDevice(&dev));
+  std::lock_guard<std::mutex> l(g_kctrl_mu);
+  uint32_t *&p = g_kctrl[dev];
+  if (!p) {
+    CK(cudaMalloc(&p, kCtrlWords * 4));
+    CK(cudaMemset(p, 0, kCtrlWords * 4));
+  }
+  return p;
+}
+
+static int kguard(const std::function<void()> &f) {
+  try {
+    f();
+    return VG_OK;
+  } catch (const Error &e) {
+    return e.code;
+  }
+}
+
+int vg_k_packed_bytes(int dtype, uint32_t rows, uint32_t cols, uint64_t *bytes) {
+  if (!bytes || rows == 0 || cols == 0) return VG_EINVAL;
+  if (dtype == VG_FORMAT_Q8_0 && cols % 32 == 0) *bytes = (uint64_t)rows * q8_row_bytes(cols);
+  else if (dtype == VG_FORMAT_F16 && cols % 8 == 0) *bytes = (uint64_t)rows * f16_row_bytes(cols);
+  else return VG_EUNSUPPORTED;
+  return VG_OK;
+}
+
+int vg_k_repack(int dtype, const void *gguf_bytes, uint32_t rows, uint32_t cols, void *packed, void *cuda_stream) {
+  uint64_t b;
+  int rc = vg_k_packed_bytes(dtype, rows, cols, &b);
+  if (rc) return rc;
+  if (!gguf_bytes || !packed) return VG_EINVAL;
+  return kguard([&] {
+    const uint32_t rb = dtype == VG_FORMAT_Q8_0 ? q8_row_bytes(cols) : f16_row_bytes(cols);
+    repack_kernel<<<std::min<uint32_t>(rows, 65535u), 256, 0, (cudaStream_t)cuda_stream>>>(
+        (const uint8_t *)gguf_bytes, dtype == VG_FORMAT_Q8_0, rows, cols, (uint8_t *)packed, rb, 1, 0, 0);
+    CK(cudaGetLastError());
+  });
+}
+
+int vg_k_matvec(int dtype, const void *packed, uint32_t rows, uint32_t cols, const float *x, float *y, float alpha,
+                void *cuda_stream) {
+  uint64_t b;
+  int rc = vg_k_packed_bytes(dtype, rows, cols, &b);
+  if (rc) return rc;
+  if (!packed || !x || !y) return VG_EINVAL;
+  return kguard([&] {
+    int dev = 0, sms = 0;
+    CK(cudaGetDevice(&dev));
+    CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    DevMat m{(uint8_t *)packed, rows, cols, (uint32_t)(b / rows), (uint32_t)dtype};
+    MvPlan pl = plan_matvec<Mode::PLAIN, Pro::COPY>(m, dev, (uint32_t)sms);
+    pl.p.xsrc = x;
+    pl.p.out = y;
+    pl.p.alpha = alpha;
+    pl.p.ctrl = kernel_ctrl();
+    CK(run_matvec(pl, (cudaStream_t)cuda_stream, false));
+  });
+}
+
+int vg_k_embedding(int dtype, const void *packed, uint32_t rows, uint32_t cols, uint32_t row, float alpha,
+                   float *out, void *cuda_stream) {
+  uint64_t b;
+  int rc = vg_k_packed_bytes(dtype, rows, cols, &b);
+  if (rc) return rc;
+  if (!packed || !out) return VG_EINVAL;
+  if (row >= rows) return VG_ERANGE;
+  return kguard([&] {
+    embedding_kernel<<<(cols + 255) / 256, 256, 0, (cudaStream_t)cuda_stream>>>(
+        (const uint8_t *)packed, dtype == VG_FORMAT_Q8_0, rows, cols, (uint32_t)(b / rows), nullptr, row, alpha, out,
+        kernel_ctrl() + kCtrlErr);
+    CK(cudaGetLastError());
+  });
+}
+
+int vg_k_residual_rmsnorm(float *hidden, const float *branch, const float *w, uint32_t n, float eps, float scale,
+                          float *y, void *cuda_stream) {
+  if (!hidden || !w || !y || n == 0) return VG_EINVAL;
+  return kguard([&] {
+    residual_rmsnorm_kernel<<<1, std::min<uint32_t>(1024u, round_up(n, 32)), 0, (cudaStream_t)cuda_stream>>>(
+        hidden, branch, w, n, eps, scale, y, nullptr, 0);
+    CK(cudaGetLastError());
+  });
+}
+
+int vg_k_attention(const float *q, const uint16_t *k_cache, const uint16_t *v_cache, uint32_t heads,
+                   uint32_t kv_heads, uint32_t head_dim, uint32_t ctx, uint32_t position, float *out,
+                   void *cuda_stream) {
+  if (!q || !k_cache || !v_cache || !out || !heads || !kv_heads || heads % kv_heads || position >= ctx)
+    return VG_EINVAL;
+  if (head_dim != 32 && head_dim != 64 && head_dim != 128 && head_dim != 256) return VG_EUNSUPPORTED;
+  return kguard([&] {
+    cudaStream_t st = (cudaStream_t)cuda_stream;
+    int dev = 0;
+    CK(cudaGetDevice(&dev));
+    const uint32_t G = heads / kv_heads;
+    AttnParams ap{};
+    ap.nsplit = std::max<uint32_t>(16u, (ctx + 2047u) / 2048u);
+    ap.chunk_cap = (ctx + ap.nsplit - 1) / ap.nsplit;
+    const size_t part_bytes = (size_t)kv_heads * ap.nsplit * G * (head_dim + 2) * 4;
+    void *scratch = nullptr;
+    CK(cudaMallocAsync(&scratch, part_bytes + 256 + kv_heads * 4, st));
+    uint32_t *tickets = (uint32_t *)((uint8_t *)scratch + round_up_sz(part_bytes, 256));
+    CK(cudaMemsetAsync(tickets, 0, kv_heads * 4, st));
+    ap.q = q;
+    ap.kc = (const __half *)k_cache;
+    ap.vc = (const __half *)v_cache;
+    ap.out = out;
+    ap.part = (float *)scratch;
+    ap.tickets = tickets;
+    ap.heads = heads;
+    ap.kv_heads = kv_heads;
+    ap.ctx = ctx;
+    ap.scale = 1.0f / sqrtf((float)head_dim);
+    ap.fixed_pos = position;
+    ap.ctrl = nullptr;
+    const AttnFn fn = pick_attention(head_dim);
+    const uint32_t smem = attention_smem_bytes(G, head_dim, ap.chunk_cap, ap.nsplit);
+    ensure_smem((const void *)fn, dev, smem);
+    cudaError_t e = launch_ex(fn, dim3(ap.nsplit, kv_heads), dim3(256), smem, st, false, ap);
+    cudaError_t e2 = cudaFreeAsync(scratch, st);
+    CK(e);
+    CK(e2);
+  });
+}
+
+}  // extern "C"

@@ -1,0 +1,231 @@
+"""Seeded synthetic BaseLM models and inputs for the BASELINE configurations.
+
+The VoxCPM2 BaseLM GGUF files are not available, so every model is generated here with the
+value distributions the configurations state:
+
+* Q8_0 matrices: int8 quants uniform in [-127, 127], one fp16 scale per 32-element block
+  drawn as ``fp16(|N(0, 0.02)| / 127)``;
+* F16 matrices and the token-embedding table: ``N(0, 0.02)``;
+* norm weights: ``1 + N(0, 0.01)`` in fp32 (attn_norm, ffn_norm, output_norm);
+* RoPE: theta 1e4, ``rope.scaling.type = longrope`` with all-ones short/long factors and
+  ``context_length == original_context_length``, so ``ext = 1`` and the scaling factor is 1
+  (``rope_scaling_factor``, src/baselm.rs:194-205);
+* fp16 KV-cache contents and input hidden states: ``N(0, 1)``.
+
+Every tensor draws from its own generator, ``np.random.default_rng([seed, index])``, so a
+model is reproducible byte for byte and tensors can be generated lazily while writing.
+"""
+from __future__ import annotations
+
+import hashlib
+import os
+from dataclasses import dataclass, replace
+from pathlib import Path
+from typing import Callable, Dict, List, Optional, Tuple
+
+import numpy as np
+
+from .gguf import (GGML_F16, GGML_F32, GGML_Q8_0, F32, U32, GgufFile, q8_0_pack,
+                   storage_bytes, write_gguf)
+
+
+@dataclass(frozen=True)
+class ModelSpec:
+    name: str
+    layers: int
+    hidden: int
+    heads: int
+    kv_heads: int
+    head_dim: int
+    ffn: int
+    vocab: int
+    fmt: int                   # GGML_Q8_0 or GGML_F16 for the projection matrices
+    embd_fmt: int = GGML_F16   # token_embd.weight type
+    seed: int = 0
+    context_length: int = 32768
+    eps: float = 1e-5
+    theta: float = 10000.0
+    embedding_scale: float = 0.0
+    residual_scale: float = 0.0
+    logit_scale: float = 0.0
+    tied_output: bool = True
+    rope_scaling: str = "longrope"
+    alignment: int = 32
+
+    @property
+    def kv_dim(self) -> int:
+        return self.kv_heads * self.head_dim
+
+
+# BASELINE.json configs (seeds 0-4). cfg0 has no embedding input in the spec; it still
+# carries a small token table because the loader requires token_embd.weight.
+PRESETS: Dict[str, ModelSpec] = {
+    "cfg0": ModelSpec("cfg0", 1, 1024, 16, 2, 64, 4096, 4096, GGML_Q8_0, seed=0),
+    "cfg1": ModelSpec("cfg1", 24, 1024, 16, 2, 64, 4096, 73448, GGML_Q8_0, seed=1),
+    "cfg2": ModelSpec("cfg2", 28, 2048, 16, 2, 128, 6144, 73448, GGML_Q8_0, seed=2),
+    "cfg3": ModelSpec("cfg3", 28, 2048, 16, 2, 128, 6144, 73448, GGML_F16, seed=3),
+    "cfg4": ModelSpec("cfg4", 28, 2048, 16, 2, 128, 6144, 73448, GGML_Q8_0, seed=4),
+    # small shapes for parity tests (odd row counts, several layers, GQA ratio 4)
+    "tiny": ModelSpec("tiny", 2, 256, 8, 2, 32, 608, 512, GGML_Q8_0, seed=11),
+    "tiny_f16": ModelSpec("tiny_f16", 2, 256, 8, 2, 32, 608, 512, GGML_F16, seed=12),
+}
+
+# Runtime inputs per config (BASELINE.json configs and the survey's measurement plan).
+CFG_RUNS = {
+    "cfg0": dict(prefill_positions=512, steps=1),
+    "cfg1": dict(prefill_tokens=128, steps=256),
+    "cfg2": dict(prefill_positions=1023, steps=3073, max_context=4096),
+    "cfg3": dict(prefill_positions=1023, steps=3073, max_context=4096),
+    "cfg4": dict(streams=16, kv_lo=64, kv_hi=4096, steps=256, max_context=4096 + 256),
+}
+
+
+def _rng(seed: int, index: int) -> np.random.Generator:
+    return np.random.default_rng([seed, index])
+
+
+def q8_matrix(rng: np.random.Generator, rows: int, cols: int) -> np.ndarray:
+    """Q8_0 bytes of a rows x cols matrix with the configs' distributions."""
+    qs = rng.integers(-127, 128, size=(rows, cols), dtype=np.int8)
+    d = (np.abs(rng.standard_normal((rows, cols // 32), dtype=np.float32)) * 0.02 / 127.0)
+    return q8_0_pack(d.astype(np.float16), qs)
+
+
+def f16_matrix(rng: np.random.Generator, rows: int, cols: int) -> np.ndarray:
+    return (rng.standard_normal((rows, cols), dtype=np.float32) * 0.02).astype(np.float16)
+
+
+def norm_vector(rng: np.random.Generator, n: int) -> np.ndarray:
+    return (1.0 + 0.01 * rng.standard_normal(n, dtype=np.float32)).astype(np.float32)
+
+
+def _matrix(spec: ModelSpec, fmt: int, rows: int, cols: int, index: int) -> Callable[[], np.ndarray]:
+    def gen() -> np.ndarray:
+        r = _rng(spec.seed, index)
+        return q8_matrix(r, rows, cols) if fmt == GGML_Q8_0 else f16_matrix(r, rows, cols)
+    return gen
+
+
+def build_gguf(spec: ModelSpec) -> Tuple[GgufFile, List[Tuple[str, Tuple[int, ...], int, Callable]]]:
+    H, F, KV = spec.hidden, spec.ffn, spec.kv_dim
+    meta = {
+        "general.architecture": "minicpm4",
+        "general.name": f"voxgen-b200-synthetic-{spec.name}",
+        "minicpm4.context_length": U32(spec.context_length),
+        "minicpm4.embedding_length": U32(H),
+        "minicpm4.block_count": U32(spec.layers),
+        "minicpm4.feed_forward_length": U32(F),
+        "minicpm4.attention.head_count": U32(spec.heads),
+        "minicpm4.attention.head_count_kv": U32(spec.kv_heads),
+        "minicpm4.attention.key_length": U32(spec.head_dim),
+        "minicpm4.rope.dimension_count": U32(spec.head_dim),
+        "minicpm4.attention.layer_norm_rms_epsilon": F32(spec.eps),
+        "minicpm4.rope.freq_base": F32(spec.theta),
+        "minicpm4.rope.scaling.type": spec.rope_scaling,
+        "minicpm4.rope.scaling.original_context_length": U32(spec.context_length),
+    }
+    if spec.embedding_scale:
+        meta["minicpm4.embedding_scale"] = F32(spec.embedding_scale)
+    if spec.residual_scale:
+        meta["minicpm4.residual_scale"] = F32(spec.residual_scale)
+    if spec.logit_scale:
+        meta["minicpm4.logit_scale"] = F32(spec.logit_scale)
+    g = GgufFile(metadata=meta, alignment=spec.alignment)
+    plan: List[Tuple[str, Tuple[int, ...], int, Callable]] = []
+    idx = 0
+
+    def add(name, dims, ty, gen):
+        nonlocal idx
+        plan.append((name, tuple(dims), ty, gen))
+        idx += 1
+
+    def vec(n, index, ones=False):
+        return lambda: (np.ones(n, np.float32) if ones else norm_vector(_rng(spec.seed, index), n))
+
+    add("token_embd.weight", (H, spec.vocab), spec.embd_fmt,
+        _matrix(spec, spec.embd_fmt, spec.vocab, H, 0))
+    if not spec.tied_output:
+        add("output.weight", (H, spec.vocab), spec.embd_fmt,
+            _matrix(spec, spec.embd_fmt, spec.vocab, H, 1))
+    add("output_norm.weight", (H,), GGML_F32, vec(H, 2))
+    if spec.rope_scaling == "longrope":
+        add("rope_factors_short.weight", (spec.head_dim // 2,), GGML_F32,
+            vec(spec.head_dim // 2, 3, ones=True))
+        add("rope_factors_long.weight", (spec.head_dim // 2,), GGML_F32,
+            vec(spec.head_dim // 2, 4, ones=True))
+    for layer in range(spec.layers):
+        base = 16 + 16 * layer
+        p = f"blk.{layer}."
+        add(p + "attn_norm.weight", (H,), GGML_F32, vec(H, base + 0))
+        add(p + "attn_q.weight", (H, H), spec.fmt, _matrix(spec, spec.fmt, H, H, base + 1))
+        add(p + "attn_k.weight", (H, KV), spec.fmt, _matrix(spec, spec.fmt, KV, H, base + 2))
+        add(p + "attn_v.weight", (H, KV), spec.fmt, _matrix(spec, spec.fmt, KV, H, base + 3))
+        add(p + "attn_output.weight", (H, H), spec.fmt, _matrix(spec, spec.fmt, H, H, base + 4))
+        add(p + "ffn_norm.weight", (H,), GGML_F32, vec(H, base + 5))
+        add(p + "ffn_gate.weight", (H, F), spec.fmt, _matrix(spec, spec.fmt, F, H, base + 6))
+        add(p + "ffn_up.weight", (H, F), spec.fmt, _matrix(spec, spec.fmt, F, H, base + 7))
+        add(p + "ffn_down.weight", (F, H), spec.fmt, _matrix(spec, spec.fmt, H, F, base + 8))
+    return g, plan
+
+
+class _Deferred:
+    """Stands in for an ndarray inside GgufFile until the writer asks for it."""
+
+    def __init__(self, nbytes: int, gen: Callable[[], np.ndarray]):
+        self.size = nbytes
+        self.gen = gen
+
+    def tofile(self, f) -> None:
+        a = self.gen()
+        np.ascontiguousarray(a).view(np.uint8).reshape(-1).tofile(f)
+
+
+def write_model(spec: ModelSpec, path: Path) -> Path:
+    from .gguf import Tensor
+    g, plan = build_gguf(spec)
+    for name, dims, ty, gen in plan:
+        g.tensors.append(Tensor(name, dims, ty, _Deferred(storage_bytes(ty, int(np.prod(dims))), gen)))
+    tmp = Path(str(path) + f".tmp{os.getpid()}")
+    write_gguf(tmp, g)
+    tmp.replace(path)
+    return path
+
+
+def spec_digest(spec: ModelSpec) -> str:
+    return hashlib.sha1(repr(spec).encode()).hexdigest()[:12]
+
+
+def model_path(spec: ModelSpec, cache_dir: Optional[Path] = None) -> Path:
+    """Generates (once) and returns the GGUF path of ``spec`` under ``cache_dir``
+    (default: ``$VOXGEN_MODEL_CACHE`` or ``/tmp/voxgen_b200_models``)."""
+    d = Path(cache_dir or os.environ.get("VOXGEN_MODEL_CACHE", "/tmp/voxgen_b200_models"))
+    d.mkdir(parents=True, exist_ok=True)
+    p = d / f"{spec.name}-{spec_digest(spec)}.gguf"
+    if not p.exists():
+        write_model(spec, p)
+    return p
+
+
+def preset(name: str, **overrides) -> ModelSpec:
+    spec = PRESETS[name]
+    return replace(spec, **overrides) if overrides else spec
+
+
+def kv_prefill(spec: ModelSpec, n_positions: int, seed_index: int = 1000) -> Tuple[np.ndarray, np.ndarray]:
+    """fp16 K and V ~N(0,1) in the reference cache layout [layer][pos][kv_dim]
+    (store_kv.comp:21 with context = n_positions), returned as uint16 bit patterns."""
+    r = _rng(spec.seed, seed_index)
+    shape = (spec.layers, n_positions, spec.kv_dim)
+    k = r.standard_normal(shape, dtype=np.float32).astype(np.float16).view(np.uint16)
+    v = r.standard_normal(shape, dtype=np.float32).astype(np.float16).view(np.uint16)
+    return k, v
+
+
+def hidden_inputs(spec: ModelSpec, n: int, seed_index: int = 2000) -> np.ndarray:
+    """fp32 ~N(0,1) input hidden states, shape [n, H]."""
+    return _rng(spec.seed, seed_index).standard_normal((n, spec.hidden), dtype=np.float32)
+
+
+def token_ids(spec: ModelSpec, n: int, seed_index: int = 3000) -> np.ndarray:
+    """Uniform random token ids in [0, vocab)."""
+    return _rng(spec.seed, seed_index).integers(0, spec.vocab, size=n, dtype=np.uint32)
