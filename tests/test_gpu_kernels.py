@@ -54,22 +54,43 @@ def test_matvec(dtype, rows, cols):
     assert_close(y.cpu().numpy(), want, what=f"matvec {dtype} {rows}x{cols}")
 
 
-@pytest.mark.parametrize("dtype", [Q8, F16])
-def test_repack_layout(dtype):
-    rows, cols = 6, 64
+def tile_offsets(rows, cols, q8):
+    """Byte offsets of the segmented 8-row tile layout (mirror of TileGeom in kernels.cuh)."""
+    step = 32 if q8 else 16
+    seg_cols = 16 * step
+    nseg = -(-cols // seg_cols)
+    seg_bytes = 4096 + (256 if q8 else 0)
+    r = np.arange(rows)[:, None]
+    k = np.arange(cols)[None, :]
+    seg, kk = k // seg_cols, k % seg_cols
+    kb = (kk % step) * (1 if q8 else 2)
+    base = ((r // 8) * nseg + seg) * seg_bytes
+    elem = base + (kk // step) * 256 + (kb >> 4) * 128 + (r % 8) * 16 + (kb & 15)
+    b = np.arange(cols // 32)[None, :]
+    scale = ((r // 8) * nseg + b // 16) * seg_bytes + 4096 + ((b % 16) * 8 + r % 8) * 2
+    return elem, scale, (-(-rows // 8)) * nseg * seg_bytes
+
+
+@pytest.mark.parametrize("dtype,rows,cols", [(Q8, 6, 64), (Q8, 17, 544), (F16, 9, 272)])
+def test_repack_layout(dtype, rows, cols):
     rng = np.random.default_rng(1)
     raw = make_matrix(rng, dtype, rows, cols)
     packed = packed_matrix(dtype, raw, rows, cols).cpu().numpy()
+    elem, scale, total = tile_offsets(rows, cols, dtype == Q8)
+    assert packed.size == total
+    used = np.zeros(total, bool)
     if dtype == Q8:
-        rb = (cols + cols // 16 + 15) // 16 * 16
         d, qs = gguf.q8_0_unpack(raw, rows, cols)
-        for r in range(rows):
-            rec = packed[r * rb:(r + 1) * rb]
-            assert np.array_equal(rec[:cols].view(np.int8), qs[r])
-            assert np.array_equal(rec[cols:cols + cols // 16].view(np.float16), d[r])
-            assert not rec[cols + cols // 16:].any()
+        assert np.array_equal(packed[elem].view(np.int8), qs)
+        lo, hi = packed[scale], packed[scale + 1]
+        assert np.array_equal((lo.astype(np.uint16) | (hi.astype(np.uint16) << 8)).view(np.float16), d)
+        used[elem] = True
+        used[scale] = used[scale + 1] = True
     else:
-        assert np.array_equal(packed.view(np.float16).reshape(rows, cols), raw.view(np.float16).reshape(rows, cols))
+        h = raw.view(np.uint8).reshape(rows, cols * 2)
+        assert np.array_equal(packed[elem], h[:, 0::2]) and np.array_equal(packed[elem + 1], h[:, 1::2])
+        used[elem] = used[elem + 1] = True
+    assert not packed[~used].any(), "padding bytes must be zero"
 
 
 @pytest.mark.parametrize("dtype,cols", [(Q8, 1024), (Q8, 2048), (F16, 1024), (F16, 2048)])

@@ -19,6 +19,12 @@ def ctx():
     c.close()
 
 
+def _ordinal(bits):
+    """fp16 bit patterns mapped to integers that are monotonic in the value."""
+    b = bits.astype(np.int32)
+    return np.where(b & 0x8000, -(b & 0x7FFF), b)
+
+
 class Pair:
     """The same session on the CUDA engine and on the oracle."""
 
@@ -51,9 +57,13 @@ class Pair:
             fa = a.view(np.float16).astype(np.float32)
             fb = b.view(np.float16).astype(np.float32)
             assert_close(fa, fb, what=f"{what} {name} cache")
-            # fp16 stores: at most one unit in the last place apart
-            diff = np.abs(a.astype(np.int32) - b.astype(np.int32))
-            assert diff.max() <= 1, f"{what} {name}: fp16 bits differ by {diff.max()}"
+            # Layer 0 projects bit-identical inputs (the embedding lookup is exact), so its
+            # fp16 stores of ordinary-magnitude values are at most one unit in the last place
+            # apart; deeper layers carry accumulated fp32 differences and are held to the
+            # value tolerance above.
+            big = np.abs(fb[0]) >= 1e-2
+            diff = np.abs(_ordinal(a[0]) - _ordinal(b[0]))[big]
+            assert diff.max(initial=0) <= 1, f"{what} {name} layer 0: fp16 values {diff.max()} ulp apart"
 
     def close(self):
         self.eng.close()

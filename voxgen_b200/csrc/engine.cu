@@ -44,8 +44,16 @@ namespace {
 
 struct DevMat {
   uint8_t *w = nullptr;
-  uint32_t rows = 0, cols = 0, row_bytes = 0, type = GGML_Q8_0;
+  TileGeom g{0, 0, 1};
+  uint32_t type = GGML_Q8_0;
 };
+
+DevMat make_mat(uint32_t rows, uint32_t cols, uint32_t type) {
+  DevMat d;
+  d.g = TileGeom{rows, cols, type == GGML_Q8_0 ? 1u : 0u};
+  d.type = type;
+  return d;
+}
 
 struct Layer {
   DevMat qkv, o, gateup, down;
@@ -103,8 +111,8 @@ std::string strf(const char *f, ...) {
 uint32_t round_up(uint32_t x, uint32_t a) { return (x + a - 1) / a * a; }
 size_t round_up_sz(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
-uint32_t row_bytes_of(uint32_t type, uint32_t cols) {
-  return type == GGML_Q8_0 ? q8_row_bytes(cols) : f16_row_bytes(cols);
+uint64_t packed_bytes(uint32_t type, uint32_t rows, uint32_t cols) {
+  return TileGeom{rows, cols, type == GGML_Q8_0 ? 1u : 0u}.bytes();
 }
 
 // Bounded host wait on an event: spin briefly, then poll with short sleeps.
@@ -122,17 +130,29 @@ int host_wait(cudaEvent_t ev, uint64_t timeout_ns) {
 }
 
 template <class K, class... Args>
-cudaError_t launch_ex(K kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl, Args... args) {
+cudaError_t launch_ex(K kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl, uint32_t cluster_x,
+                      Args... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = pdl ? attr : nullptr;
-  cfg.numAttrs = pdl ? 1 : 0;
+  cudaLaunchAttribute attr[2];
+  unsigned n = 0;
+  if (pdl) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (cluster_x > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cluster_x;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = n ? attr : nullptr;
+  cfg.numAttrs = n;
   return cudaLaunchKernelEx(&cfg, kernel, args...);
 }
 
@@ -140,12 +160,8 @@ cudaError_t launch_ex(K kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t
 using MvFn = void (*)(MvParams);
 
 template <Mode M, Pro P>
-MvFn pick_matvec(uint32_t type, uint32_t cols, uint32_t &rw) {
-  const bool big = cols > 4096;
-  rw = big ? 2 : 4;
-  if (type == GGML_Q8_0)
-    return big ? matvec_kernel<WFmt::Q8, M, P, 2> : matvec_kernel<WFmt::Q8, M, P, 4>;
-  return big ? matvec_kernel<WFmt::F16, M, P, 2> : matvec_kernel<WFmt::F16, M, P, 4>;
+MvFn matvec_fn(bool q8) {
+  return q8 ? matvec_kernel<true, M, P> : matvec_kernel<false, M, P>;
 }
 
 std::mutex g_attr_mu;
@@ -167,38 +183,55 @@ struct MvPlan {
   MvParams p{};
 };
 
+uint32_t next_pow2(uint32_t x) {
+  uint32_t p = 1;
+  while (p < x) p <<= 1;
+  return p;
+}
+
 template <Mode M, Pro P>
 MvPlan plan_matvec(const DevMat &m, int device, uint32_t sms) {
   MvPlan pl;
-  uint32_t rw = 4;
-  pl.fn = pick_matvec<M, P>(m.type, m.cols, rw);
-  const bool q8 = m.type == GGML_Q8_0;
-  const uint32_t xpad = q8 ? Fmt<WFmt::Q8>::xpad(m.cols) : Fmt<WFmt::F16>::xpad(m.cols);
-  const uint32_t x_bytes = round_up(xpad * 4u, 128u);
-  const uint32_t units = (m.rows + rw - 1) / rw;
-  const uint32_t grid = std::min<uint32_t>(sms, units);
-  const uint32_t per_cta = (units + grid - 1) / grid;
-  const uint32_t slot = rw * m.row_bytes;
-  uint32_t budget = kSmemBudget > x_bytes + 1024 ? kSmemBudget - x_bytes - 1024 : 0;
-  uint32_t slots = std::max<uint32_t>(1u, std::min<uint32_t>(budget / slot, per_cta));
-  uint32_t smem = matvec_smem_bytes(x_bytes, slots, slot);
-  while (smem > kSmemMax && slots > 1) smem = matvec_smem_bytes(x_bytes, --slots, slot);
-  if (smem > kSmemMax) fail(VG_EUNSUPPORTED, strf("matrix rows of %u columns do not fit in shared memory", m.cols));
+  const TileGeom g = m.g;
+  const uint32_t T = g.tiles();
+  const uint32_t grid = std::min<uint32_t>(sms, T);
+  const uint32_t per_cta = (T + grid - 1) / grid;
+  const uint32_t cols_pad = g.nseg() * g.seg_cols();
+  MvParams &p = pl.p;
+  p.w = m.w;
+  p.g = g;
+  p.a_bytes = mv_a_bytes(g.q8, cols_pad);
+  p.plane = mv_a_plane(g.q8, cols_pad);
+  // Tile reduction buffers: one per tile of the CTA when that is at most 64,
+  // else 64 (a warp cannot run more than a few tiles ahead of the others).
+  p.rb = next_pow2(std::max<uint32_t>(1u, std::min<uint32_t>(per_cta, 64u)));
+  // Ring slots per consumer warp: as many as the budget holds, at most 4 and
+  // at most the warp's share of items.
+  const uint32_t items_per_warp = (per_cta * g.nseg() + kMvConsumers - 1) / kMvConsumers;
+  p.spw = 1;
+  MvSmem probe(p);
+  const uint32_t per_slot = kMvConsumers * (g.seg_bytes() + 16u);
+  const uint32_t fixed = probe.total - per_slot;
+  const uint32_t fit = kSmemBudget > fixed ? (kSmemBudget - fixed) / per_slot : 1u;
+  p.spw = std::max<uint32_t>(1u, std::min<uint32_t>({fit, 4u, std::max<uint32_t>(1u, items_per_warp)}));
+  const uint32_t smem = MvSmem(p).total;
+  if (smem > kSmemMax) fail(VG_EUNSUPPORTED, strf("matrix of %u columns does not fit in shared memory", g.cols));
+  pl.fn = matvec_fn<M, P>(g.q8 != 0);
   pl.grid = dim3(grid);
   pl.smem = smem;
-  pl.p.w = m.w;
-  pl.p.rows = m.rows;
-  pl.p.cols = m.cols;
-  pl.p.row_bytes = m.row_bytes;
-  pl.p.units = units;
-  pl.p.slots = slots;
-  pl.p.x_bytes = x_bytes;
   ensure_smem((const void *)pl.fn, device, smem);
   return pl;
 }
 
 cudaError_t run_matvec(const MvPlan &pl, cudaStream_t st, bool pdl) {
-  return launch_ex(pl.fn, pl.grid, dim3(kMatvecThreads), pl.smem, st, pdl, pl.p);
+  return launch_ex(pl.fn, pl.grid, dim3(kMvThreads), pl.smem, st, pdl, 1u, pl.p);
+}
+
+// Attention split count: chunks of at most 64 positions, a multiple of the cluster size.
+void plan_attention(uint32_t ctx, uint32_t &nsplit, uint32_t &chunk_cap) {
+  nsplit = std::max<uint32_t>(1u, (ctx + 63u) / 64u);
+  nsplit = (nsplit + kAttnCluster - 1) / kAttnCluster * kAttnCluster;
+  chunk_cap = (ctx + nsplit - 1) / nsplit;
 }
 
 using AttnFn = void (*)(AttnParams);
@@ -333,21 +366,21 @@ void load_model(vg_model *m, const std::string &path, uint32_t requested) {
     auto nm = [&](const char *s) { return strf("blk.%u.%s.weight", l, s); };
     const uint32_t tq = tensor(nm("attn_q")).type, to = tensor(nm("attn_output")).type;
     const uint32_t tg = tensor(nm("ffn_gate")).type, td = tensor(nm("ffn_down")).type;
-    L.qkv = {nullptr, H + 2 * KV, H, row_bytes_of(tq, H), tq};
-    L.o = {nullptr, H, H, row_bytes_of(to, H), to};
-    L.gateup = {nullptr, 2 * F, H, row_bytes_of(tg, H), tg};
-    L.down = {nullptr, H, F, row_bytes_of(td, F), td};
-    for (DevMat *d : {&L.qkv, &L.o, &L.gateup, &L.down}) mats.push_back({d, take((size_t)d->rows * d->row_bytes)});
+    L.qkv = make_mat(H + 2 * KV, H, tq);
+    L.o = make_mat(H, H, to);
+    L.gateup = make_mat(2 * F, H, tg);
+    L.down = make_mat(H, F, td);
+    for (DevMat *d : {&L.qkv, &L.o, &L.gateup, &L.down}) mats.push_back({d, take(d->g.bytes())});
     vecs.push_back({&L.attn_norm, take((size_t)H * 4)});
     vecs.push_back({&L.ffn_norm, take((size_t)H * 4)});
   }
   const TensorInfo &tok = tensor("token_embd.weight");
-  m->tok = {nullptr, c.vocab_size, H, row_bytes_of(tok.type, H), tok.type};
-  mats.push_back({&m->tok, take((size_t)m->tok.rows * m->tok.row_bytes)});
+  m->tok = make_mat(c.vocab_size, H, tok.type);
+  mats.push_back({&m->tok, take(m->tok.g.bytes())});
   if (!c.tied_output) {
     const TensorInfo &o = tensor("output.weight");
-    m->out = {nullptr, c.vocab_size, H, row_bytes_of(o.type, H), o.type};
-    mats.push_back({&m->out, take((size_t)m->out.rows * m->out.row_bytes)});
+    m->out = make_mat(c.vocab_size, H, o.type);
+    mats.push_back({&m->out, take(m->out.g.bytes())});
   }
   vecs.push_back({&m->out_norm, take((size_t)H * 4)});
   vecs.push_back({&m->inv_freq, take((size_t)c.head_dim / 2 * 4)});
@@ -355,6 +388,7 @@ void load_model(vg_model *m, const std::string &path, uint32_t requested) {
   m->arena_bytes = off;
   CK(cudaMalloc(&m->arena, m->arena_bytes));
   for (auto &p : mats) p.mat->w = m->arena + p.off;
+  CK(cudaMemset(m->arena, 0, m->arena_bytes));  // tile padding stays zero
   for (auto &v : vecs) *v.first = reinterpret_cast<float *>(m->arena + v.second);
   if (c.tied_output) m->out = m->tok;
 
@@ -372,14 +406,17 @@ void load_model(vg_model *m, const std::string &path, uint32_t requested) {
   try {
     CK(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
     CK(cudaMalloc(&staging, max_raw));
-    auto repack = [&](const std::string &name, const DevMat &dst, size_t row0, uint32_t stride, uint32_t offset,
+    // row0: first packed row of this tensor inside dst (a multiple of the tile height)
+    auto repack = [&](const std::string &name, const DevMat &dst, uint32_t row0, uint32_t stride, uint32_t offset,
                       uint32_t pair_group) {
       const TensorInfo &t = tensor(name);
       CK(cudaMemcpyAsync(staging, data + t.offset, t.bytes, cudaMemcpyHostToDevice, st));
-      const uint32_t rows = (uint32_t)t.dims[1], cols = (uint32_t)t.dims[0];
+      const uint32_t rows = (uint32_t)t.dims[1];
+      if (row0 % kTileRows) fail(VG_EUNSUPPORTED, "tensor " + name + " does not start on a tile boundary");
+      TileGeom sub = dst.g;  // the tensor's rows as their own tiled matrix inside dst
+      sub.rows = dst.g.rows - row0;
       repack_kernel<<<std::min<uint32_t>(rows, 65535u), 256, 0, st>>>(
-          staging, t.type == GGML_Q8_0, rows, cols, dst.w + row0 * dst.row_bytes, dst.row_bytes, stride, offset,
-          pair_group);
+          staging, rows, sub, dst.w + dst.g.seg_base(row0, 0), stride, offset, pair_group);
       CK(cudaGetLastError());
       CK(cudaStreamSynchronize(st));
     };
@@ -446,13 +483,12 @@ void build_program(vg_stream *s, bool token_input, bool logits, std::vector<Laun
     const float alpha = eff_scale(c.embedding_scale);
     float *out = s->hid_a;
     prog.push_back({[=](cudaStream_t st, bool pdl) {
-      return launch_ex(embedding_kernel, dim3((H + 255) / 256), dim3(256), 0, st, pdl, (const uint8_t *)tok.w,
-                       (int)(tok.type == GGML_Q8_0), tok.rows, tok.cols, tok.row_bytes,
-                       (const uint32_t *)(ctrl + kCtrlToken), 0u, alpha, out, ctrl + kCtrlErr);
-    }, "embedding", 0, gguf_bytes(tok.type, H) + (uint64_t)H * 4});
+      return launch_ex(embedding_kernel, dim3((H + 255) / 256), dim3(256), 0, st, pdl, 1u, (const uint8_t *)tok.w,
+                       tok.g, (const uint32_t *)(ctrl + kCtrlToken), 0u, alpha, out, ctrl + kCtrlErr);
+    }, "embedding", 0, gguf_bytes(tok.type, H)});
   }
   const AttnFn afn = pick_attention(D);
-  const uint32_t asmem = attention_smem_bytes(G, D, s->chunk_cap, s->nsplit);
+  const uint32_t asmem = attention_smem_bytes(G, D, s->chunk_cap);
   ensure_smem((const void *)afn, dev, asmem);
   for (uint32_t l = 0; l < c.block_count; ++l) {
     const Layer &L = m->layers[l];
@@ -474,7 +510,7 @@ void build_program(vg_stream *s, bool token_input, bool logits, std::vector<Laun
     qkv.p.rope_scaling = c.rope_scaling_factor();
     qkv.p.ctrl = ctrl;
     prog.push_back({[=](cudaStream_t st, bool pdl) { return run_matvec(qkv, st, pdl); }, "qkv", l,
-                    gguf_bytes(L.qkv.type, H) * L.qkv.rows + (uint64_t)H * 4 + 2ull * c.kv_dim * 2});
+                    gguf_bytes(L.qkv.type, H) * L.qkv.g.rows + (uint64_t)H * 4 + 2ull * c.kv_dim * 2});
 
     AttnParams ap{};
     ap.q = s->q;
@@ -492,7 +528,7 @@ void build_program(vg_stream *s, bool token_input, bool logits, std::vector<Laun
     ap.fixed_pos = 0xFFFFFFFFu;
     ap.ctrl = ctrl;
     prog.push_back({[=](cudaStream_t st, bool pdl) {
-      return launch_ex(afn, dim3(ap.nsplit, ap.kv_heads), dim3(256), asmem, st, pdl, ap);
+      return launch_ex(afn, dim3(ap.nsplit, ap.kv_heads), dim3(kAttnThreads), asmem, st, pdl, kAttnCluster, ap);
     }, "attention", l, 2ull * c.kv_dim * 2, true});
 
     MvPlan o = plan_matvec<Mode::RESID, Pro::COPY>(L.o, dev, sms);
@@ -502,7 +538,7 @@ void build_program(vg_stream *s, bool token_input, bool logits, std::vector<Laun
     o.p.alpha = rs;
     o.p.ctrl = ctrl;
     prog.push_back({[=](cudaStream_t st, bool pdl) { return run_matvec(o, st, pdl); }, "o_proj", l,
-                    gguf_bytes(L.o.type, H) * L.o.rows});
+                    gguf_bytes(L.o.type, H) * L.o.g.rows});
 
     MvPlan gu = plan_matvec<Mode::SWIGLU, Pro::RMSNORM>(L.gateup, dev, sms);
     gu.p.xsrc = s->hid_b;
@@ -511,7 +547,7 @@ void build_program(vg_stream *s, bool token_input, bool logits, std::vector<Laun
     gu.p.out = s->gate;
     gu.p.ctrl = ctrl;
     prog.push_back({[=](cudaStream_t st, bool pdl) { return run_matvec(gu, st, pdl); }, "gate_up", l,
-                    gguf_bytes(L.gateup.type, H) * L.gateup.rows + (uint64_t)H * 4});
+                    gguf_bytes(L.gateup.type, H) * L.gateup.g.rows + (uint64_t)H * 4});
 
     MvPlan dn = plan_matvec<Mode::RESID, Pro::COPY>(L.down, dev, sms);
     dn.p.xsrc = s->gate;
@@ -520,7 +556,7 @@ void build_program(vg_stream *s, bool token_input, bool logits, std::vector<Laun
     dn.p.alpha = rs;
     dn.p.ctrl = ctrl;
     prog.push_back({[=](cudaStream_t st, bool pdl) { return run_matvec(dn, st, pdl); }, "down", l,
-                    gguf_bytes(L.down.type, c.feed_forward_length) * L.down.rows});
+                    gguf_bytes(L.down.type, c.feed_forward_length) * L.down.g.rows});
   }
   {
     float *hid = s->hid_a, *y = s->out_norm;
@@ -528,7 +564,7 @@ void build_program(vg_stream *s, bool token_input, bool logits, std::vector<Laun
     const float eps = c.rms_epsilon;
     prog.push_back({[=](cudaStream_t st, bool pdl) {
       return launch_ex(residual_rmsnorm_kernel, dim3(1), dim3(std::min<uint32_t>(1024u, round_up(H, 32))), 0, st,
-                       pdl, hid, (const float *)nullptr, w, H, eps, 1.0f, y, ctrl, 1);
+                       pdl, 1u, hid, (const float *)nullptr, w, H, eps, 1.0f, y, ctrl, 1);
     }, "final_norm", c.block_count, (uint64_t)H * 4});
   }
   if (logits) {
@@ -538,7 +574,7 @@ void build_program(vg_stream *s, bool token_input, bool logits, std::vector<Laun
     lg.p.alpha = eff_scale(c.logit_scale);
     lg.p.ctrl = ctrl;
     prog.push_back({[=](cudaStream_t st, bool pdl) { return run_matvec(lg, st, pdl); }, "logits", c.block_count,
-                    gguf_bytes(m->out.type, H) * m->out.rows});
+                    gguf_bytes(m->out.type, H) * m->out.g.rows});
   }
 }
 
@@ -676,16 +712,16 @@ int vg_gguf_inspect(const char *path, int format, vg_model_info *info, char *err
     auto add = [&](size_t b) { bytes = round_up_sz(bytes + b, 256); };
     for (uint32_t l = 0; l < c.block_count; ++l) {
       auto t = [&](const char *s) { return tmp.summary.find(strf("blk.%u.%s.weight", l, s))->type; };
-      add((size_t)(c.embedding_length + 2 * c.kv_dim) * row_bytes_of(t("attn_q"), c.embedding_length));
-      add((size_t)c.embedding_length * row_bytes_of(t("attn_output"), c.embedding_length));
-      add((size_t)2 * c.feed_forward_length * row_bytes_of(t("ffn_gate"), c.embedding_length));
-      add((size_t)c.embedding_length * row_bytes_of(t("ffn_down"), c.feed_forward_length));
+      add(packed_bytes(t("attn_q"), c.embedding_length + 2 * c.kv_dim, c.embedding_length));
+      add(packed_bytes(t("attn_output"), c.embedding_length, c.embedding_length));
+      add(packed_bytes(t("ffn_gate"), 2 * c.feed_forward_length, c.embedding_length));
+      add(packed_bytes(t("ffn_down"), c.embedding_length, c.feed_forward_length));
       add((size_t)c.embedding_length * 4);
       add((size_t)c.embedding_length * 4);
     }
-    add((size_t)c.vocab_size * row_bytes_of(tmp.summary.find("token_embd.weight")->type, c.embedding_length));
+    add(packed_bytes(tmp.summary.find("token_embd.weight")->type, c.vocab_size, c.embedding_length));
     if (!c.tied_output)
-      add((size_t)c.vocab_size * row_bytes_of(tmp.summary.find("output.weight")->type, c.embedding_length));
+      add(packed_bytes(tmp.summary.find("output.weight")->type, c.vocab_size, c.embedding_length));
     add((size_t)c.embedding_length * 4);
     add((size_t)c.head_dim / 2 * 4);
     add((size_t)c.head_dim / 2 * 4);
@@ -780,8 +816,7 @@ int vg_stream_create(vg_model *m, uint32_t max_context, vg_stream **out) {
     CK(cudaSetDevice(m->ctx->device));
     s->max_ctx = max_context;
     const uint32_t H = c.embedding_length, D = c.head_dim, G = c.head_count / c.head_count_kv;
-    s->nsplit = std::max<uint32_t>(16u, (max_context + 2047u) / 2048u);
-    s->chunk_cap = (max_context + s->nsplit - 1) / s->nsplit;
+    plan_attention(max_context, s->nsplit, s->chunk_cap);
     const size_t kv_elems = (size_t)c.block_count * c.head_count_kv * max_context * D;
     CK(cudaMalloc(&s->kc, kv_elems * 2 * sizeof(__half)));
     s->vc = s->kc + kv_elems;
@@ -796,8 +831,8 @@ int vg_stream_create(vg_model *m, uint32_t max_context, vg_stream **out) {
     const size_t o_a = take((size_t)H * 4), o_b = take((size_t)H * 4), o_q = take((size_t)H * 4),
                  o_att = take((size_t)H * 4), o_g = take((size_t)c.feed_forward_length * 4),
                  o_lg = take((size_t)c.vocab_size * 4),
-                 o_part = take((size_t)c.head_count_kv * s->nsplit * G * (D + 2) * 4),
-                 o_tk = take((size_t)c.head_count_kv * 4);
+                 o_part = take((size_t)c.head_count_kv * (s->nsplit / kAttnCluster) * G * (D + 2) * 4),
+                 o_tk = take((size_t)c.head_count_kv * G * 4);
     CK(cudaMalloc(&s->dev_block, off));
     CK(cudaMemset(s->dev_block, 0, off));
     uint8_t *b = static_cast<uint8_t *>(s->dev_block);
@@ -1182,8 +1217,8 @@ static int kguard(const std::function<void()> &f) {
 
 int vg_k_packed_bytes(int dtype, uint32_t rows, uint32_t cols, uint64_t *bytes) {
   if (!bytes || rows == 0 || cols == 0) return VG_EINVAL;
-  if (dtype == VG_FORMAT_Q8_0 && cols % 32 == 0) *bytes = (uint64_t)rows * q8_row_bytes(cols);
-  else if (dtype == VG_FORMAT_F16 && cols % 8 == 0) *bytes = (uint64_t)rows * f16_row_bytes(cols);
+  if (dtype == VG_FORMAT_Q8_0 && cols % 32 == 0) *bytes = packed_bytes(GGML_Q8_0, rows, cols);
+  else if (dtype == VG_FORMAT_F16 && cols % 8 == 0) *bytes = packed_bytes(GGML_F16, rows, cols);
   else return VG_EUNSUPPORTED;
   return VG_OK;
 }
@@ -1194,9 +1229,11 @@ int vg_k_repack(int dtype, const void *gguf_bytes, uint32_t rows, uint32_t cols,
   if (rc) return rc;
   if (!gguf_bytes || !packed) return VG_EINVAL;
   return kguard([&] {
-    const uint32_t rb = dtype == VG_FORMAT_Q8_0 ? q8_row_bytes(cols) : f16_row_bytes(cols);
-    repack_kernel<<<std::min<uint32_t>(rows, 65535u), 256, 0, (cudaStream_t)cuda_stream>>>(
-        (const uint8_t *)gguf_bytes, dtype == VG_FORMAT_Q8_0, rows, cols, (uint8_t *)packed, rb, 1, 0, 0);
+    cudaStream_t st = (cudaStream_t)cuda_stream;
+    CK(cudaMemsetAsync(packed, 0, b, st));
+    const TileGeom g{rows, cols, dtype == VG_FORMAT_Q8_0 ? 1u : 0u};
+    repack_kernel<<<std::min<uint32_t>(rows, 65535u), 256, 0, st>>>((const uint8_t *)gguf_bytes, rows, g,
+                                                                     (uint8_t *)packed, 1, 0, 0);
     CK(cudaGetLastError());
   });
 }
@@ -1211,7 +1248,8 @@ int vg_k_matvec(int dtype, const void *packed, uint32_t rows, uint32_t cols, con
     int dev = 0, sms = 0;
     CK(cudaGetDevice(&dev));
     CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-    DevMat m{(uint8_t *)packed, rows, cols, (uint32_t)(b / rows), (uint32_t)dtype};
+    DevMat m = make_mat(rows, cols, dtype == VG_FORMAT_Q8_0 ? GGML_Q8_0 : GGML_F16);
+    m.w = (uint8_t *)packed;
     MvPlan pl = plan_matvec<Mode::PLAIN, Pro::COPY>(m, dev, (uint32_t)sms);
     pl.p.xsrc = x;
     pl.p.out = y;
@@ -1229,9 +1267,9 @@ int vg_k_embedding(int dtype, const void *packed, uint32_t rows, uint32_t cols, 
   if (!packed || !out) return VG_EINVAL;
   if (row >= rows) return VG_ERANGE;
   return kguard([&] {
+    const TileGeom g{rows, cols, dtype == VG_FORMAT_Q8_0 ? 1u : 0u};
     embedding_kernel<<<(cols + 255) / 256, 256, 0, (cudaStream_t)cuda_stream>>>(
-        (const uint8_t *)packed, dtype == VG_FORMAT_Q8_0, rows, cols, (uint32_t)(b / rows), nullptr, row, alpha, out,
-        kernel_ctrl() + kCtrlErr);
+        (const uint8_t *)packed, g, nullptr, row, alpha, out, kernel_ctrl() + kCtrlErr);
     CK(cudaGetLastError());
   });
 }
@@ -1258,13 +1296,12 @@ int vg_k_attention(const float *q, const uint16_t *k_cache, const uint16_t *v_ca
     CK(cudaGetDevice(&dev));
     const uint32_t G = heads / kv_heads;
     AttnParams ap{};
-    ap.nsplit = std::max<uint32_t>(16u, (ctx + 2047u) / 2048u);
-    ap.chunk_cap = (ctx + ap.nsplit - 1) / ap.nsplit;
-    const size_t part_bytes = (size_t)kv_heads * ap.nsplit * G * (head_dim + 2) * 4;
+    plan_attention(ctx, ap.nsplit, ap.chunk_cap);
+    const size_t part_bytes = (size_t)kv_heads * (ap.nsplit / kAttnCluster) * G * (head_dim + 2) * 4;
     void *scratch = nullptr;
-    CK(cudaMallocAsync(&scratch, part_bytes + 256 + kv_heads * 4, st));
+    CK(cudaMallocAsync(&scratch, round_up_sz(part_bytes, 256) + (size_t)kv_heads * G * 4, st));
     uint32_t *tickets = (uint32_t *)((uint8_t *)scratch + round_up_sz(part_bytes, 256));
-    CK(cudaMemsetAsync(tickets, 0, kv_heads * 4, st));
+    CK(cudaMemsetAsync(tickets, 0, (size_t)kv_heads * G * 4, st));
     ap.q = q;
     ap.kc = (const __half *)k_cache;
     ap.vc = (const __half *)v_cache;
@@ -1278,9 +1315,9 @@ int vg_k_attention(const float *q, const uint16_t *k_cache, const uint16_t *v_ca
     ap.fixed_pos = position;
     ap.ctrl = nullptr;
     const AttnFn fn = pick_attention(head_dim);
-    const uint32_t smem = attention_smem_bytes(G, head_dim, ap.chunk_cap, ap.nsplit);
+    const uint32_t smem = attention_smem_bytes(G, head_dim, ap.chunk_cap);
     ensure_smem((const void *)fn, dev, smem);
-    cudaError_t e = launch_ex(fn, dim3(ap.nsplit, kv_heads), dim3(256), smem, st, false, ap);
+    cudaError_t e = launch_ex(fn, dim3(ap.nsplit, kv_heads), dim3(kAttnThreads), smem, st, false, kAttnCluster, ap);
     cudaError_t e2 = cudaFreeAsync(scratch, st);
     CK(e);
     CK(e2);
