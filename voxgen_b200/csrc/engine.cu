@@ -183,12 +183,6 @@ struct MvPlan {
   MvParams p{};
 };
 
-uint32_t next_pow2(uint32_t x) {
-  uint32_t p = 1;
-  while (p < x) p <<= 1;
-  return p;
-}
-
 template <Mode M, Pro P>
 MvPlan plan_matvec(const DevMat &m, int device, uint32_t sms) {
   MvPlan pl;
@@ -202,18 +196,21 @@ MvPlan plan_matvec(const DevMat &m, int device, uint32_t sms) {
   p.g = g;
   p.a_bytes = mv_a_bytes(g.q8, cols_pad);
   p.plane = mv_a_plane(g.q8, cols_pad);
-  // Tile reduction buffers: one per tile of the CTA when that is at most 64,
-  // else 64 (a warp cannot run more than a few tiles ahead of the others).
-  p.rb = next_pow2(std::max<uint32_t>(1u, std::min<uint32_t>(per_cta, 64u)));
-  // Ring slots per consumer warp: as many as the budget holds, at most 4 and
-  // at most the warp's share of items.
-  const uint32_t items_per_warp = (per_cta * g.nseg() + kMvConsumers - 1) / kMvConsumers;
-  p.spw = 1;
+  // One partial-sum row per tile of the CTA.
+  p.rb = per_cta;
+  // Pipeline stages: as many as the budget holds (up to 8), at most the CTA's
+  // stage count, at least 2 so a copy is in flight while a stage is consumed.
+  const uint32_t n_st = (per_cta * g.nseg() + kStageSegs - 1) / kStageSegs;
+  p.stages = 1;
   MvSmem probe(p);
-  const uint32_t per_slot = kMvConsumers * (g.seg_bytes() + 16u);
-  const uint32_t fixed = probe.total - per_slot;
-  const uint32_t fit = kSmemBudget > fixed ? (kSmemBudget - fixed) / per_slot : 1u;
-  p.spw = std::max<uint32_t>(1u, std::min<uint32_t>({fit, 4u, std::max<uint32_t>(1u, items_per_warp)}));
+  const uint32_t per_stage = kStageSegs * g.seg_bytes() + 16u;
+  const uint32_t fixed = probe.total - per_stage;
+  const uint32_t fit = kSmemBudget > fixed ? (kSmemBudget - fixed) / per_stage : 1u;
+  // An even number of stages keeps each stage slot with one warp group (see the kernel).
+  uint32_t st = std::min<uint32_t>({fit, 8u, std::max<uint32_t>(2u, n_st + (n_st & 1u))});
+  st &= ~1u;
+  if (st < 2) fail(VG_EUNSUPPORTED, strf("matrix of %u columns does not fit two pipeline stages", g.cols));
+  p.stages = st;
   const uint32_t smem = MvSmem(p).total;
   if (smem > kSmemMax) fail(VG_EUNSUPPORTED, strf("matrix of %u columns does not fit in shared memory", g.cols));
   pl.fn = matvec_fn<M, P>(g.q8 != 0);

@@ -34,11 +34,14 @@ enum class Mode { PLAIN, RESID, SWIGLU, QKV };
 enum class Pro { COPY, RMSNORM };
 
 constexpr int kMvConsumers = 8;                       // consumer warps per matvec CTA
-constexpr int kMvThreads = 32 * (1 + kMvConsumers);   // + one producer warp
+constexpr int kMvThreads = 32 * (kMvConsumers + 1);   // + one producer warp
 constexpr uint32_t kTileRows = 8;
 constexpr uint32_t kSegSteps = 16;                    // K-steps per segment
 constexpr uint32_t kStepBytes = 256;                  // 8 rows x 32 bytes
 constexpr uint32_t kSegQsBytes = kSegSteps * kStepBytes;
+constexpr uint32_t kStageSegs = 4;                    // segments per pipeline stage (one bulk copy)
+constexpr uint32_t kChunkSteps = kStageSegs * kSegSteps / 8;  // K-steps per consumer warp per stage
+static_assert(kChunkSteps == 8, "a stage holds one 8 K-step chunk per consumer warp");
 
 // Slots of the per-stream device control block.
 constexpr uint32_t kCtrlPos = 0;    // decode position of the step being run
@@ -72,8 +75,8 @@ struct TileGeom {
 struct MvParams {
   const uint8_t *w;       // segmented tiles
   TileGeom g;
-  uint32_t spw;           // ring slots per consumer warp
-  uint32_t rb;            // tile reduction buffers (power of two)
+  uint32_t stages;        // pipeline stages in the shared-memory ring
+  uint32_t rb;            // tiles per CTA (partial-sum buffer rows)
   uint32_t a_bytes;       // shared bytes of the activation operand region (128-aligned)
   uint32_t plane;         // bytes between activation planes
   const float *xsrc;      // input vector (COPY) or hidden state (RMSNORM)
@@ -93,16 +96,14 @@ struct MvParams {
 
 // Shared-memory plan of one matvec CTA (host and device agree on it).
 struct MvSmem {
-  uint32_t a, ring, bars, red, cnt, gen, scr, total;
+  uint32_t a, ring, bars, red, scr, total;
   __host__ __device__ MvSmem(const MvParams &p) {
-    const uint32_t ns = kMvConsumers * p.spw;
+    const uint32_t ns = p.stages;
     a = 0;
     ring = p.a_bytes;
-    bars = ring + ns * p.g.seg_bytes();
+    bars = ring + ns * kStageSegs * p.g.seg_bytes();
     red = bars + ns * 16u;
-    cnt = red + p.rb * kMvConsumers * kTileRows * 4u;
-    gen = cnt + p.rb * 4u;
-    scr = gen + p.rb * 4u;
+    scr = red + p.rb * kMvConsumers * kTileRows * 4u;
     total = scr + 64u * 4u;
   }
 };
@@ -130,6 +131,30 @@ __device__ __forceinline__ float warp_max(float v) {
   return v;
 }
 
+// Sums 8 per-lane values over the warp with 9 shuffles (instead of 8 x 5): on
+// return, lane l holds the warp total of value (l >> 2) & 7.
+__device__ __forceinline__ float warp_sum8(const float (&v)[8], uint32_t lane) {
+  const bool h4 = (lane >> 4) & 1, h2 = (lane >> 3) & 1, h1 = (lane >> 2) & 1;
+  float a[4], b[2], c;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float keep = h4 ? v[4 + i] : v[i], send = h4 ? v[i] : v[4 + i];
+    a[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const float keep = h2 ? a[2 + i] : a[i], send = h2 ? a[i] : a[2 + i];
+    b[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+  {
+    const float keep = h1 ? b[1] : b[0], send = h1 ? b[0] : b[1];
+    c = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+  }
+  c += __shfl_xor_sync(0xffffffffu, c, 2);
+  c += __shfl_xor_sync(0xffffffffu, c, 1);
+  return c;
+}
+
 __device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], const void *p) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
@@ -138,7 +163,7 @@ __device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], const void *p) {
 
 // D = A(16x32 s8, row) * B(32x8 s8, col); rows 8-15 of A are zero.
 __device__ __forceinline__ void mma_s8(int (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
       "{%10, %11, %12, %13};"
       : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
@@ -147,7 +172,7 @@ __device__ __forceinline__ void mma_s8(int (&d)[4], uint32_t a0, uint32_t a2, ui
 
 // C += A(16x16 f16, row) * B(16x8 f16, col) in fp32; rows 8-15 of A are zero.
 __device__ __forceinline__ void mma_f16(float (&c)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
       "{%0, %1, %2, %3};"
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
@@ -218,103 +243,120 @@ __device__ __forceinline__ void mv_epilogue(const MvParams &p, uint32_t R, float
 // ---------------------------------------------------------------------------
 // Matrix-vector product with fused prologue and epilogue.
 //
-// CTA c owns a contiguous range of tiles; its segments ("items", tile-major)
-// are dealt round-robin to the 8 consumer warps. Warp 0 (lane 0) streams the
-// items into the ring with cp.async.bulk; each consumer warp owns `spw` slots
-// and consumes its items in order, so every mbarrier parity wait is at most
-// one phase ahead. Streaming starts before griddepcontrol.wait: the weights
-// arrive while the previous kernel of the step is still running.
-// After the dependency resolves the consumers build the activation operand
-// (RMSNorm of the hidden state or a copy, then the exact int8 digits or fp16
-// hi/lo split), run the tensor-core K-steps of their items, and reduce each
-// tile's 8 rows across warps through shared memory; the last warp to finish a
-// tile (arrival counter) sums the warps' partials in warp order (so results
-// are deterministic) and runs the epilogue.
+// CTA c owns a contiguous range of tiles, i.e. a contiguous run of segments in
+// HBM. The producer warp streams that run in stages of kStageSegs segments
+// (one ~17 KB cp.async.bulk per stage: large copies are what reach full HBM
+// bandwidth on this part) into a ring of shared-memory stages, starting
+// before griddepcontrol.wait so the weights arrive while the previous kernel
+// of the step is still running. Consumer warp w takes segments w, w + 8, ...
+// of the run. After the dependency resolves the consumers build the
+// activation operand (RMSNorm of the hidden state or a copy, then the exact
+// int8 digits or the fp16 hi/lo split) and run the tensor-core K-steps of
+// their segments, keeping one partial per (tile, warp) in shared memory; a
+// single barrier at the end precedes the reduction of each tile's 8 partials
+// in warp order (deterministic) and the epilogue. Warps never wait on each
+// other while streaming.
 // ---------------------------------------------------------------------------
 template <bool Q8, Mode M, Pro P>
 __global__ void __launch_bounds__(kMvThreads, 1) matvec_kernel(const __grid_constant__ MvParams p) {
   extern __shared__ __align__(128) uint8_t smem[];
   const MvSmem L(p);
   const TileGeom g = p.g;
-  const uint32_t NSEG = g.nseg(), SEGB = g.seg_bytes(), SPW = p.spw, NS = kMvConsumers * SPW;
+  const uint32_t NSEG = g.nseg(), SEGB = g.seg_bytes(), NST = p.stages;
+  const uint32_t STB = kStageSegs * SEGB;
   uint8_t *ring = smem + L.ring;
   uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.bars);
-  uint64_t *empty = full + NS;
-  float *red = reinterpret_cast<float *>(smem + L.red);
-  uint32_t *cnt = reinterpret_cast<uint32_t *>(smem + L.cnt);
-  uint32_t *gen = reinterpret_cast<uint32_t *>(smem + L.gen);
+  uint64_t *empty = full + NST;
+  float *red = reinterpret_cast<float *>(smem + L.red);  // [tile][warp][row] partial sums
   float *scr = reinterpret_cast<float *>(smem + L.scr);
 
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
   const uint32_t T = g.tiles();
   const uint32_t t0 = (uint32_t)((uint64_t)blockIdx.x * T / gridDim.x);
   const uint32_t t1 = (uint32_t)((uint64_t)(blockIdx.x + 1) * T / gridDim.x);
-  const uint32_t n_items = (t1 - t0) * NSEG;
+  const uint32_t n_items = (t1 - t0) * NSEG;                    // segments of this CTA
+  const uint32_t n_st = (n_items + kStageSegs - 1) / kStageSegs;  // stages of this CTA
   uint32_t *err = p.ctrl + kCtrlErr;
 
   if (threadIdx.x == 0) {
-    for (uint32_t i = 0; i < NS; ++i) {
+    for (uint32_t i = 0; i < NST; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], 1);
+      mbar_init(&empty[i], kStageSegs);  // a stage's segments go to 4 different warps
     }
     fence_mbar_init();
   }
-  for (uint32_t i = threadIdx.x; i < p.rb; i += blockDim.x) {
-    cnt[i] = 0;
-    gen[i] = 0;
-  }
+  for (uint32_t i = threadIdx.x; i < (t1 - t0) * kMvConsumers * kTileRows; i += blockDim.x) red[i] = 0.f;
   __syncthreads();
   pdl_launch_dependents();
 
-  if (warp == 0) {
+  if (warp == kMvConsumers) {
+    // ---------------- producer ----------------
     if (lane == 0) {
-      uint32_t kw[kMvConsumers] = {};
-      bool ok = true;
-      for (uint32_t i = 0; i < n_items && ok; ++i) {
-        const uint32_t w = i % kMvConsumers, k = kw[w];
-        const uint32_t slot = w * SPW + k % SPW;
-        if (k >= SPW && !mbar_wait_bounded(&empty[slot], ((k / SPW) - 1u) & 1u)) {
-          set_error(err, kErrProducerWait);
-          ok = false;
+      const uint8_t *src = p.w + (uint64_t)t0 * NSEG * SEGB;
+      uint32_t j = 0;
+      for (; j < n_st; ++j) {
+        const uint32_t slot = j % NST;
+        if (j >= NST && !mbar_wait_bounded(&empty[slot], ((j / NST) - 1u) & 1u)) {
+          set_error(err, kErrConsumerWait);
           break;
         }
-        kw[w] = k + 1;
-        const uint8_t *src = p.w + ((uint64_t)(t0 + i / NSEG) * NSEG + i % NSEG) * SEGB;
-        mbar_arrive_expect_tx(&full[slot], SEGB);
-        bulk_g2s(ring + slot * SEGB, src, SEGB, &full[slot]);
+        const uint32_t segs = min(kStageSegs, n_items - j * kStageSegs);
+        mbar_arrive_expect_tx(&full[slot], segs * SEGB);
+        bulk_g2s(ring + slot * STB, src + (uint64_t)j * STB, segs * SEGB, &full[slot]);
       }
-      // Never leave with copies in flight: wait (bounded) for the last phase
-      // armed on every slot.
-      for (uint32_t w = 0; w < kMvConsumers && ok; ++w)
-        for (uint32_t j = 0; j < SPW && j < kw[w]; ++j) {
-          const uint32_t last = j + ((kw[w] - 1u - j) / SPW) * SPW;
-          if (!mbar_wait_bounded(&full[w * SPW + j], (last / SPW) & 1u)) {
-            set_error(err, kErrDrainWait);
-            ok = false;
-            break;
-          }
+      // never leave with copies in flight: wait (bounded) for the last phase of each stage
+      for (uint32_t i = 0; i < NST && i < j; ++i) {
+        const uint32_t last = i + ((j - 1u - i) / NST) * NST;
+        if (!mbar_wait_bounded(&full[i], (last / NST) & 1u)) {
+          set_error(err, kErrDrainWait);
+          break;
         }
+      }
     }
     return;
   }
 
-  // ---------------- consumers ----------------
+  // ---------------- consumers: activation operand ----------------
   constexpr uint32_t NCT = kMvConsumers * 32;
-  const uint32_t cw = warp - 1;
+  const uint32_t cw = warp;
   const uint32_t C = g.cols;
   const uint32_t cols_pad = NSEG * g.seg_cols();
   uint8_t *areg = smem + L.a;
-  float *sx = reinterpret_cast<float *>(areg + 3u * p.plane);  // Q8: per-block 2^e
+  float *sx = reinterpret_cast<float *>(areg + 3u * p.plane);      // Q8: per-block 2^e
   float *xscale = reinterpret_cast<float *>(areg + 2u * p.plane);  // F16: 2^e of the whole vector
 
+  // Every activation load is issued up front (one round trip to L2); the
+  // RMSNorm weight does not depend on the previous kernel and is loaded
+  // before griddepcontrol.wait. Warp cw handles 32-element blocks cw, cw + 8,
+  // ... with one element per lane, so a block's max is one redux.
+  // Register path for up to 4096 (RMSNorm inputs) or 6144 (copied inputs) columns.
+  constexpr uint32_t MAXJ = P == Pro::RMSNORM ? 16 : 24;
+  const uint32_t NBLK = cols_pad / 32u;
+  const uint32_t J = (NBLK + kMvConsumers - 1 - cw) / kMvConsumers;  // blocks of this warp
+  float xr[MAXJ], wr[MAXJ];
+  const bool regs = (NBLK + kMvConsumers - 1) / kMvConsumers <= MAXJ;
+  if constexpr (P == Pro::RMSNORM) {
+#pragma unroll
+    for (uint32_t j = 0; j < MAXJ; ++j) {
+      const uint32_t k = (cw + j * kMvConsumers) * 32u + lane;
+      wr[j] = (regs && j < J && k < C) ? p.normw[k] : 0.f;
+    }
+  }
   pdl_wait();
+#pragma unroll
+  for (uint32_t j = 0; j < MAXJ; ++j) {
+    const uint32_t k = (cw + j * kMvConsumers) * 32u + lane;
+    xr[j] = (regs && j < J && k < C) ? p.xsrc[k] : 0.f;
+  }
   float inv_rms = 1.0f;
   if constexpr (P == Pro::RMSNORM) {
     // rmsnorm.comp:21-42 (inversesqrt taken as 1/sqrt); x = h * inv_rms * w.
     float ss = 0.f;
-    for (uint32_t i = threadIdx.x - 32; i < C; i += NCT) {
-      const float v = p.xsrc[i];
-      ss += v * v;
+    if (regs) {
+#pragma unroll
+      for (uint32_t j = 0; j < MAXJ; ++j) ss += xr[j] * xr[j];
+    } else {
+      for (uint32_t i = threadIdx.x; i < C; i += NCT) ss += p.xsrc[i] * p.xsrc[i];
     }
     ss = warp_sum(ss);
     if (lane == 0) scr[cw] = ss;
@@ -323,22 +365,25 @@ __global__ void __launch_bounds__(kMvThreads, 1) matvec_kernel(const __grid_cons
 #pragma unroll
     for (int w = 0; w < kMvConsumers; ++w) tot += scr[w];
     inv_rms = 1.0f / sqrtf(tot / (float)C + p.eps);
+    if (regs) {
+#pragma unroll
+      for (uint32_t j = 0; j < MAXJ; ++j) xr[j] = __fmul_rn(__fmul_rn(xr[j], inv_rms), wr[j]);
+    }
   }
-  auto xval = [&](uint32_t k) -> float {
+  // element k when the row is too long for the register path
+  auto xglobal = [&](uint32_t k) -> float {
     if (k >= C) return 0.f;
     const float v = p.xsrc[k];
     if constexpr (P == Pro::RMSNORM) return __fmul_rn(__fmul_rn(v, inv_rms), p.normw[k]);
     return v;
   };
   if constexpr (Q8) {
-    // one warp per 32-element block: digits and the block exponent
+    // int8 digits and the per-block exponent (warp-collective per block)
     int8_t *d0p = reinterpret_cast<int8_t *>(areg), *d1p = d0p + p.plane, *d2p = d1p + p.plane;
-    for (uint32_t b = cw; b < cols_pad / 32u; b += kMvConsumers) {
-      const uint32_t k = b * 32u + lane;
-      const float x = xval(k);
+    auto digits = [&](uint32_t j, float x) {
+      const uint32_t b = cw + j * kMvConsumers, k = b * 32u + lane;
       const uint32_t mb = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(x)));
-      int e = 0;
-      int q0 = 0, q1 = 0, q2 = 0;
+      int e = 0, q0 = 0, q1 = 0, q2 = 0;
       const bool nz = block_exponent(mb, e);
       if (nz) {
         const float v = x * pow2f(-e);  // exact, |v| < 64
@@ -352,11 +397,23 @@ __global__ void __launch_bounds__(kMvThreads, 1) matvec_kernel(const __grid_cons
       d1p[k] = (int8_t)q1;
       d2p[k] = (int8_t)q2;
       if (lane == 0) sx[b] = nz ? pow2f(e) : 0.f;
+    };
+    if (regs) {
+#pragma unroll
+      for (uint32_t j = 0; j < MAXJ; ++j)
+        if (j < J) digits(j, xr[j]);
+    } else {
+      for (uint32_t j = 0; j < J; ++j) digits(j, xglobal((cw + j * kMvConsumers) * 32u + lane));
     }
   } else {
     // whole-vector power-of-two scale, then fp16 hi + lo
     float m = 0.f;
-    for (uint32_t k = threadIdx.x - 32; k < C; k += NCT) m = fmaxf(m, fabsf(xval(k)));
+    if (regs) {
+#pragma unroll
+      for (uint32_t j = 0; j < MAXJ; ++j) m = fmaxf(m, fabsf(xr[j]));
+    } else {
+      for (uint32_t j = 0; j < J; ++j) m = fmaxf(m, fabsf(xglobal((cw + j * kMvConsumers) * 32u + lane)));
+    }
     m = warp_max(m);
     named_bar(1, NCT);  // scr[] reuse after the RMSNorm reduction
     if (lane == 0) scr[cw] = m;
@@ -368,126 +425,145 @@ __global__ void __launch_bounds__(kMvThreads, 1) matvec_kernel(const __grid_cons
     const int e = ef < 20 ? 0 : (int)ef - 127 - 13;  // max|x| * 2^-e < 2^14
     const float inv = pow2f(-e);
     __half *hi = reinterpret_cast<__half *>(areg), *lo = reinterpret_cast<__half *>(areg + p.plane);
-    for (uint32_t k = threadIdx.x - 32; k < cols_pad; k += NCT) {
-      const float v = xval(k) * inv;
+    auto halves = [&](uint32_t j, float x) {
+      const uint32_t k = (cw + j * kMvConsumers) * 32u + lane;
+      const float v = x * inv;
       const __half h = __float2half_rn(v);
       hi[k] = h;
       lo[k] = __float2half_rn(v - __half2float(h));
+    };
+    if (regs) {
+#pragma unroll
+      for (uint32_t j = 0; j < MAXJ; ++j)
+        if (j < J) halves(j, xr[j]);
+    } else {
+      for (uint32_t j = 0; j < J; ++j) halves(j, xglobal((cw + j * kMvConsumers) * 32u + lane));
     }
-    if (threadIdx.x == 32) *xscale = pow2f(e);
+    if (threadIdx.x == 0) *xscale = pow2f(e);
   }
   named_bar(1, NCT);
 
+  // ---------------- consumers: K-step chunks ----------------
   const uint32_t pos = (M == Mode::QKV) ? p.ctrl[kCtrlPos] : 0u;
   const uint32_t gq = lane >> 2, tq = lane & 3u;
   // digit / half plane this lane feeds into the A fragment (rows 0-2 or 0-1)
   const bool arow = Q8 ? (gq < 3) : (gq < 2);
   const uint8_t *aplane = areg + (arow ? gq : 0u) * p.plane;
   const float dscale = gq == 0 ? 1.0f : gq == 1 ? 0.0078125f : 6.103515625e-05f;  // 2^(-7 gq)
-  uint32_t k = 0;  // items consumed by this warp
+  float acc0 = 0.f, acc1 = 0.f;
+  float cf[4][4] = {};  // F16: four independent accumulators (one per K-step of a batch)
   bool ok = true;
-  for (uint32_t t = t0; t < t1; ++t) {
-    float acc0 = 0.f, acc1 = 0.f;
-    float cf[4] = {0.f, 0.f, 0.f, 0.f};
-    const uint32_t i0 = (t - t0) * NSEG;
-    for (uint32_t s = (cw + kMvConsumers - i0 % kMvConsumers) % kMvConsumers; ok && s < NSEG;
-         s += kMvConsumers) {
-      const uint32_t slot = cw * SPW + k % SPW;
-      if (!mbar_wait_bounded(&full[slot], (k / SPW) & 1u)) {
-        set_error(err, kErrConsumerWait);
-        ok = false;
-        break;
-      }
-      const uint8_t *seg = ring + slot * SEGB;
-      const uint32_t ks0 = s * kSegSteps;
-#pragma unroll 2
-      for (uint32_t ks = 0; ks < kSegSteps; ks += 2) {
-        uint32_t b[4];
-        ldmatrix_x4(b, seg + ks * kStepBytes + lane * 16u);
-#pragma unroll
-        for (uint32_t j = 0; j < 2; ++j) {
-          const uint32_t kg = ks0 + ks + j;
-          if constexpr (Q8) {
-            uint32_t a0 = 0, a2 = 0;
-            if (arow) {
-              a0 = *reinterpret_cast<const uint32_t *>(aplane + kg * 32u + tq * 4u);
-              a2 = *reinterpret_cast<const uint32_t *>(aplane + kg * 32u + 16u + tq * 4u);
-            }
-            int c[4];
-            mma_s8(c, a0, a2, b[2 * j], b[2 * j + 1]);
-            if (arow) {
-              const __half2 dp =
-                  *reinterpret_cast<const __half2 *>(seg + kSegQsBytes + ((ks + j) * kTileRows + 2u * tq) * 2u);
-              const float sc = sx[kg] * dscale;
-              acc0 = fmaf((float)c[0], __low2float(dp) * sc, acc0);
-              acc1 = fmaf((float)c[1], __high2float(dp) * sc, acc1);
-            }
-          } else {
-            uint32_t a0 = 0, a2 = 0;
-            if (arow) {
-              a0 = *reinterpret_cast<const uint32_t *>(aplane + (kg * 16u + tq * 2u) * 2u);
-              a2 = *reinterpret_cast<const uint32_t *>(aplane + (kg * 16u + 8u + tq * 2u) * 2u);
-            }
-            mma_f16(cf, a0, a2, b[2 * j], b[2 * j + 1]);
-          }
-        }
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[slot]);
-      ++k;
-    }
-    // this warp's partial for the 8 rows of tile t: lanes 0-3 hold rows 2tq, 2tq+1
+
+  // This warp's partial of one tile's 8 rows (lanes 0-3 hold rows 2tq, 2tq+1)
+  // goes to red[tile][warp]; the final reduction sums the warps in order.
+  auto flush = [&](uint32_t rel) {
     float v0, v1;
     if constexpr (Q8) {
       v0 = acc0 + __shfl_down_sync(0xffffffffu, acc0, 4) + __shfl_down_sync(0xffffffffu, acc0, 8);
       v1 = acc1 + __shfl_down_sync(0xffffffffu, acc1, 4) + __shfl_down_sync(0xffffffffu, acc1, 8);
     } else {
-      v0 = (cf[0] + __shfl_down_sync(0xffffffffu, cf[0], 4)) * *xscale;
-      v1 = (cf[1] + __shfl_down_sync(0xffffffffu, cf[1], 4)) * *xscale;
+      const float c0 = (cf[0][0] + cf[1][0]) + (cf[2][0] + cf[3][0]);
+      const float c1 = (cf[0][1] + cf[1][1]) + (cf[2][1] + cf[3][1]);
+      v0 = (c0 + __shfl_down_sync(0xffffffffu, c0, 4)) * *xscale;
+      v1 = (c1 + __shfl_down_sync(0xffffffffu, c1, 4)) * *xscale;
     }
-    const uint32_t rel = t - t0, buf = rel & (p.rb - 1u), want_gen = rel / p.rb;
-    // the previous use of this buffer must have been reduced (bounded wait)
-    if (lane == 0 && rel >= p.rb) {
-      const uint64_t ts = globaltimer();
-      uint32_t it = 0;
-      while (*reinterpret_cast<volatile uint32_t *>(&gen[buf]) != want_gen) {
-        if (++it > kWaitMaxIters || ((it & 255u) == 0 && globaltimer() - ts > kWaitLimitNs)) {
-          set_error(err, kErrConsumerWait);
-          break;
-        }
-      }
-    }
-    __syncwarp();
     if (lane < 4) {
-      red[(buf * kMvConsumers + cw) * kTileRows + 2 * lane] = v0;
-      red[(buf * kMvConsumers + cw) * kTileRows + 2 * lane + 1] = v1;
+      red[(rel * kMvConsumers + cw) * kTileRows + 2 * lane] = v0;
+      red[(rel * kMvConsumers + cw) * kTileRows + 2 * lane + 1] = v1;
     }
-    __syncwarp();
-    uint32_t last = 0;
-    if (lane == 0) {
-      __threadfence_block();
-      last = atomicAdd(&cnt[buf], 1u) == kMvConsumers - 1;
-    }
-    last = __shfl_sync(0xffffffffu, last, 0);
-    if (last) {
-      __threadfence_block();
-      if (lane < 4) {
-        float a = 0.f, bsum = 0.f;
+    acc0 = acc1 = 0.f;
 #pragma unroll
-        for (int w = 0; w < kMvConsumers; ++w) {
-          a += *reinterpret_cast<volatile float *>(&red[(buf * kMvConsumers + w) * kTileRows + 2 * lane]);
-          bsum += *reinterpret_cast<volatile float *>(&red[(buf * kMvConsumers + w) * kTileRows + 2 * lane + 1]);
+    for (int a = 0; a < 4; ++a)
+#pragma unroll
+      for (int b = 0; b < 4; ++b) cf[a][b] = 0.f;
+  };
+
+  // Warp cw takes segments cw, cw + 8, cw + 16, ... of the CTA's run. Stage j
+  // holds segments 4j..4j+3, read by warps 0-3 (j even) or 4-7 (j odd), so a
+  // warp waits on every other stage; with an even number of stages a stage
+  // slot is always read by the same warp group and a parity wait is never
+  // more than one phase ahead.
+  uint32_t cur = 0xFFFFFFFFu;  // tile (relative) of the accumulated partial
+  for (uint32_t i = cw; i < n_items && ok; i += kMvConsumers) {
+    const uint32_t j = i / kStageSegs, slot = j % NST;
+    const uint32_t rel = i / NSEG;
+    if (rel != cur) {
+      if (cur != 0xFFFFFFFFu) flush(cur);
+      cur = rel;
+    }
+    if (!mbar_wait_bounded(&full[slot], (j / NST) & 1u)) {
+      set_error(err, kErrConsumerWait);
+      ok = false;
+      break;
+    }
+    const uint8_t *seg = ring + slot * STB + (i % kStageSegs) * SEGB;
+    const uint32_t ks0 = (i % NSEG) * kSegSteps;  // first K-step of the segment in the row
+    // Batches of 4 K-steps: all shared-memory loads first, then 4 independent
+    // MMAs, then the rescale, so their latencies overlap.
+#pragma unroll 2
+    for (uint32_t qb = 0; qb < kSegSteps; qb += 4) {
+      uint32_t b[2][4];
+      ldmatrix_x4(b[0], seg + qb * kStepBytes + lane * 16u);
+      ldmatrix_x4(b[1], seg + (qb + 2) * kStepBytes + lane * 16u);
+      uint32_t a0[4], a2[4];
+#pragma unroll
+      for (uint32_t q = 0; q < 4; ++q) {
+        const uint32_t kg = ks0 + qb + q;
+        a0[q] = 0;
+        a2[q] = 0;
+        if (arow) {
+          if constexpr (Q8) {
+            a0[q] = *reinterpret_cast<const uint32_t *>(aplane + kg * 32u + tq * 4u);
+            a2[q] = *reinterpret_cast<const uint32_t *>(aplane + kg * 32u + 16u + tq * 4u);
+          } else {
+            a0[q] = *reinterpret_cast<const uint32_t *>(aplane + (kg * 16u + tq * 2u) * 2u);
+            a2[q] = *reinterpret_cast<const uint32_t *>(aplane + (kg * 16u + 8u + tq * 2u) * 2u);
+          }
         }
-        mv_epilogue<M>(p, t * kTileRows + 2 * lane, a, bsum, pos);
       }
-      __syncwarp();
-      if (lane == 0) {
-        cnt[buf] = 0;
-        __threadfence_block();
-        *reinterpret_cast<volatile uint32_t *>(&gen[buf]) = want_gen + 1;
+      if constexpr (Q8) {
+        __half2 dp[4];
+        float sc[4];
+#pragma unroll
+        for (uint32_t q = 0; q < 4; ++q) {
+          dp[q] = *reinterpret_cast<const __half2 *>(seg + kSegQsBytes + ((qb + q) * kTileRows + 2u * tq) * 2u);
+          sc[q] = sx[ks0 + qb + q] * dscale;
+        }
+        int r[4][4];
+#pragma unroll
+        for (uint32_t q = 0; q < 4; ++q)
+          mma_s8(r[q], a0[q], a2[q], b[q >> 1][2 * (q & 1)], b[q >> 1][2 * (q & 1) + 1]);
+        if (arow) {
+#pragma unroll
+          for (uint32_t q = 0; q < 4; ++q) {
+            acc0 = fmaf((float)r[q][0], __low2float(dp[q]) * sc[q], acc0);
+            acc1 = fmaf((float)r[q][1], __high2float(dp[q]) * sc[q], acc1);
+          }
+        }
+      } else {
+#pragma unroll
+        for (uint32_t q = 0; q < 4; ++q)
+          mma_f16(cf[q], a0[q], a2[q], b[q >> 1][2 * (q & 1)], b[q >> 1][2 * (q & 1) + 1]);
       }
     }
-    if (!ok) break;
+    // release the segment's share of the stage
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[slot]);
+  }
+  if (ok && cur != 0xFFFFFFFFu) flush(cur);
+  named_bar(1, NCT);  // every partial written
+
+  // Tile reduction and epilogue: tile rel goes to warp rel % 8, lanes 0-3.
+  for (uint32_t rel = cw; rel < t1 - t0; rel += kMvConsumers) {
+    if (lane < 4) {
+      float a = 0.f, b = 0.f;
+#pragma unroll
+      for (int w = 0; w < kMvConsumers; ++w) {
+        a += red[(rel * kMvConsumers + w) * kTileRows + 2 * lane];
+        b += red[(rel * kMvConsumers + w) * kTileRows + 2 * lane + 1];
+      }
+      mv_epilogue<M>(p, (t0 + rel) * kTileRows + 2 * lane, a, b, pos);
+    }
   }
 }
 
@@ -596,19 +672,27 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
     set_error(p.ctrl + kCtrlErr, kErrConsumerWait);
   __syncthreads();
 
-  // scores: warp per position; lane holds DPL dims of K
+  // scores: warp per position; lane holds DPL dims of K; query heads in groups of 8
   for (uint32_t t = warp; t < len; t += nwarps) {
     float kf[DPL];
     const __half *kr = sK + t * D + lane * DPL;
 #pragma unroll
     for (int j = 0; j < DPL; ++j) kf[j] = __half2float(kr[j]);
-    for (uint32_t g0 = 0; g0 < G; ++g0) {
-      const float *qg = sQ + g0 * D + lane * DPL;
-      float s = 0.f;
+    for (uint32_t gb = 0; gb < G; gb += 8) {
+      float part[8];
 #pragma unroll
-      for (int j = 0; j < DPL; ++j) s = fmaf(qg[j], kf[j], s);
-      s = warp_sum(s);
-      if (lane == 0) sS[g0 * p.chunk_cap + t] = __fmul_rn(s, p.scale);
+      for (uint32_t i = 0; i < 8; ++i) {
+        float acc = 0.f;
+        if (gb + i < G) {
+          const float *qg = sQ + (gb + i) * D + lane * DPL;
+#pragma unroll
+          for (int j = 0; j < DPL; ++j) acc = fmaf(qg[j], kf[j], acc);
+        }
+        part[i] = acc;
+      }
+      const float tot = warp_sum8(part, lane);
+      const uint32_t gi = gb + ((lane >> 2) & 7u);
+      if ((lane & 3u) == 0 && gi < G) sS[gi * p.chunk_cap + t] = __fmul_rn(tot, p.scale);
     }
   }
   __syncthreads();
@@ -648,29 +732,31 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
   cluster_sync();
   const uint32_t rank = cluster_rank();
   const uint32_t ncl = p.nsplit / kAttnCluster, cl = split / kAttnCluster;
-  __shared__ float wts[kAttnCluster];
+  __shared__ float wts[32];
   __shared__ float stat[2];
   for (uint32_t g0 = rank; g0 < G; g0 += kAttnCluster) {
-    if (threadIdx.x == 0) {
-      float mj[kAttnCluster], M = -INFINITY;
-      for (uint32_t j = 0; j < kAttnCluster; ++j) {
-        mj[j] = ld_dsmem(&sM[g0], j);
-        M = fmaxf(M, mj[j]);
+    if (warp == 0) {
+      // lanes 0-7 read one peer each
+      const float mj = lane < kAttnCluster ? ld_dsmem(&sM[g0], lane) : -INFINITY;
+      const float lj = lane < kAttnCluster ? ld_dsmem(&sL[g0], lane) : 0.f;
+      const float M = warp_max(mj);
+      const float w = mj == -INFINITY ? 0.f : expf(mj - M);
+      const float Lsum = warp_sum(w * lj);
+      if (lane < kAttnCluster) wts[lane] = w;
+      if (lane == 0) {
+        stat[0] = M;
+        stat[1] = Lsum;
       }
-      float Lsum = 0.f;
-      for (uint32_t j = 0; j < kAttnCluster; ++j) {
-        const float w = mj[j] == -INFINITY ? 0.f : expf(mj[j] - M);
-        wts[j] = w;
-        Lsum += w * ld_dsmem(&sL[g0], j);
-      }
-      stat[0] = M;
-      stat[1] = Lsum;
     }
     __syncthreads();
     float *dst = p.part + (((size_t)kvh * ncl + cl) * G + g0) * (D + 2);
     for (uint32_t d = threadIdx.x; d < D; d += blockDim.x) {
+      float o[kAttnCluster];
+#pragma unroll
+      for (uint32_t j = 0; j < kAttnCluster; ++j) o[j] = ld_dsmem(&sO[g0 * D + d], j);
       float acc = 0.f;
-      for (uint32_t j = 0; j < kAttnCluster; ++j) acc = fmaf(wts[j], ld_dsmem(&sO[g0 * D + d], j), acc);
+#pragma unroll
+      for (uint32_t j = 0; j < kAttnCluster; ++j) acc = fmaf(wts[j], o[j], acc);
       dst[d] = acc;
     }
     if (threadIdx.x == 0) {
@@ -692,31 +778,42 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
       __threadfence();
       const float *pb = p.part + ((size_t)kvh * ncl * G + g0) * (D + 2);
       const size_t stride = (size_t)G * (D + 2);
-      if (threadIdx.x < 32) {
-        float M = -INFINITY;
-        for (uint32_t c = lane; c < ncl; c += 32) M = fmaxf(M, __ldcg(pb + c * stride + D));
-        M = warp_max(M);
-        float Lsum = 0.f;
-        for (uint32_t c = lane; c < ncl; c += 32) {
-          const float mc = __ldcg(pb + c * stride + D);
-          Lsum += (mc == -INFINITY ? 0.f : expf(mc - M)) * __ldcg(pb + c * stride + D + 1);
+      for (uint32_t c0 = 0; c0 < ncl; c0 += 32) {
+        // weights of up to 32 clusters per pass (ncl is small: nsplit / 8)
+        if (warp == 0) {
+          float M = stat[0];
+          if (c0 == 0) {
+            M = -INFINITY;
+            for (uint32_t c = lane; c < ncl; c += 32) M = fmaxf(M, __ldcg(pb + c * stride + D));
+            M = warp_max(M);
+          }
+          float Lpart = 0.f;
+          const uint32_t c = c0 + lane;
+          if (c < ncl) {
+            const float mc = __ldcg(pb + c * stride + D);
+            const float w = mc == -INFINITY ? 0.f : expf(mc - M);
+            wts[lane] = w;
+            Lpart = w * __ldcg(pb + c * stride + D + 1);
+          } else {
+            wts[lane] = 0.f;
+          }
+          Lpart = warp_sum(Lpart);
+          if (lane == 0) {
+            stat[0] = M;
+            stat[1] = c0 == 0 ? Lpart : stat[1] + Lpart;
+          }
         }
-        Lsum = warp_sum(Lsum);
-        if (lane == 0) {
-          stat[0] = M;
-          stat[1] = 1.0f / Lsum;
+        __syncthreads();
+        const uint32_t nc = min(32u, ncl - c0);
+        for (uint32_t d = threadIdx.x; d < D; d += blockDim.x) {
+          float acc = c0 == 0 ? 0.f : p.out[((size_t)kvh * G + g0) * D + d];
+          for (uint32_t c = 0; c < nc; ++c) acc = fmaf(wts[c], __ldcg(pb + (c0 + c) * stride + d), acc);
+          p.out[((size_t)kvh * G + g0) * D + d] = acc;
         }
+        __syncthreads();
       }
-      __syncthreads();
-      for (uint32_t d = threadIdx.x; d < D; d += blockDim.x) {
-        float acc = 0.f;
-        for (uint32_t c = 0; c < ncl; ++c) {
-          const float mc = __ldcg(pb + c * stride + D);
-          const float w = mc == -INFINITY ? 0.f : expf(mc - stat[0]);
-          acc = fmaf(w, __ldcg(pb + c * stride + d), acc);
-        }
-        p.out[((size_t)kvh * G + g0) * D + d] = acc * stat[1];
-      }
+      const float invL = 1.0f / stat[1];
+      for (uint32_t d = threadIdx.x; d < D; d += blockDim.x) p.out[((size_t)kvh * G + g0) * D + d] *= invL;
       if (threadIdx.x == 0) p.tickets[kvh * G + g0] = 0;
     }
     __syncthreads();

@@ -15,8 +15,7 @@ constexpr uint32_t kWaitMaxIters = 1u << 26;
 
 // Device error flag bits (ctrl[kCtrlErr]).
 enum : uint32_t {
-  kErrConsumerWait = 1u,   // a consumer gave up waiting for a filled ring slot
-  kErrProducerWait = 2u,   // the producer gave up waiting for a free ring slot
+  kErrConsumerWait = 1u,   // a warp gave up waiting for its bulk copy or a peer warp
   kErrDrainWait = 4u,      // bulk copies still in flight at kernel exit
   kErrBadToken = 8u,       // token id outside the vocabulary
   kErrPosition = 16u,      // position outside the KV cache
@@ -96,28 +95,6 @@ __device__ __forceinline__ void prefetch_l2(const void *p) {
 // Named barrier over `threads` threads (a multiple of 32), id 1..15.
 __device__ __forceinline__ void named_bar(uint32_t id, uint32_t threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
-}
-
-__device__ __forceinline__ uint4 ld_shared_v4(const void *p) {
-  uint4 v;
-  asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
-               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-               : "r"(smem_u32(p)));
-  return v;
-}
-
-__device__ __forceinline__ float4 ld_shared_f4(const void *p) {
-  float4 v;
-  asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(smem_u32(p)));
-  return v;
-}
-
-__device__ __forceinline__ uint2 ld_nc_v2(const void *p) {
-  uint2 v;
-  asm volatile("ld.global.nc.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "l"(p));
-  return v;
 }
 
 __device__ __forceinline__ void set_error(uint32_t *flag, uint32_t bits) {
