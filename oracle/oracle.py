@@ -259,6 +259,15 @@ def swiglu(dtype: int, rg: np.ndarray, ru: np.ndarray, rows: int, cols: int, x: 
     return y
 
 
+def rope(q: np.ndarray, k: np.ndarray, ext: np.ndarray, position: int, heads: int, kv_heads: int,
+         head_dim: int, theta: float, scaling: float):
+    """rope.comp:22-51 on copies of q and k."""
+    q, k = np.array(q, np.float32), np.array(k, np.float32)
+    lib().vgo_rope(fptr(q), fptr(k), fptr(np.ascontiguousarray(ext, np.float32)), position, heads,
+                   kv_heads, head_dim, theta, scaling)
+    return q, k
+
+
 def attention(q: np.ndarray, k_cache: np.ndarray, v_cache: np.ndarray, heads: int,
               kv_heads: int, head_dim: int, position: int):
     """One layer; caches are [ctx][kv_dim] fp16 bits (reference layout)."""

@@ -1,0 +1,66 @@
+// glsl_shim.h — the GLSL built-ins that VoxGen's BaseLM compute shaders use,
+// as C++, so the shader bodies compile unchanged with g++ and run on the CPU.
+//
+// TEST INFRASTRUCTURE ONLY (the parity pin of the oracle): nothing in the
+// product links this.
+//
+// Semantics follow the GLSL 4.60 specification: 32-bit uint/int/float,
+// unpackHalf2x16 (low half in .x), packHalf2x16 (round to nearest even, the
+// conversion the oracle and the CUDA path use), inversesqrt as 1/sqrt.
+// Translation units that include this header must not include <cmath> or
+// <math.h>: the unqualified exp/pow/cos/sin/max/min calls of a shader have to
+// resolve to the float overloads below.
+//
+// Workgroup model: every invocation of a workgroup is a fiber on one host
+// thread; barrier() switches to the next fiber, and `shared` variables are
+// thread-local, so one workgroup's invocations share them. Host threads run
+// different workgroups of a dispatch in parallel.
+#pragma once
+
+#include "workgroup.h"
+
+struct vec2 {
+  float x, y;
+  vec2() = default;
+  vec2(float a, float b) : x(a), y(b) {}
+};
+
+extern "C" {
+float expf(float);
+float powf(float, float);
+float cosf(float);
+float sinf(float);
+float sqrtf(float);
+}
+
+inline float exp(float x) { return expf(x); }
+inline float pow(float x, float y) { return powf(x, y); }
+inline float cos(float x) { return cosf(x); }
+inline float sin(float x) { return sinf(x); }
+inline float inversesqrt(float x) { return 1.0f / sqrtf(x); }
+inline float max(float a, float b) { return a < b ? b : a; }
+inline float min(float a, float b) { return b < a ? b : a; }
+inline uint max(uint a, uint b) { return a < b ? b : a; }
+inline uint min(uint a, uint b) { return b < a ? b : a; }
+
+inline float uintBitsToFloat(uint u) {
+  float f;
+  __builtin_memcpy(&f, &u, 4);
+  return f;
+}
+inline uint floatBitsToUint(float f) {
+  uint u;
+  __builtin_memcpy(&u, &f, 4);
+  return u;
+}
+
+inline vec2 unpackHalf2x16(uint v) {
+  return vec2(vgref::half_to_float(v & 0xFFFFu), vgref::half_to_float(v >> 16));
+}
+inline uint packHalf2x16(vec2 v) { return vgref::float_to_half(v.x) | (vgref::float_to_half(v.y) << 16); }
+inline void barrier() { vgref::barrier(); }
+
+#define gl_LocalInvocationID (::vgref::local_id())
+#define gl_WorkGroupID (::vgref::group_id())
+#define gl_NumWorkGroups (::vgref::num_groups())
+#define shared static thread_local

@@ -10,10 +10,8 @@
  * fp32 throughout, mul and add kept separate (built with -ffp-contract=off).
  * Citations are file:line inside the VoxGen project.
  *
- * Parity status: the reference cannot run here (Rust host, Vulkan GLSL
- * shaders, no cargo/glslc/Vulkan). This restatement is pinned against the
- * reference's own known-answer tests and, when oracle/_ref has been built
- * from the reference shader sources, against that build's golden vectors.
+ * Parity status: pinned bit for bit against the reference's own shader code
+ * (compiled as C++ by oracle/ref_shim) and its known-answer tests.
  */
 #include "voxgen_oracle.h"
 

@@ -7,11 +7,14 @@
  * CPU baseline. Only tests/, __graft_entry__.smoke() and bench.py's CPU legs
  * may load it; the product library never links or calls it.
  *
- * Parity pinning: the reference (Rust + Vulkan GLSL) cannot be built or run in
- * this environment (no cargo, no glslc, no Vulkan). The restatement is pinned
- * against the reference's own known-answer tests (src/baselm.rs:1315-1358,
- * src/gguf.rs:41-45) and, where available, against golden vectors produced by
- * executing the reference shader sources compiled as C++ (oracle/_ref).
+ * Parity pinning: the reference's Rust host cannot be built here (no cargo)
+ * and its shaders cannot run on Vulkan (no glslc, no Vulkan stack). Its GLSL
+ * compute shaders are instead compiled as C++ and run on the CPU by
+ * oracle/ref_shim (workgroups emulated with fibers); this restatement matches
+ * that build bit for bit, shader by shader and over whole decode steps, on
+ * head_dim 128 models (tests/test_cpu_ref_pin.py, with committed golden
+ * vectors in tests/golden/). It also matches the reference's known-answer
+ * tests (src/baselm.rs:1315-1358, src/gguf.rs:41-45).
  */
 #ifndef VOXGEN_ORACLE_H
 #define VOXGEN_ORACLE_H

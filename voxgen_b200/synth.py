@@ -68,6 +68,11 @@ PRESETS: Dict[str, ModelSpec] = {
     # small shapes for parity tests (odd row counts, several layers, GQA ratio 4)
     "tiny": ModelSpec("tiny", 2, 256, 8, 2, 32, 608, 512, GGML_Q8_0, seed=11),
     "tiny_f16": ModelSpec("tiny_f16", 2, 256, 8, 2, 32, 608, 512, GGML_F16, seed=12),
+    # head_dim 128, the only head size the reference's attn_scores shader reduces correctly
+    # (its workgroup is 128 invocations wide): the models the reference shaders are run on
+    "pin": ModelSpec("pin", 2, 256, 2, 1, 128, 512, 96, GGML_Q8_0, seed=31),
+    "pin_f16": ModelSpec("pin_f16", 2, 256, 2, 1, 128, 512, 96, GGML_F16, seed=32, tied_output=False,
+                         embedding_scale=12.0, residual_scale=0.25, logit_scale=0.125),
 }
 
 # Runtime inputs per config (BASELINE.json configs and the survey's measurement plan).
