@@ -13,9 +13,10 @@ with CUDA events on the engine's stream, max over ranks. `e2e` is the same metri
 C ABI with host buffers: every step copies its token from pinned host memory and reads the
 output hidden state back to the host.
 
-`--impl reference` times the reference's CPU path: the C restatement of the reference shaders
-(oracle/) on all host cores, on the same workload. The reference itself (Rust + Vulkan GLSL)
-cannot be built or run here.
+`--impl reference` times the reference's CPU path on all host cores, on the same workload: the
+reference's own BaseLM shaders compiled as C++ (oracle/_ref) where that library was built, else
+the C restatement of the shaders (oracle/). The reference's Rust host and its Vulkan path cannot
+be built or run here.
 """
 from __future__ import annotations
 
@@ -129,43 +130,53 @@ def algorithmic_bytes(info, positions):
 
 
 def run_reference(args, rank, world):
-    """CPU path of the reference (oracle port) on this host's cores."""
+    """The reference's own CPU path on this host's cores, rank 0 only: its BaseLM shaders compiled
+    as C++ (oracle/_ref, run under a workgroup emulator, the stand-in for the lavapipe run the
+    reference would use) when that library was built, else the oracle port."""
     if rank != 0:
         return
     from oracle import oracle as O
+    from oracle import ref as R
     from voxgen_b200 import synth
     wl = WORKLOADS[args.workload]
     spec = synth.preset(wl["preset"])
     path = synth.model_path(spec, model_cache())
-    m = O.OracleModel(path)
-    st = O.OracleState(m, wl["ctx"])
+    shaders = R.LIB.exists()
+    if shaders:
+        eng = R.RefEngine(path, wl["ctx"])
+        kind, what = "reference", "the reference's BaseLM GLSL shaders compiled as C++, workgroups emulated"
+        budget, min_steps = float(os.environ.get("VOXGEN_REF_SECONDS", "45")), 2
+    else:
+        m = O.OracleModel(path)
+        eng = O.OracleState(m, wl["ctx"])
+        kind, what = "port", "C restatement of the reference shaders"
+        budget, min_steps = float(os.environ.get("VOXGEN_REF_SECONDS", "120")), 3
     k, v = synth.kv_prefill(spec, wl["prefill"])
     toks = synth.token_ids(spec, args.warmup + args.steps)
     cores = O.threads()
-    # each bench step is one decode token; the run is bounded so that K+W steps end in minutes
-    budget = float(os.environ.get("VOXGEN_REF_SECONDS", "120"))
-    st.write_kv(k, v)
-    for t in toks[: min(args.warmup, 3)]:
-        st.decode_token(int(t))
-    st.write_kv(k, v)
+    # each bench step is one decode token; the run is bounded so that it ends in minutes
+    warm = 1 if shaders else min(args.warmup, 3)
+    eng.write_kv(k, v)
+    for t in toks[:warm]:
+        eng.decode_token(int(t))
+    eng.write_kv(k, v)
     t0 = time.perf_counter()
     n = 0
     for t in toks[: args.steps]:
-        st.decode_token(int(t))
+        eng.decode_token(int(t))
         n += 1
-        if time.perf_counter() - t0 > budget:
+        if n >= min_steps and time.perf_counter() - t0 > budget:
             break
     el = time.perf_counter() - t0
     val = n / el
     line = {
         "metric": "decode tok/s", "value": val, "unit": "tok/s", "n_gpus": world, "steps": n,
-        "warmup": min(args.warmup, 3), "ms_per_step": 1000 * el / n, "higher_is_better": True,
+        "warmup": warm, "ms_per_step": 1000 * el / n, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic", "impl": "reference",
         "config": {"workload": f"{args.workload}: {wl['desc']}", "positions": [wl["prefill"], wl["prefill"] + n - 1],
                    "streams_per_gpu": 1, "parallelism": "cpu"},
-        "cpu_baseline": {"value": val, "unit": "tok/s", "cores": cores, "kind": "port",
-                         "sample": f"{n} decode steps from position {wl['prefill']} (C restatement of the "
-                                   f"reference shaders, OpenMP, {cores} threads)"},
+        "cpu_baseline": {"value": val, "unit": "tok/s", "cores": cores, "kind": kind,
+                         "sample": f"{n} decode steps from position {wl['prefill']} ({what}, {cores} threads)"},
         "e2e": {"value": val, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
