@@ -252,6 +252,34 @@ int vg_k_attention(const float *q, const uint16_t *k_cache,
                    uint32_t head_dim, uint32_t ctx, uint32_t position,
                    float *out, void *cuda_stream);
 
+/* The same attention with its scratch in a fixed device buffer that lives in
+ * the library (no reference counterpart: the reference records attention into
+ * a command buffer whose scratch belongs to the session). It makes no device
+ * allocation and frees nothing, for callers that must not allocate: a
+ * streaming thread that may not wait on the allocator (cudaMallocAsync can
+ * grow and map its pool with unbounded latency), or a process that has handed
+ * all free HBM to weights and KV caches, where vg_k_attention's temporary
+ * allocation could fail with VG_ENOMEM in the middle of a stream.
+ *
+ * Scratch: VG_K_ATTENTION_NOALLOC_TICKET_BYTES of merge counters, cleared on
+ * every call with cudaMemsetAsync, plus at most
+ * VG_K_ATTENTION_NOALLOC_PARTIAL_BYTES of per-cluster partial results, i.e.
+ *   kv_heads * ceil(ceil(ctx / 64) / 8) * (heads / kv_heads) * (head_dim + 2) * 4
+ * bytes (16 heads of 128 fit a context of 64,512 positions). A larger shape,
+ * or more than 1024 heads, returns VG_ERANGE before anything is enqueued.
+ * The first call on a device looks the buffer's address up with
+ * cudaGetSymbolAddress, which may load the library's device code: make that
+ * first call outside any stream capture. There is one buffer per device, so
+ * calls on one device must not overlap: calls on different streams or host
+ * threads that can run at the same time race on the scratch and give wrong
+ * results. Order them on one stream or synchronise between them. */
+#define VG_K_ATTENTION_NOALLOC_TICKET_BYTES 4096u
+#define VG_K_ATTENTION_NOALLOC_PARTIAL_BYTES (1u << 20)
+int vg_k_attention_noalloc(const float *q, const uint16_t *k_cache,
+                           const uint16_t *v_cache, uint32_t heads,
+                           uint32_t kv_heads, uint32_t head_dim, uint32_t ctx,
+                           uint32_t position, float *out, void *cuda_stream);
+
 #ifdef __cplusplus
 }
 #endif

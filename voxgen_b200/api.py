@@ -36,7 +36,7 @@ EXPORTS = [
     "vg_decode_embedding_device", "vg_prefill_tokens", "vg_stream_output", "vg_stream_logits",
     "vg_copy_output", "vg_copy_logits", "vg_stream_sync", "vg_step_result_get", "vg_benchmark",
     "vg_stream_profile_step", "vg_decode_batch", "vg_k_packed_bytes", "vg_k_repack", "vg_k_matvec", "vg_k_embedding",
-    "vg_k_residual_rmsnorm", "vg_k_attention",
+    "vg_k_residual_rmsnorm", "vg_k_attention", "vg_k_attention_noalloc",
 ]
 
 
@@ -124,6 +124,7 @@ def lib() -> C.CDLL:
         "vg_k_embedding": ([I, P, U32, U32, U32, F, P, P], I),
         "vg_k_residual_rmsnorm": ([P, P, P, U32, F, F, P, P], I),
         "vg_k_attention": ([P, P, P, U32, U32, U32, U32, U32, P, P], I),
+        "vg_k_attention_noalloc": ([P, P, P, U32, U32, U32, U32, U32, P, P], I),
     }
     for name, (args, res) in sig.items():
         f = getattr(L, name)

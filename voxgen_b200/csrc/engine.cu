@@ -1203,6 +1203,26 @@ static uint32_t *kernel_ctrl() {
   return p;
 }
 
+// Scratch of vg_k_attention_noalloc: merge tickets, then per-cluster partials.
+// A file-scope device array, zero when the module loads; its address is looked
+// up once per device and cached.
+constexpr uint32_t kNoAllocScratchBytes = VG_K_ATTENTION_NOALLOC_TICKET_BYTES + VG_K_ATTENTION_NOALLOC_PARTIAL_BYTES;
+static __device__ __align__(256) uint8_t g_noalloc_scratch[kNoAllocScratchBytes];
+
+static uint8_t *noalloc_scratch(int dev) {
+  constexpr int kMaxDevices = 64;
+  static std::mutex mu;
+  static uint8_t *addr[kMaxDevices] = {};
+  if (dev < 0 || dev >= kMaxDevices) fail(VG_EDEVICE, strf("device %d out of range", dev));
+  std::lock_guard<std::mutex> lk(mu);
+  if (!addr[dev]) {
+    void *a = nullptr;
+    CK(cudaGetSymbolAddress(&a, g_noalloc_scratch));
+    addr[dev] = (uint8_t *)a;
+  }
+  return addr[dev];
+}
+
 static int kguard(const std::function<void()> &f) {
   try {
     f();
@@ -1318,6 +1338,44 @@ int vg_k_attention(const float *q, const uint16_t *k_cache, const uint16_t *v_ca
     cudaError_t e2 = cudaFreeAsync(scratch, st);
     CK(e);
     CK(e2);
+  });
+}
+
+int vg_k_attention_noalloc(const float *q, const uint16_t *k_cache, const uint16_t *v_cache, uint32_t heads,
+                           uint32_t kv_heads, uint32_t head_dim, uint32_t ctx, uint32_t position, float *out,
+                           void *cuda_stream) {
+  if (!q || !k_cache || !v_cache || !out || !heads || !kv_heads || heads % kv_heads || position >= ctx)
+    return VG_EINVAL;
+  if (head_dim != 32 && head_dim != 64 && head_dim != 128 && head_dim != 256) return VG_EUNSUPPORTED;
+  const uint32_t G = heads / kv_heads;
+  AttnParams ap{};
+  plan_attention(ctx, ap.nsplit, ap.chunk_cap);
+  const uint64_t part_bytes = (uint64_t)kv_heads * (ap.nsplit / kAttnCluster) * G * (head_dim + 2) * 4;
+  if (part_bytes > VG_K_ATTENTION_NOALLOC_PARTIAL_BYTES || (uint64_t)heads * 4 > VG_K_ATTENTION_NOALLOC_TICKET_BYTES)
+    return VG_ERANGE;
+  return kguard([&] {
+    cudaStream_t st = (cudaStream_t)cuda_stream;
+    int dev = 0;
+    CK(cudaGetDevice(&dev));
+    uint8_t *scratch = noalloc_scratch(dev);
+    uint32_t *tickets = (uint32_t *)scratch;
+    CK(cudaMemsetAsync(tickets, 0, (size_t)heads * 4, st));
+    ap.q = q;
+    ap.kc = (const __half *)k_cache;
+    ap.vc = (const __half *)v_cache;
+    ap.out = out;
+    ap.part = (float *)(scratch + VG_K_ATTENTION_NOALLOC_TICKET_BYTES);
+    ap.tickets = tickets;
+    ap.heads = heads;
+    ap.kv_heads = kv_heads;
+    ap.ctx = ctx;
+    ap.scale = 1.0f / sqrtf((float)head_dim);
+    ap.fixed_pos = position;
+    ap.ctrl = nullptr;
+    const AttnFn fn = pick_attention(head_dim);
+    const uint32_t smem = attention_smem_bytes(G, head_dim, ap.chunk_cap);
+    ensure_smem((const void *)fn, dev, smem);
+    CK(launch_ex(fn, dim3(ap.nsplit, kv_heads), dim3(kAttnThreads), smem, st, false, kAttnCluster, ap));
   });
 }
 
