@@ -55,23 +55,26 @@ def test_matvec(dtype, rows, cols):
 
 
 def tile_offsets(rows, cols, q8):
-    """Byte offsets of the segmented 8-row tile layout (mirror of TileGeom in kernels.cuh)."""
+    """Byte offsets of the segmented 16-row tile layout (mirror of TileGeom in kernels.cuh): a
+    K-step of 16 rows x 32 bytes is four 8x16-byte matrices [rows 0-7 | rows 8-15] x [bytes 0-15 |
+    bytes 16-31]; 8 K-steps and then (Q8_0) their scales [K-step][row % 8][row / 8] per segment."""
     step = 32 if q8 else 16
-    seg_cols = 16 * step
+    seg_cols = 8 * step
     nseg = -(-cols // seg_cols)
     seg_bytes = 4096 + (256 if q8 else 0)
     r = np.arange(rows)[:, None]
     k = np.arange(cols)[None, :]
     seg, kk = k // seg_cols, k % seg_cols
     kb = (kk % step) * (1 if q8 else 2)
-    base = ((r // 8) * nseg + seg) * seg_bytes
-    elem = base + (kk // step) * 256 + (kb >> 4) * 128 + (r % 8) * 16 + (kb & 15)
+    tr = r % 16
+    base = ((r // 16) * nseg + seg) * seg_bytes
+    elem = base + (kk // step) * 512 + ((kb >> 4) * 2 + (tr >> 3)) * 128 + (tr & 7) * 16 + (kb & 15)
     b = np.arange(cols // 32)[None, :]
-    scale = ((r // 8) * nseg + b // 16) * seg_bytes + 4096 + ((b % 16) * 8 + r % 8) * 2
-    return elem, scale, (-(-rows // 8)) * nseg * seg_bytes
+    scale = ((r // 16) * nseg + b // 8) * seg_bytes + 4096 + (b % 8) * 32 + (tr & 7) * 4 + (tr >> 3) * 2
+    return elem, scale, (-(-rows // 16)) * nseg * seg_bytes
 
 
-@pytest.mark.parametrize("dtype,rows,cols", [(Q8, 6, 64), (Q8, 17, 544), (F16, 9, 272)])
+@pytest.mark.parametrize("dtype,rows,cols", [(Q8, 6, 64), (Q8, 17, 544), (Q8, 40, 1024), (F16, 9, 272), (F16, 33, 640)])
 def test_repack_layout(dtype, rows, cols):
     rng = np.random.default_rng(1)
     raw = make_matrix(rng, dtype, rows, cols)

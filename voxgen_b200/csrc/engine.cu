@@ -206,9 +206,7 @@ MvPlan plan_matvec(const DevMat &m, int device, uint32_t sms) {
   const uint32_t per_stage = kStageSegs * g.seg_bytes() + 16u;
   const uint32_t fixed = probe.total - per_stage;
   const uint32_t fit = kSmemBudget > fixed ? (kSmemBudget - fixed) / per_stage : 1u;
-  // An even number of stages keeps each stage slot with one warp group (see the kernel).
-  uint32_t st = std::min<uint32_t>({fit, 8u, std::max<uint32_t>(2u, n_st + (n_st & 1u))});
-  st &= ~1u;
+  const uint32_t st = std::min<uint32_t>({fit, 8u, std::max<uint32_t>(2u, n_st)});
   if (st < 2) fail(VG_EUNSUPPORTED, strf("matrix of %u columns does not fit two pipeline stages", g.cols));
   p.stages = st;
   const uint32_t smem = MvSmem(p).total;
@@ -404,8 +402,8 @@ void load_model(vg_model *m, const std::string &path, uint32_t requested) {
     CK(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
     CK(cudaMalloc(&staging, max_raw));
     // row0: first packed row of this tensor inside dst (a multiple of the tile height)
-    auto repack = [&](const std::string &name, const DevMat &dst, uint32_t row0, uint32_t stride, uint32_t offset,
-                      uint32_t pair_group) {
+    auto repack = [&](const std::string &name, const DevMat &dst, uint32_t row0, uint32_t perm, uint32_t group,
+                      uint32_t half) {
       const TensorInfo &t = tensor(name);
       CK(cudaMemcpyAsync(staging, data + t.offset, t.bytes, cudaMemcpyHostToDevice, st));
       const uint32_t rows = (uint32_t)t.dims[1];
@@ -413,7 +411,7 @@ void load_model(vg_model *m, const std::string &path, uint32_t requested) {
       TileGeom sub = dst.g;  // the tensor's rows as their own tiled matrix inside dst
       sub.rows = dst.g.rows - row0;
       repack_kernel<<<std::min<uint32_t>(rows, 65535u), 256, 0, st>>>(
-          staging, rows, sub, dst.w + dst.g.seg_base(row0, 0), stride, offset, pair_group);
+          staging, rows, sub, dst.w + dst.g.seg_base(row0, 0), perm, group, half);
       CK(cudaGetLastError());
       CK(cudaStreamSynchronize(st));
     };
@@ -424,18 +422,18 @@ void load_model(vg_model *m, const std::string &path, uint32_t requested) {
     for (uint32_t l = 0; l < c.block_count; ++l) {
       Layer &L = m->layers[l];
       auto nm = [&](const char *s) { return strf("blk.%u.%s.weight", l, s); };
-      repack(nm("attn_q"), L.qkv, 0, 1, 0, c.head_dim);
-      repack(nm("attn_k"), L.qkv, H, 1, 0, c.head_dim);
-      repack(nm("attn_v"), L.qkv, H + KV, 1, 0, 0);
-      repack(nm("attn_output"), L.o, 0, 1, 0, 0);
-      repack(nm("ffn_gate"), L.gateup, 0, 2, 0, 0);
-      repack(nm("ffn_up"), L.gateup, 0, 2, 1, 0);
-      repack(nm("ffn_down"), L.down, 0, 1, 0, 0);
+      repack(nm("attn_q"), L.qkv, 0, kPermRope, c.head_dim, 0);
+      repack(nm("attn_k"), L.qkv, H, kPermRope, c.head_dim, 0);
+      repack(nm("attn_v"), L.qkv, H + KV, kPermIdentity, 0, 0);
+      repack(nm("attn_output"), L.o, 0, kPermIdentity, 0, 0);
+      repack(nm("ffn_gate"), L.gateup, 0, kPermHalves, 0, 0);
+      repack(nm("ffn_up"), L.gateup, 0, kPermHalves, 0, 1);
+      repack(nm("ffn_down"), L.down, 0, kPermIdentity, 0, 0);
       upload_vec(nm("attn_norm"), L.attn_norm);
       upload_vec(nm("ffn_norm"), L.ffn_norm);
     }
-    repack("token_embd.weight", m->tok, 0, 1, 0, 0);
-    if (!c.tied_output) repack("output.weight", m->out, 0, 1, 0, 0);
+    repack("token_embd.weight", m->tok, 0, kPermIdentity, 0, 0);
+    if (!c.tied_output) repack("output.weight", m->out, 0, kPermIdentity, 0, 0);
     upload_vec("output_norm.weight", m->out_norm);
     // RoPE tables: inv_freq as rope.comp:29-30 computes it, evaluated once on
     // the host; ext = the factor set record_transformer picks (baselm.rs:902-913).
@@ -1250,7 +1248,7 @@ int vg_k_repack(int dtype, const void *gguf_bytes, uint32_t rows, uint32_t cols,
     CK(cudaMemsetAsync(packed, 0, b, st));
     const TileGeom g{rows, cols, dtype == VG_FORMAT_Q8_0 ? 1u : 0u};
     repack_kernel<<<std::min<uint32_t>(rows, 65535u), 256, 0, st>>>((const uint8_t *)gguf_bytes, rows, g,
-                                                                     (uint8_t *)packed, 1, 0, 0);
+                                                                     (uint8_t *)packed, kPermIdentity, 0, 0);
     CK(cudaGetLastError());
   });
 }

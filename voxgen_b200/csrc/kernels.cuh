@@ -35,13 +35,14 @@ enum class Pro { COPY, RMSNORM };
 
 constexpr int kMvConsumers = 8;                       // consumer warps per matvec CTA
 constexpr int kMvThreads = 32 * (kMvConsumers + 1);   // + one producer warp
-constexpr uint32_t kTileRows = 8;
-constexpr uint32_t kSegSteps = 16;                    // K-steps per segment
-constexpr uint32_t kStepBytes = 256;                  // 8 rows x 32 bytes
+constexpr uint32_t kTileRows = 16;                     // rows of a tile = M of one MMA
+constexpr uint32_t kSegSteps = 8;                      // K-steps per segment
+constexpr uint32_t kStepBytes = 512;                   // 16 rows x 32 bytes
 constexpr uint32_t kSegQsBytes = kSegSteps * kStepBytes;
 constexpr uint32_t kStageSegs = 4;                    // segments per pipeline stage (one bulk copy)
 constexpr uint32_t kChunkSteps = kStageSegs * kSegSteps / 8;  // K-steps per consumer warp per stage
-static_assert(kChunkSteps == 8, "a stage holds one 8 K-step chunk per consumer warp");
+static_assert(kChunkSteps == 4 && kSegSteps % kChunkSteps == 0,
+              "each consumer warp takes one batch of 4 K-steps of one segment per stage");
 
 // Slots of the per-stream device control block.
 constexpr uint32_t kCtrlPos = 0;    // decode position of the step being run
@@ -49,6 +50,15 @@ constexpr uint32_t kCtrlToken = 1;  // token id of a token step
 constexpr uint32_t kCtrlErr = 2;    // error flag bits (ptx.cuh)
 constexpr uint32_t kCtrlWords = 16;
 
+// Segmented 16-row tiles. A K-step is 32 columns of Q8_0 quants or 16 columns
+// of fp16 values of the tile's 16 rows: 512 bytes stored as four 8x16-byte
+// matrices [rows 0-7, bytes 0-15][rows 8-15, bytes 0-15][rows 0-7, bytes
+// 16-31][rows 8-15, bytes 16-31], which is the order ldmatrix.x4 delivers the
+// A fragment of mma m16n8k32 (s8) / m16n8k16 (f16) in. A segment is kSegSteps
+// K-steps, followed for Q8_0 by their fp16 block scales laid [K-step][row % 8]
+// [row / 8] (rows r and r+8 adjacent). A tile is its segments back to back and
+// the tiles of a matrix follow each other, so a run of tiles is one contiguous
+// byte range. Padding rows and columns are zero.
 struct TileGeom {
   uint32_t rows, cols, q8;
   __host__ __device__ uint32_t step_cols() const { return q8 ? 32u : 16u; }
@@ -64,11 +74,13 @@ struct TileGeom {
   __host__ __device__ uint64_t elem_off(uint32_t r, uint32_t k) const {
     const uint32_t sc = seg_cols(), seg = k / sc, kk = k % sc;
     const uint32_t st = kk / step_cols(), kb = (kk % step_cols()) * (q8 ? 1u : 2u);
-    return seg_base(r, seg) + st * kStepBytes + (kb >> 4) * 128u + (r % kTileRows) * 16u + (kb & 15u);
+    const uint32_t tr = r % kTileRows;
+    return seg_base(r, seg) + st * kStepBytes + ((kb >> 4) * 2u + (tr >> 3)) * 128u + (tr & 7u) * 16u + (kb & 15u);
   }
   // byte offset of the fp16 scale of Q8_0 block b of row r
   __host__ __device__ uint64_t scale_off(uint32_t r, uint32_t b) const {
-    return seg_base(r, b / kSegSteps) + kSegQsBytes + ((b % kSegSteps) * kTileRows + (r % kTileRows)) * 2u;
+    const uint32_t tr = r % kTileRows;
+    return seg_base(r, b / kSegSteps) + kSegQsBytes + (b % kSegSteps) * 32u + (tr & 7u) * 4u + (tr >> 3) * 2u;
   }
 };
 
@@ -161,22 +173,21 @@ __device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], const void *p) {
                : "r"(smem_u32(p)));
 }
 
-// D = A(16x32 s8, row) * B(32x8 s8, col); rows 8-15 of A are zero.
-__device__ __forceinline__ void mma_s8(int (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+// D = A(16x32 s8, row) * B(32x8 s8, col), A fragment as ldmatrix.x4 delivers it.
+__device__ __forceinline__ void mma_s8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
   asm(
       "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
       "{%10, %11, %12, %13};"
       : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
-      : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1), "r"(0), "r"(0), "r"(0), "r"(0));
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0), "r"(0), "r"(0), "r"(0));
 }
 
-// C += A(16x16 f16, row) * B(16x8 f16, col) in fp32; rows 8-15 of A are zero.
-__device__ __forceinline__ void mma_f16(float (&c)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
-  asm(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+// C += A(16x16 f16, row) * B(16x8 f16, col) in fp32.
+__device__ __forceinline__ void mma_f16(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
       "{%0, %1, %2, %3};"
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a0), "r"(0u), "r"(a2), "r"(0u), "r"(b0), "r"(b1));
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
 // RoPE of one (a, b) pair, rope.comp:28-49 with inv_freq precomputed on the host.
@@ -203,39 +214,46 @@ __device__ __forceinline__ bool block_exponent(uint32_t mbits, int &e) {
 }
 __device__ __forceinline__ float pow2f(int e) { return __uint_as_float((uint32_t)(127 + e) << 23); }
 
-// Epilogue of one pair of adjacent packed rows (R even for pair modes).
+// Epilogue of packed rows R and R + 8 of one tile (R = 16t + l, l < 8). The
+// pair modes store the two halves of a pair there: SWIGLU gate row 8t + l and
+// up row 8t + l; QKV (Q and K) RoPE elements i and i + d/2 of one head.
 template <Mode M>
 __device__ __forceinline__ void mv_epilogue(const MvParams &p, uint32_t R, float a, float b, uint32_t pos) {
+  const uint32_t R2 = R + 8u;
   if constexpr (M == Mode::PLAIN) {
     if (R < p.g.rows) p.out[R] = __fmul_rn(a, p.alpha);  // matvec.comp:61
-    if (R + 1 < p.g.rows) p.out[R + 1] = __fmul_rn(b, p.alpha);
+    if (R2 < p.g.rows) p.out[R2] = __fmul_rn(b, p.alpha);
   } else if constexpr (M == Mode::RESID) {
     // residual_rmsnorm.comp:27, hidden + branch * scale, with branch = this row's product
     if (R < p.g.rows) p.out[R] = __fadd_rn(p.resid[R], __fmul_rn(a, p.alpha));
-    if (R + 1 < p.g.rows) p.out[R + 1] = __fadd_rn(p.resid[R + 1], __fmul_rn(b, p.alpha));
+    if (R2 < p.g.rows) p.out[R2] = __fadd_rn(p.resid[R2], __fmul_rn(b, p.alpha));
   } else if constexpr (M == Mode::SWIGLU) {
-    if (R < p.g.rows) p.out[R >> 1] = __fmul_rn(__fdiv_rn(a, __fadd_rn(1.0f, expf(-a))), b);  // matvec_swiglu.comp:67
+    const uint32_t o = (R / kTileRows) * 8u + (R % kTileRows);
+    if (2u * o < p.g.rows) p.out[o] = __fmul_rn(__fdiv_rn(a, __fadd_rn(1.0f, expf(-a))), b);  // matvec_swiglu.comp:67
   } else {
     if (R >= p.g.rows) return;
     const uint32_t hd = p.head_dim, half_d = hd >> 1;
     if (pos >= p.ctx) {
       set_error(p.ctrl + kCtrlErr, kErrPosition);
-    } else if (R < p.q_rows) {
-      const uint32_t pi = R >> 1, head = pi / half_d, i = pi % half_d;
-      rope_pair(a, b, pos, i, p.inv_freq, p.ext, p.rope_scaling);
-      p.out[head * hd + i] = a;
-      p.out[head * hd + i + half_d] = b;
     } else if (R < p.q_rows + p.kv_rows) {
-      const uint32_t pi = (R - p.q_rows) >> 1, kvh = pi / half_d, i = pi % half_d;
+      // Q or K: tile m of a head holds pair elements i = 8m + l and i + d/2
+      const bool isq = R < p.q_rows;
+      const uint32_t Rr = isq ? R : R - p.q_rows;
+      const uint32_t head = Rr / hd, w = Rr % hd, i = (w / kTileRows) * 8u + (w % kTileRows);
       rope_pair(a, b, pos, i, p.inv_freq, p.ext, p.rope_scaling);
-      __half *dst = p.kc + ((size_t)kvh * p.ctx + pos) * hd;  // store_kv.comp:21-22, RNE
-      dst[i] = __float2half_rn(a);
-      dst[i + half_d] = __float2half_rn(b);
+      if (isq) {
+        p.out[head * hd + i] = a;
+        p.out[head * hd + i + half_d] = b;
+      } else {
+        __half *dst = p.kc + ((size_t)head * p.ctx + pos) * hd;  // store_kv.comp:21-22, RNE
+        dst[i] = __float2half_rn(a);
+        dst[i + half_d] = __float2half_rn(b);
+      }
     } else {
-      const uint32_t R2 = R - p.q_rows - p.kv_rows, kvh = R2 / hd, j = R2 % hd;
+      const uint32_t v = R - p.q_rows - p.kv_rows, kvh = v / hd, j = v % hd;
       __half *dst = p.vc + ((size_t)kvh * p.ctx + pos) * hd;
       dst[j] = __float2half_rn(a);
-      dst[j + 1] = __float2half_rn(b);
+      dst[j + 8u] = __float2half_rn(b);
     }
   }
 }
@@ -248,14 +266,13 @@ __device__ __forceinline__ void mv_epilogue(const MvParams &p, uint32_t R, float
 // (one ~17 KB cp.async.bulk per stage: large copies are what reach full HBM
 // bandwidth on this part) into a ring of shared-memory stages, starting
 // before griddepcontrol.wait so the weights arrive while the previous kernel
-// of the step is still running. Consumer warp w takes segments w, w + 8, ...
-// of the run. After the dependency resolves the consumers build the
+// of the step is still running. Every consumer warp takes one half-segment of
+// every stage. After the dependency resolves the consumers build the
 // activation operand (RMSNorm of the hidden state or a copy, then the exact
-// int8 digits or the fp16 hi/lo split) and run the tensor-core K-steps of
-// their segments, keeping one partial per (tile, warp) in shared memory; a
-// single barrier at the end precedes the reduction of each tile's 8 partials
-// in warp order (deterministic) and the epilogue. Warps never wait on each
-// other while streaming.
+// int8 digits or the fp16 hi/lo split) and run the tensor-core K-steps,
+// keeping one partial per (tile, warp) in shared memory; a single barrier at
+// the end precedes the reduction of each tile's 8 partials in warp order
+// (deterministic) and the epilogue.
 // ---------------------------------------------------------------------------
 template <bool Q8, Mode M, Pro P>
 __global__ void __launch_bounds__(kMvThreads, 1) matvec_kernel(const __grid_constant__ MvParams p) {
@@ -281,7 +298,7 @@ __global__ void __launch_bounds__(kMvThreads, 1) matvec_kernel(const __grid_cons
   if (threadIdx.x == 0) {
     for (uint32_t i = 0; i < NST; ++i) {
       mbar_init(&full[i], 1);
-      mbar_init(&empty[i], kStageSegs);  // a stage's segments go to 4 different warps
+      mbar_init(&empty[i], kMvConsumers);  // every consumer warp releases every stage
     }
     fence_mbar_init();
   }
@@ -443,126 +460,133 @@ __global__ void __launch_bounds__(kMvThreads, 1) matvec_kernel(const __grid_cons
   }
   named_bar(1, NCT);
 
-  // ---------------- consumers: K-step chunks ----------------
+  // ---------------- consumers: K-steps ----------------
+  // mma m16n8k32.s8 (Q8_0) / m16n8k16.f16 (F16) with the weights as A (16 rows
+  // x one K-step) and the activation as B: column n of B is digit n (Q8_0) or
+  // the hi/lo half n (F16); the other columns are zero (their lanes load plane
+  // 0 and mask it). Lane (gq, tq) receives D rows gq and gq + 8, columns 2tq
+  // and 2tq + 1.
   const uint32_t pos = (M == Mode::QKV) ? p.ctrl[kCtrlPos] : 0u;
   const uint32_t gq = lane >> 2, tq = lane & 3u;
-  // digit / half plane this lane feeds into the A fragment (rows 0-2 or 0-1)
-  const bool arow = Q8 ? (gq < 3) : (gq < 2);
-  const uint8_t *aplane = areg + (arow ? gq : 0u) * p.plane;
-  const float dscale = gq == 0 ? 1.0f : gq == 1 ? 0.0078125f : 6.103515625e-05f;  // 2^(-7 gq)
+  const bool brow = Q8 ? (gq < 3) : (gq < 2);
+  const uint8_t *bplane = areg + (brow ? gq : 0u) * p.plane;
+  const uint32_t bmask = brow ? 0xFFFFFFFFu : 0u;
+  // Q8_0: lane tq=0 accumulates t = S0*128 + S1 (digits 0, 1), tq=1 t = S2*128,
+  // so the partial of a row is acc * 2^-7 (tq=0) + acc * 2^-21 (tq=1).
+  // F16: lane tq=0 holds hi (column 0) and lo (column 1).
+  const float lane_scale = Q8 ? (tq == 0 ? 0.0078125f : tq == 1 ? 4.76837158203125e-07f : 0.f) : (tq == 0 ? 1.f : 0.f);
   float acc0 = 0.f, acc1 = 0.f;
-  float cf[4][4] = {};  // F16: four independent accumulators (one per K-step of a batch)
+  float cf[2][4] = {};  // F16: two accumulator chains
   bool ok = true;
 
-  // This warp's partial of one tile's 8 rows (lanes 0-3 hold rows 2tq, 2tq+1)
-  // goes to red[tile][warp]; the final reduction sums the warps in order.
+  // This warp's partial of one tile: after the tq reduction, lane (gq, 0)
+  // holds rows gq and gq + 8; they go to red[tile][warp][row].
   auto flush = [&](uint32_t rel) {
     float v0, v1;
     if constexpr (Q8) {
-      v0 = acc0 + __shfl_down_sync(0xffffffffu, acc0, 4) + __shfl_down_sync(0xffffffffu, acc0, 8);
-      v1 = acc1 + __shfl_down_sync(0xffffffffu, acc1, 4) + __shfl_down_sync(0xffffffffu, acc1, 8);
+      v0 = acc0 * lane_scale;
+      v1 = acc1 * lane_scale;
     } else {
-      const float c0 = (cf[0][0] + cf[1][0]) + (cf[2][0] + cf[3][0]);
-      const float c1 = (cf[0][1] + cf[1][1]) + (cf[2][1] + cf[3][1]);
-      v0 = (c0 + __shfl_down_sync(0xffffffffu, c0, 4)) * *xscale;
-      v1 = (c1 + __shfl_down_sync(0xffffffffu, c1, 4)) * *xscale;
+      v0 = (cf[0][0] + cf[0][1] + cf[1][0] + cf[1][1]) * lane_scale;
+      v1 = (cf[0][2] + cf[0][3] + cf[1][2] + cf[1][3]) * lane_scale;
     }
-    if (lane < 4) {
-      red[(rel * kMvConsumers + cw) * kTileRows + 2 * lane] = v0;
-      red[(rel * kMvConsumers + cw) * kTileRows + 2 * lane + 1] = v1;
+    v0 += __shfl_xor_sync(0xffffffffu, v0, 1);
+    v1 += __shfl_xor_sync(0xffffffffu, v1, 1);
+    v0 += __shfl_xor_sync(0xffffffffu, v0, 2);
+    v1 += __shfl_xor_sync(0xffffffffu, v1, 2);
+    if (tq == 0) {
+      if constexpr (!Q8) {
+        v0 *= *xscale;
+        v1 *= *xscale;
+      }
+      red[(rel * kMvConsumers + cw) * kTileRows + gq] = v0;
+      red[(rel * kMvConsumers + cw) * kTileRows + gq + 8u] = v1;
     }
     acc0 = acc1 = 0.f;
 #pragma unroll
-    for (int a = 0; a < 4; ++a)
+    for (int a = 0; a < 2; ++a)
 #pragma unroll
       for (int b = 0; b < 4; ++b) cf[a][b] = 0.f;
   };
 
-  // Warp cw takes segments cw, cw + 8, cw + 16, ... of the CTA's run. Stage j
-  // holds segments 4j..4j+3, read by warps 0-3 (j even) or 4-7 (j odd), so a
-  // warp waits on every other stage; with an even number of stages a stage
-  // slot is always read by the same warp group and a parity wait is never
-  // more than one phase ahead.
-  uint32_t cur = 0xFFFFFFFFu;  // tile (relative) of the accumulated partial
-  for (uint32_t i = cw; i < n_items && ok; i += kMvConsumers) {
-    const uint32_t j = i / kStageSegs, slot = j % NST;
-    const uint32_t rel = i / NSEG;
-    if (rel != cur) {
-      if (cur != 0xFFFFFFFFu) flush(cur);
-      cur = rel;
-    }
+  // Every warp reads every stage: stage j holds segments 4j..4j+3 and warp cw
+  // takes K-steps 4*(cw%2) .. 4*(cw%2)+3 of segment 4j + cw/2, so all 8 warps
+  // work on the stage at once. A segment never spans two tiles. Every warp
+  // waits for every stage and releases it (the empty barrier counts 8
+  // arrivals), so no warp can run more than one ring phase ahead.
+  const uint32_t sq = (cw & 1u) * kChunkSteps;  // first K-step of this warp within its segment
+  uint32_t cur = 0xFFFFFFFFu;                    // tile (relative) of the accumulated partial
+  for (uint32_t j = 0; j < n_st; ++j) {
+    const uint32_t slot = j % NST;
     if (!mbar_wait_bounded(&full[slot], (j / NST) & 1u)) {
       set_error(err, kErrConsumerWait);
       ok = false;
       break;
     }
-    const uint8_t *seg = ring + slot * STB + (i % kStageSegs) * SEGB;
-    const uint32_t ks0 = (i % NSEG) * kSegSteps;  // first K-step of the segment in the row
-    // Batches of 4 K-steps: all shared-memory loads first, then 4 independent
-    // MMAs, then the rescale, so their latencies overlap.
-#pragma unroll 2
-    for (uint32_t qb = 0; qb < kSegSteps; qb += 4) {
-      uint32_t b[2][4];
-      ldmatrix_x4(b[0], seg + qb * kStepBytes + lane * 16u);
-      ldmatrix_x4(b[1], seg + (qb + 2) * kStepBytes + lane * 16u);
-      uint32_t a0[4], a2[4];
+    const uint32_t i = j * kStageSegs + (cw >> 1);  // this warp's segment
+    if (i < n_items) {
+      const uint32_t rel = i / NSEG;
+      if (rel != cur) {
+        if (cur != 0xFFFFFFFFu) flush(cur);
+        cur = rel;
+      }
+      const uint8_t *seg = ring + slot * STB + (cw >> 1) * SEGB;
+      const uint32_t ks0 = (i % NSEG) * kSegSteps + sq;  // K-step index in the row
+      // all shared-memory loads first, then 4 independent MMAs, then the rescale
+      uint32_t a[4][4], b0[4], b1[4];
 #pragma unroll
       for (uint32_t q = 0; q < 4; ++q) {
-        const uint32_t kg = ks0 + qb + q;
-        a0[q] = 0;
-        a2[q] = 0;
-        if (arow) {
-          if constexpr (Q8) {
-            a0[q] = *reinterpret_cast<const uint32_t *>(aplane + kg * 32u + tq * 4u);
-            a2[q] = *reinterpret_cast<const uint32_t *>(aplane + kg * 32u + 16u + tq * 4u);
-          } else {
-            a0[q] = *reinterpret_cast<const uint32_t *>(aplane + (kg * 16u + tq * 2u) * 2u);
-            a2[q] = *reinterpret_cast<const uint32_t *>(aplane + (kg * 16u + 8u + tq * 2u) * 2u);
-          }
+        ldmatrix_x4(a[q], seg + (sq + q) * kStepBytes + lane * 16u);
+        const uint32_t kg = ks0 + q;
+        if constexpr (Q8) {
+          b0[q] = *reinterpret_cast<const uint32_t *>(bplane + kg * 32u + tq * 4u) & bmask;
+          b1[q] = *reinterpret_cast<const uint32_t *>(bplane + kg * 32u + 16u + tq * 4u) & bmask;
+        } else {
+          b0[q] = *reinterpret_cast<const uint32_t *>(bplane + (kg * 16u + tq * 2u) * 2u) & bmask;
+          b1[q] = *reinterpret_cast<const uint32_t *>(bplane + (kg * 16u + 8u + tq * 2u) * 2u) & bmask;
         }
       }
       if constexpr (Q8) {
-        __half2 dp[4];
-        float sc[4];
+        __half2 ws[4];
+        float xs[4];
 #pragma unroll
         for (uint32_t q = 0; q < 4; ++q) {
-          dp[q] = *reinterpret_cast<const __half2 *>(seg + kSegQsBytes + ((qb + q) * kTileRows + 2u * tq) * 2u);
-          sc[q] = sx[ks0 + qb + q] * dscale;
+          ws[q] = *reinterpret_cast<const __half2 *>(seg + kSegQsBytes + (sq + q) * 32u + gq * 4u);
+          xs[q] = sx[ks0 + q];
         }
         int r[4][4];
 #pragma unroll
-        for (uint32_t q = 0; q < 4; ++q)
-          mma_s8(r[q], a0[q], a2[q], b[q >> 1][2 * (q & 1)], b[q >> 1][2 * (q & 1) + 1]);
-        if (arow) {
+        for (uint32_t q = 0; q < 4; ++q) mma_s8(r[q], a[q], b0[q], b1[q]);
 #pragma unroll
-          for (uint32_t q = 0; q < 4; ++q) {
-            acc0 = fmaf((float)r[q][0], __low2float(dp[q]) * sc[q], acc0);
-            acc1 = fmaf((float)r[q][1], __high2float(dp[q]) * sc[q], acc1);
-          }
+        for (uint32_t q = 0; q < 4; ++q) {
+          const float2 w = __half22float2(ws[q]);
+          const int t0 = r[q][0] * 128 + r[q][1], t1 = r[q][2] * 128 + r[q][3];
+          acc0 = fmaf((float)t0, w.x * xs[q], acc0);
+          acc1 = fmaf((float)t1, w.y * xs[q], acc1);
         }
       } else {
 #pragma unroll
-        for (uint32_t q = 0; q < 4; ++q)
-          mma_f16(cf[q], a0[q], a2[q], b[q >> 1][2 * (q & 1)], b[q >> 1][2 * (q & 1) + 1]);
+        for (uint32_t q = 0; q < 4; ++q) mma_f16(cf[q & 1], a[q], b0[q], b1[q]);
       }
     }
-    // release the segment's share of the stage
+    // release the stage
     __syncwarp();
     if (lane == 0) mbar_arrive(&empty[slot]);
   }
   if (ok && cur != 0xFFFFFFFFu) flush(cur);
   named_bar(1, NCT);  // every partial written
 
-  // Tile reduction and epilogue: tile rel goes to warp rel % 8, lanes 0-3.
+  // Tile reduction and epilogue: tile rel goes to warp rel % 8, lanes 0-7
+  // take rows (l, l + 8), summing the 8 warps' partials in order.
   for (uint32_t rel = cw; rel < t1 - t0; rel += kMvConsumers) {
-    if (lane < 4) {
+    if (lane < 8) {
       float a = 0.f, b = 0.f;
 #pragma unroll
       for (int w = 0; w < kMvConsumers; ++w) {
-        a += red[(rel * kMvConsumers + w) * kTileRows + 2 * lane];
-        b += red[(rel * kMvConsumers + w) * kTileRows + 2 * lane + 1];
+        a += red[(rel * kMvConsumers + w) * kTileRows + lane];
+        b += red[(rel * kMvConsumers + w) * kTileRows + lane + 8u];
       }
-      mv_epilogue<M>(p, (t0 + rel) * kTileRows + 2 * lane, a, b, pos);
+      mv_epilogue<M>(p, (t0 + rel) * kTileRows + lane, a, b, pos);
     }
   }
 }
@@ -880,19 +904,30 @@ __global__ void __launch_bounds__(1024) residual_rmsnorm_kernel(float *hidden, c
 // ---------------------------------------------------------------------------
 // GGUF matrix -> segmented tiles. One CTA per source row; the destination is
 // zero-filled beforehand (padding rows and columns stay zero). The packed row
-// is perm(row) * dst_stride + dst_offset, where perm interleaves the two
-// halves of each group of `pair_group` rows (0 = identity).
+// of source row r is
+//   kPermIdentity: r
+//   kPermRope:     within each group of `group` rows (one head of d rows),
+//                  element i < d/2 and its RoPE partner i + d/2 go to rows l
+//                  and l + 8 of tile i / 8 of the head (l = i % 8)
+//   kPermHalves:   tile r / 8, row r % 8 + 8 * half (gate rows half 0, up
+//                  rows half 1 of an interleaved gate/up matrix)
 // ---------------------------------------------------------------------------
-__global__ void repack_kernel(const uint8_t *src, uint32_t src_rows, TileGeom g, uint8_t *dst, uint32_t dst_stride,
-                              uint32_t dst_offset, uint32_t pair_group) {
+enum : uint32_t { kPermIdentity = 0, kPermRope = 1, kPermHalves = 2 };
+
+__host__ __device__ inline uint32_t packed_row(uint32_t r, uint32_t perm, uint32_t group, uint32_t half) {
+  if (perm == kPermRope) {
+    const uint32_t w = r % group, h = group / 2, i = w < h ? w : w - h;
+    return (r / group) * group + (i / 8u) * kTileRows + (i % 8u) + (w < h ? 0u : 8u);
+  }
+  if (perm == kPermHalves) return (r / 8u) * kTileRows + (r % 8u) + 8u * half;
+  return r;
+}
+
+__global__ void repack_kernel(const uint8_t *src, uint32_t src_rows, TileGeom g, uint8_t *dst, uint32_t perm,
+                              uint32_t group, uint32_t half) {
   const uint32_t cols = g.cols;
   for (uint32_t r = blockIdx.x; r < src_rows; r += gridDim.x) {
-    uint32_t pr = r;
-    if (pair_group) {
-      const uint32_t grp = r / pair_group, w = r % pair_group, h = pair_group / 2;
-      pr = grp * pair_group + (w < h ? 2 * w : 2 * (w - h) + 1);
-    }
-    const uint32_t R = pr * dst_stride + dst_offset;
+    const uint32_t R = packed_row(r, perm, group, half);
     if (g.q8) {
       const uint32_t nb = cols / 32;
       const uint8_t *in = src + (size_t)r * nb * 34;
