@@ -144,6 +144,14 @@ int vg_stream_destroy(vg_stream *stream);
  * src/baselm.rs:616-620). */
 int vg_stream_reset(vg_stream *stream);
 int vg_stream_position(const vg_stream *stream, uint32_t *position);
+/* How this stream runs a decode step: 1 = one persistent cooperative kernel
+ * per token (all layers, grid barriers between phases), 0 = one kernel per
+ * projection / attention / norm (the program the reference records,
+ * record_transformer, src/baselm.rs:892-1052). Chosen at vg_stream_create:
+ * the persistent kernel needs one weight format for all projections and
+ * cooperative launch; the environment variable VOXGEN_STEP_KERNEL=0 selects
+ * the per-kernel program. */
+int vg_stream_kernel_mode(const vg_stream *stream, int *mode);
 /* The cudaStream_t every call of this stream is enqueued on. */
 int vg_stream_cuda_stream(const vg_stream *stream, void **cuda_stream);
 /* Writes fp16 K and V for positions [0, n_positions) of every layer from host

@@ -31,7 +31,7 @@ EXPORTS = [
     "vg_ctx_create", "vg_ctx_destroy", "vg_last_error", "vg_ctx_sm_count", "vg_gguf_inspect",
     "vg_kv_cache_bytes", "vg_top_k_logits",
     "vg_model_load_gguf", "vg_model_info_get", "vg_model_destroy", "vg_stream_create",
-    "vg_stream_destroy", "vg_stream_reset", "vg_stream_position", "vg_stream_cuda_stream",
+    "vg_stream_destroy", "vg_stream_reset", "vg_stream_position", "vg_stream_cuda_stream", "vg_stream_kernel_mode",
     "vg_stream_write_kv", "vg_stream_read_kv", "vg_decode_token", "vg_decode_embedding",
     "vg_decode_embedding_device", "vg_prefill_tokens", "vg_stream_output", "vg_stream_logits",
     "vg_copy_output", "vg_copy_logits", "vg_stream_sync", "vg_step_result_get", "vg_benchmark",
@@ -108,6 +108,7 @@ def lib() -> C.CDLL:
         "vg_stream_create": ([P, U32, PP], I), "vg_stream_destroy": ([P], I),
         "vg_stream_reset": ([P], I), "vg_stream_position": ([P, C.POINTER(U32)], I),
         "vg_stream_cuda_stream": ([P, PP], I),
+        "vg_stream_kernel_mode": ([P, C.POINTER(I)], I),
         "vg_stream_write_kv": ([P, P, P, U32], I), "vg_stream_read_kv": ([P, P, P, U32], I),
         "vg_decode_token": ([P, U32, I], I), "vg_decode_embedding": ([P, P, I], I),
         "vg_decode_embedding_device": ([P, P, I], I), "vg_prefill_tokens": ([P, P, U32, I], I),
@@ -268,6 +269,13 @@ class BaseLmEngine:
 
     def reset(self) -> None:
         self._check(lib().vg_stream_reset(self.h))
+
+    @property
+    def kernel_mode(self) -> int:
+        """1: one persistent kernel per step; 0: one kernel per projection/attention/norm."""
+        m = C.c_int()
+        self._check(lib().vg_stream_kernel_mode(self.h, C.byref(m)))
+        return m.value
 
     @property
     def cuda_stream(self) -> int:

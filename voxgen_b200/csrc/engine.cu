@@ -22,11 +22,12 @@
 #include <set>
 #include <string>
 #include <thread>
+#include <type_traits>
 #include <vector>
 
 #include "../../include/voxgen_cuda.h"
 #include "gguf_loader.h"
-#include "kernels.cuh"
+#include "step_kernel.cuh"
 
 using namespace vg;
 
@@ -273,6 +274,12 @@ struct vg_stream {
   cudaEvent_t ev_done = nullptr;
   cudaGraphExec_t graphs[2][2] = {{nullptr, nullptr}, {nullptr, nullptr}};  // [token_input][logits]
   bool logits_valid = false;
+  // persistent decode-step kernel (one cooperative launch per token)
+  bool use_step = false;     // else the step is the per-kernel program of build_program
+  bool step_graph = true;    // the cooperative launch is captured in the step graphs
+  StepParams sp{};           // token_input / want_logits set per launch
+  void (*step_fn)(StepParams) = nullptr;
+  uint32_t step_smem = 0, step_grid = 0;
 };
 
 namespace {
@@ -573,16 +580,115 @@ void build_program(vg_stream *s, bool token_input, bool logits, std::vector<Laun
   }
 }
 
+// ---- persistent decode-step kernel ------------------------------------------
+using StepFn = void (*)(StepParams);
+template <bool Q8>
+StepFn pick_step_dpl(uint32_t head_dim) {
+  switch (head_dim) {
+    case 32: return decode_step_kernel<Q8, 1>;
+    case 64: return decode_step_kernel<Q8, 2>;
+    case 128: return decode_step_kernel<Q8, 4>;
+    case 256: return decode_step_kernel<Q8, 8>;
+  }
+  return nullptr;
+}
+
+// Shared-memory plan and kernel choice of the step kernel (pointers are filled
+// in by vg_stream_create). False when the model or the device does not fit it:
+// the projections must share one weight format, the device must support
+// cooperative launch, and one CTA with its plan must fit on an SM.
+bool plan_step(vg_stream *s) {
+  vg_model *m = s->m;
+  const BaseLmConfig &c = m->cfg;
+  const char *env = getenv("VOXGEN_STEP_KERNEL");
+  if (env && env[0] == '0') return false;
+  const uint32_t type = m->layers[0].qkv.type;
+  for (const Layer &L : m->layers)
+    for (const DevMat *d : {&L.qkv, &L.o, &L.gateup, &L.down})
+      if (d->type != type) return false;
+  const int dev = m->ctx->device;
+  int coop = 0;
+  CK(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev));
+  if (!coop) return false;
+  const uint32_t D = c.head_dim, G = c.head_count / c.head_count_kv;
+  StepParams &p = s->sp;
+  p = StepParams{};
+  const Layer &L0 = m->layers[0];
+  p.g_qkv = L0.qkv.g;
+  p.g_o = L0.o.g;
+  p.g_gu = L0.gateup.g;
+  p.g_down = L0.down.g;
+  p.g_tok = m->tok.g;
+  p.g_head = m->out.g;
+  p.n_layers = c.block_count;
+  const uint32_t grid = (uint32_t)m->ctx->sms;
+  uint32_t segb = 0, plane = 0, cpad = 0, rb = 1;
+  for (const TileGeom *g : {&p.g_qkv, &p.g_o, &p.g_gu, &p.g_down, &p.g_head}) {
+    segb = std::max(segb, g->seg_bytes());
+    const uint32_t cp = g->nseg() * g->seg_cols();
+    cpad = std::max(cpad, cp);
+    plane = std::max(plane, mv_a_plane(g->q8, cp));
+    rb = std::max(rb, (g->tiles() + grid - 1) / grid);
+  }
+  p.slot = kStageSegs * segb;
+  p.chunk = std::min<uint32_t>(64u, p.slot / (2u * D));
+  p.max_chunks = (s->max_ctx + p.chunk - 1) / p.chunk;
+  p.plane = plane;
+  p.a_bytes = std::max(round_up(3u * plane + cpad / 32u * 4u + 16u, 128u), step_attn_bytes(G, D, p.chunk, p.max_chunks));
+  p.rb = rb;
+  p.nst = 0;
+  const uint32_t fixed = StepSmem(p).total;
+  if (fixed + 2u * (p.slot + 16u) > kSmemMax) return false;
+  p.nst = std::min<uint32_t>(16u, (kSmemMax - fixed) / (p.slot + 16u));
+  s->step_smem = StepSmem(p).total;
+  s->step_fn = type == GGML_Q8_0 ? pick_step_dpl<true>(D) : pick_step_dpl<false>(D);
+  if (!s->step_fn) return false;
+  ensure_smem((const void *)s->step_fn, dev, s->step_smem);
+  int per_sm = 0;
+  CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, s->step_fn, kMvThreads, s->step_smem));
+  if (per_sm < 1) return false;
+  s->step_grid = grid;
+  return true;
+}
+
+cudaError_t launch_step_kernel(vg_stream *s, bool token_input, bool logits) {
+  StepParams p = s->sp;
+  p.token_input = token_input;
+  p.want_logits = logits;
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(s->step_grid);
+  cfg.blockDim = dim3(kMvThreads);
+  cfg.dynamicSmemBytes = s->step_smem;
+  cfg.stream = s->st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeCooperative;
+  at[0].val.cooperative = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, s->step_fn, p);
+}
+
 cudaGraphExec_t get_graph(vg_stream *s, bool token_input, bool logits) {
   cudaGraphExec_t &g = s->graphs[token_input][logits];
   if (g) return g;
   std::vector<Launch> prog;
-  build_program(s, token_input, logits, prog);
+  if (s->use_step) {
+    prog.push_back({[=](cudaStream_t, bool) { return launch_step_kernel(s, token_input, logits); }, "step", 0, 0});
+  } else {
+    build_program(s, token_input, logits, prog);
+  }
   cudaGraph_t graph = nullptr;
   CK(cudaStreamBeginCapture(s->st, cudaStreamCaptureModeThreadLocal));
   cudaError_t e = cudaSuccess;
   for (size_t i = 0; i < prog.size() && e == cudaSuccess; ++i) e = prog[i].fn(s->st, i > 0);
   cudaError_t e2 = cudaStreamEndCapture(s->st, &graph);
+  if (s->use_step && (e != cudaSuccess || e2 != cudaSuccess)) {
+    // capture of the cooperative launch is not available: launch it directly
+    if (graph) cudaGraphDestroy(graph);
+    cudaGetLastError();
+    s->step_graph = false;
+    return nullptr;
+  }
   if (e != cudaSuccess) {
     if (graph) cudaGraphDestroy(graph);
     fail(VG_ECUDA, strf("kernel launch during capture failed: %s", cudaGetErrorString(e)));
@@ -610,8 +716,11 @@ uint8_t *staging_slot(vg_stream *s) {
 cudaEvent_t staging_event(vg_stream *s) { return s->pin_ev[(s->pin_next + kStagingSlots - 1) % kStagingSlots]; }
 
 void launch_step(vg_stream *s, bool token_input, bool logits) {
-  cudaGraphExec_t g = get_graph(s, token_input, logits);
-  CK(cudaGraphLaunch(g, s->st));
+  cudaGraphExec_t g = s->step_graph ? get_graph(s, token_input, logits) : nullptr;
+  if (g)
+    CK(cudaGraphLaunch(g, s->st));
+  else
+    CK(launch_step_kernel(s, token_input, logits));
   s->pos += 1;
   s->logits_valid = logits;
 }
@@ -812,6 +921,8 @@ int vg_stream_create(vg_model *m, uint32_t max_context, vg_stream **out) {
     s->max_ctx = max_context;
     const uint32_t H = c.embedding_length, D = c.head_dim, G = c.head_count / c.head_count_kv;
     plan_attention(max_context, s->nsplit, s->chunk_cap);
+    s->use_step = plan_step(s);
+    const uint32_t nch = s->use_step ? s->sp.max_chunks : 0u;
     const size_t kv_elems = (size_t)c.block_count * c.head_count_kv * max_context * D;
     CK(cudaMalloc(&s->kc, kv_elems * 2 * sizeof(__half)));
     s->vc = s->kc + kv_elems;
@@ -827,7 +938,11 @@ int vg_stream_create(vg_model *m, uint32_t max_context, vg_stream **out) {
                  o_att = take((size_t)H * 4), o_g = take((size_t)c.feed_forward_length * 4),
                  o_lg = take((size_t)c.vocab_size * 4),
                  o_part = take((size_t)c.head_count_kv * (s->nsplit / kAttnCluster) * G * (D + 2) * 4),
-                 o_tk = take((size_t)c.head_count_kv * G * 4);
+                 o_tk = take((size_t)c.head_count_kv * G * 4),
+                 o_bar = take(8), o_sl = take((size_t)c.block_count * sizeof(StepLayer)),
+                 o_sp = take((size_t)c.head_count_kv * nch * G * D * 4),
+                 o_sml = take((size_t)c.head_count_kv * nch * G * 8),
+                 o_stk = take((size_t)c.head_count_kv * 4);
     CK(cudaMalloc(&s->dev_block, off));
     CK(cudaMemset(s->dev_block, 0, off));
     uint8_t *b = static_cast<uint8_t *>(s->dev_block);
@@ -841,6 +956,47 @@ int vg_stream_create(vg_model *m, uint32_t max_context, vg_stream **out) {
     s->logits = (float *)(b + o_lg);
     s->part = (float *)(b + o_part);
     s->tickets = (uint32_t *)(b + o_tk);
+    if (s->use_step) {
+      StepParams &p = s->sp;
+      std::vector<StepLayer> tab(c.block_count);
+      const size_t per_layer = (size_t)c.head_count_kv * max_context * D;
+      for (uint32_t l = 0; l < c.block_count; ++l) {
+        const Layer &L = m->layers[l];
+        tab[l] = StepLayer{L.qkv.w, L.o.w, L.gateup.w, L.down.w, L.attn_norm, L.ffn_norm,
+                           s->kc + l * per_layer, s->vc + l * per_layer};
+      }
+      CK(cudaMemcpy(b + o_sl, tab.data(), tab.size() * sizeof(StepLayer), cudaMemcpyHostToDevice));
+      p.layers = (const StepLayer *)(b + o_sl);
+      p.tok = m->tok.w;
+      p.head = m->out.w;
+      p.out_norm = m->out_norm;
+      p.hid_a = s->hid_a;
+      p.hid_b = s->hid_b;
+      p.q = s->q;
+      p.attn = s->attn;
+      p.gate = s->gate;
+      p.logits = s->logits;
+      p.out = s->out_norm;
+      p.part = (float *)(b + o_sp);
+      p.part_ml = (float2 *)(b + o_sml);
+      p.tickets = (uint32_t *)(b + o_stk);
+      p.inv_freq = m->inv_freq;
+      p.ext = m->ext;
+      p.rope_scaling = c.rope_scaling_factor();
+      p.eps = c.rms_epsilon;
+      p.res_scale = eff_scale(c.residual_scale);
+      p.emb_scale = eff_scale(c.embedding_scale);
+      p.logit_scale = eff_scale(c.logit_scale);
+      p.attn_scale = 1.0f / sqrtf((float)D);
+      p.H = H;
+      p.F = c.feed_forward_length;
+      p.heads = c.head_count;
+      p.kv_heads = c.head_count_kv;
+      p.head_dim = D;
+      p.ctx = max_context;
+      p.ctrl = s->ctrl;
+      p.bar = (unsigned long long *)(b + o_bar);
+    }
     CK(cudaStreamCreateWithFlags(&s->st, cudaStreamNonBlocking));
     CK(cudaEventCreateWithFlags(&s->ev_done, cudaEventDisableTiming));
     s->pin_in_stride = round_up_sz(16 + (size_t)H * 4, 256);
@@ -890,6 +1046,13 @@ int vg_stream_position(const vg_stream *s, uint32_t *position) {
   if (!live(s)) return VG_ESTATE;
   if (!position) return VG_EINVAL;
   *position = s->pos;
+  return VG_OK;
+}
+
+int vg_stream_kernel_mode(const vg_stream *s, int *mode) {
+  if (!live(s)) return VG_ESTATE;
+  if (!mode) return VG_EINVAL;
+  *mode = s->use_step ? 1 : 0;
   return VG_OK;
 }
 

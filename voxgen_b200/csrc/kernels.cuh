@@ -173,13 +173,14 @@ __device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], const void *p) {
                : "r"(smem_u32(p)));
 }
 
-// D = A(16x32 s8, row) * B(32x8 s8, col), A fragment as ldmatrix.x4 delivers it.
-__device__ __forceinline__ void mma_s8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+// D = A(16x32 s8, row) * B(32x8 s8, col) + c (every element), A fragment as
+// ldmatrix.x4 delivers it.
+__device__ __forceinline__ void mma_s8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1, int c) {
   asm(
       "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
-      "{%10, %11, %12, %13};"
+      "{%10, %10, %10, %10};"
       : "=r"(d[0]), "=r"(d[1]), "=r"(d[2]), "=r"(d[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0), "r"(0), "r"(0), "r"(0));
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(c));
 }
 
 // C += A(16x16 f16, row) * B(16x8 f16, col) in fp32.
@@ -261,109 +262,118 @@ __device__ __forceinline__ void mv_epilogue(const MvParams &p, uint32_t R, float
 // ---------------------------------------------------------------------------
 // Matrix-vector product with fused prologue and epilogue.
 //
-// CTA c owns a contiguous range of tiles, i.e. a contiguous run of segments in
-// HBM. The producer warp streams that run in stages of kStageSegs segments
-// (one ~17 KB cp.async.bulk per stage: large copies are what reach full HBM
-// bandwidth on this part) into a ring of shared-memory stages, starting
-// before griddepcontrol.wait so the weights arrive while the previous kernel
-// of the step is still running. Every consumer warp takes one half-segment of
-// every stage. After the dependency resolves the consumers build the
-// activation operand (RMSNorm of the hidden state or a copy, then the exact
-// int8 digits or the fp16 hi/lo split) and run the tensor-core K-steps,
-// keeping one partial per (tile, warp) in shared memory; a single barrier at
-// the end precedes the reduction of each tile's 8 partials in warp order
-// (deterministic) and the epilogue.
+// A CTA owns a contiguous range of tiles, i.e. a contiguous run of segments in
+// HBM. A producer warp streams that run in stages of kStageSegs segments (one
+// ~17 KB cp.async.bulk per stage: large copies are what reach full HBM
+// bandwidth on this part) into a ring of shared-memory stages. The consumer
+// warps build the activation operand (RMSNorm of the hidden state or a copy,
+// then the exact int8 digits or the fp16 hi/lo split), run the tensor-core
+// K-steps with every warp taking a 4-K-step batch of every stage, keep one
+// partial per (tile, warp) in shared memory, and after one barrier reduce each
+// tile's 8 partials in warp order (deterministic) and run the epilogue.
+//
+// The three parts are device functions shared by matvec_kernel (one matrix per
+// launch) and the persistent decode-step kernel (all matrices of a step in one
+// launch, the ring running across them).
 // ---------------------------------------------------------------------------
-template <bool Q8, Mode M, Pro P>
-__global__ void __launch_bounds__(kMvThreads, 1) matvec_kernel(const __grid_constant__ MvParams p) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  const MvSmem L(p);
-  const TileGeom g = p.g;
-  const uint32_t NSEG = g.nseg(), SEGB = g.seg_bytes(), NST = p.stages;
-  const uint32_t STB = kStageSegs * SEGB;
-  uint8_t *ring = smem + L.ring;
-  uint64_t *full = reinterpret_cast<uint64_t *>(smem + L.bars);
-  uint64_t *empty = full + NST;
-  float *red = reinterpret_cast<float *>(smem + L.red);  // [tile][warp][row] partial sums
-  float *scr = reinterpret_cast<float *>(smem + L.scr);
+struct MvRing {
+  uint8_t *ring;           // nst slots of `slot` bytes
+  uint64_t *full, *empty;  // per slot: bulk copy landed / all consumer warps done
+  uint32_t nst, slot;
+};
 
-  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
-  const uint32_t T = g.tiles();
-  const uint32_t t0 = (uint32_t)((uint64_t)blockIdx.x * T / gridDim.x);
-  const uint32_t t1 = (uint32_t)((uint64_t)(blockIdx.x + 1) * T / gridDim.x);
-  const uint32_t n_items = (t1 - t0) * NSEG;                    // segments of this CTA
-  const uint32_t n_st = (n_items + kStageSegs - 1) / kStageSegs;  // stages of this CTA
-  uint32_t *err = p.ctrl + kCtrlErr;
-
-  if (threadIdx.x == 0) {
-    for (uint32_t i = 0; i < NST; ++i) {
-      mbar_init(&full[i], 1);
-      mbar_init(&empty[i], kMvConsumers);  // every consumer warp releases every stage
+// Position in the ring, advanced without divisions: the slot of the next
+// stage, the parity of that slot's current use, and the stage count.
+struct RingPos {
+  uint32_t slot = 0, phase = 0, n = 0;
+  __device__ __forceinline__ void next(uint32_t nst) {
+    ++n;
+    if (++slot == nst) {
+      slot = 0;
+      phase ^= 1u;
     }
-    fence_mbar_init();
   }
-  for (uint32_t i = threadIdx.x; i < (t1 - t0) * kMvConsumers * kTileRows; i += blockDim.x) red[i] = 0.f;
-  __syncthreads();
-  pdl_launch_dependents();
+};
 
-  if (warp == kMvConsumers) {
-    // ---------------- producer ----------------
-    if (lane == 0) {
-      const uint8_t *src = p.w + (uint64_t)t0 * NSEG * SEGB;
-      uint32_t j = 0;
-      for (; j < n_st; ++j) {
-        const uint32_t slot = j % NST;
-        if (j >= NST && !mbar_wait_bounded(&empty[slot], ((j / NST) - 1u) & 1u)) {
-          set_error(err, kErrConsumerWait);
-          break;
-        }
-        const uint32_t segs = min(kStageSegs, n_items - j * kStageSegs);
-        mbar_arrive_expect_tx(&full[slot], segs * SEGB);
-        bulk_g2s(ring + slot * STB, src + (uint64_t)j * STB, segs * SEGB, &full[slot]);
-      }
-      // never leave with copies in flight: wait (bounded) for the last phase of each stage
-      for (uint32_t i = 0; i < NST && i < j; ++i) {
-        const uint32_t last = i + ((j - 1u - i) / NST) * NST;
-        if (!mbar_wait_bounded(&full[i], (last / NST) & 1u)) {
-          set_error(err, kErrDrainWait);
-          break;
-        }
-      }
+// Producer side of one stage: waits (bounded) until the slot's previous use
+// has been released, then announces `bytes` for it. False when the wait gave up.
+__device__ __forceinline__ bool ring_claim(const MvRing &R, const RingPos &rp, uint32_t bytes,
+                                           const uint32_t *abort_flag, uint32_t *err) {
+  if (rp.n >= R.nst && !mbar_wait_bounded(&R.empty[rp.slot], rp.phase ^ 1u, abort_flag)) {
+    set_error(err, kErrConsumerWait);
+    return false;
+  }
+  mbar_arrive_expect_tx(&R.full[rp.slot], bytes);
+  return true;
+}
+
+// Issues the stages of a run of n_items segments of SEGB bytes starting at src
+// as the next stages of the ring. False when a wait for a free slot gave up.
+__device__ __forceinline__ bool mv_produce(const MvRing &R, const uint8_t *src, uint32_t n_items, uint32_t SEGB,
+                                           RingPos &rp, const uint32_t *abort_flag, uint32_t *err) {
+  for (uint32_t s = 0; s < n_items; s += kStageSegs) {
+    const uint32_t bytes = min(kStageSegs, n_items - s) * SEGB;
+    if (!ring_claim(R, rp, bytes, abort_flag, err)) return false;
+    bulk_g2s(R.ring + rp.slot * R.slot, src + (uint64_t)s * SEGB, bytes, &R.full[rp.slot]);
+    rp.next(R.nst);
+  }
+  return true;
+}
+
+// Waits (bounded) until every bulk copy issued into the ring has landed, so
+// that the CTA never exits with copies in flight: the last use of each slot is
+// the one just before rp (going back one lap).
+__device__ __forceinline__ void mv_drain(const MvRing &R, const RingPos &rp, uint32_t *err) {
+  for (uint32_t i = 0; i < R.nst && i < rp.n; ++i) {
+    // slot i's last use has parity rp.phase if it lies before rp.slot in this lap, else the previous one
+    const uint32_t par = i < rp.slot ? rp.phase : rp.phase ^ 1u;
+    if (!mbar_wait_bounded(&R.full[i], par, nullptr)) {
+      set_error(err, kErrDrainWait);
+      return;
     }
-    return;
   }
+}
 
-  // ---------------- consumers: activation operand ----------------
+// Activation operand of a matvec in shared memory: Q8_0 -> three int8 digit
+// planes and the per-32-block power of two sx[]; F16 -> fp16 hi and lo planes
+// and the whole-vector power of two *xscale. Run by the kMvConsumers consumer
+// warps (named barrier 1). xload(k) returns input element k < C (the hidden
+// state for RMSNORM, the input vector for COPY); wait_input() is called after
+// the RMSNorm weights are loaded and before the first xload. With xout set,
+// the (normalised) input vector is also written there.
+template <bool Q8, Pro P, class XLoad, class Wait>
+__device__ __forceinline__ void mv_activation(uint32_t C, uint32_t cols_pad, const float *normw, float eps,
+                                              uint8_t *areg, uint32_t plane, float *scr, uint32_t cw, uint32_t lane,
+                                              XLoad xload, Wait wait_input, float *xout) {
   constexpr uint32_t NCT = kMvConsumers * 32;
-  const uint32_t cw = warp;
-  const uint32_t C = g.cols;
-  const uint32_t cols_pad = NSEG * g.seg_cols();
-  uint8_t *areg = smem + L.a;
-  float *sx = reinterpret_cast<float *>(areg + 3u * p.plane);      // Q8: per-block 2^e
-  float *xscale = reinterpret_cast<float *>(areg + 2u * p.plane);  // F16: 2^e of the whole vector
-
-  // Every activation load is issued up front (one round trip to L2); the
-  // RMSNorm weight does not depend on the previous kernel and is loaded
-  // before griddepcontrol.wait. Warp cw handles 32-element blocks cw, cw + 8,
-  // ... with one element per lane, so a block's max is one redux.
-  // Register path for up to 4096 (RMSNorm inputs) or 6144 (copied inputs) columns.
+  float *sx = reinterpret_cast<float *>(areg + 3u * plane);      // Q8: per-block 2^e
+  float *xscale = reinterpret_cast<float *>(areg + 2u * plane);  // F16: 2^e of the whole vector
+  // Warp cw handles the 32-element blocks b with (b / 4) % 8 == cw, one
+  // element per lane, so a block's max is one redux. When a tile has a
+  // multiple of 4 segments (kStageSegs) these are exactly the Q8_0 K-steps
+  // that warp cw consumes in mv_consume, so no barrier is needed between the
+  // digits and the MMAs. Every activation load is issued up front (one round
+  // trip); the RMSNorm weight does not depend on the producer of the input
+  // and is loaded before the wait. Register path for up to 4096 (RMSNorm
+  // inputs) or 6144 (copied inputs) columns.
   constexpr uint32_t MAXJ = P == Pro::RMSNORM ? 16 : 24;
   const uint32_t NBLK = cols_pad / 32u;
-  const uint32_t J = (NBLK + kMvConsumers - 1 - cw) / kMvConsumers;  // blocks of this warp
+  auto blk = [&](uint32_t j) { return ((j >> 2) * kMvConsumers + cw) * 4u + (j & 3u); };
+  const uint32_t J = (NBLK / 32u) * 4u + min(4u, (NBLK % 32u > cw * 4u) ? NBLK % 32u - cw * 4u : 0u);
   float xr[MAXJ], wr[MAXJ];
-  const bool regs = (NBLK + kMvConsumers - 1) / kMvConsumers <= MAXJ;
+  const bool regs = (NBLK / 32u) * 4u + min(4u, NBLK % 32u) <= MAXJ;  // warp 0 has the most blocks
   if constexpr (P == Pro::RMSNORM) {
 #pragma unroll
     for (uint32_t j = 0; j < MAXJ; ++j) {
-      const uint32_t k = (cw + j * kMvConsumers) * 32u + lane;
-      wr[j] = (regs && j < J && k < C) ? p.normw[k] : 0.f;
+      const uint32_t k = blk(j) * 32u + lane;
+      wr[j] = (regs && j < J && k < C) ? normw[k] : 0.f;
     }
   }
-  pdl_wait();
+  wait_input();
 #pragma unroll
   for (uint32_t j = 0; j < MAXJ; ++j) {
-    const uint32_t k = (cw + j * kMvConsumers) * 32u + lane;
-    xr[j] = (regs && j < J && k < C) ? p.xsrc[k] : 0.f;
+    const uint32_t k = blk(j) * 32u + lane;
+    xr[j] = (regs && j < J && k < C) ? xload(k) : 0.f;
   }
   float inv_rms = 1.0f;
   if constexpr (P == Pro::RMSNORM) {
@@ -373,7 +383,10 @@ __global__ void __launch_bounds__(kMvThreads, 1) matvec_kernel(const __grid_cons
 #pragma unroll
       for (uint32_t j = 0; j < MAXJ; ++j) ss += xr[j] * xr[j];
     } else {
-      for (uint32_t i = threadIdx.x; i < C; i += NCT) ss += p.xsrc[i] * p.xsrc[i];
+      for (uint32_t i = cw * 32u + lane; i < C; i += NCT) {
+        const float v = xload(i);
+        ss += v * v;
+      }
     }
     ss = warp_sum(ss);
     if (lane == 0) scr[cw] = ss;
@@ -381,7 +394,7 @@ __global__ void __launch_bounds__(kMvThreads, 1) matvec_kernel(const __grid_cons
     float tot = 0.f;
 #pragma unroll
     for (int w = 0; w < kMvConsumers; ++w) tot += scr[w];
-    inv_rms = 1.0f / sqrtf(tot / (float)C + p.eps);
+    inv_rms = 1.0f / sqrtf(tot / (float)C + eps);
     if (regs) {
 #pragma unroll
       for (uint32_t j = 0; j < MAXJ; ++j) xr[j] = __fmul_rn(__fmul_rn(xr[j], inv_rms), wr[j]);
@@ -390,15 +403,29 @@ __global__ void __launch_bounds__(kMvThreads, 1) matvec_kernel(const __grid_cons
   // element k when the row is too long for the register path
   auto xglobal = [&](uint32_t k) -> float {
     if (k >= C) return 0.f;
-    const float v = p.xsrc[k];
-    if constexpr (P == Pro::RMSNORM) return __fmul_rn(__fmul_rn(v, inv_rms), p.normw[k]);
+    const float v = xload(k);
+    if constexpr (P == Pro::RMSNORM) return __fmul_rn(__fmul_rn(v, inv_rms), normw[k]);
     return v;
   };
+  if (xout) {
+    if (regs) {
+#pragma unroll
+      for (uint32_t j = 0; j < MAXJ; ++j) {
+        const uint32_t k = blk(j) * 32u + lane;
+        if (j < J && k < C) xout[k] = xr[j];
+      }
+    } else {
+      for (uint32_t j = 0; j < J; ++j) {
+        const uint32_t k = blk(j) * 32u + lane;
+        if (k < C) xout[k] = xglobal(k);
+      }
+    }
+  }
   if constexpr (Q8) {
     // int8 digits and the per-block exponent (warp-collective per block)
-    int8_t *d0p = reinterpret_cast<int8_t *>(areg), *d1p = d0p + p.plane, *d2p = d1p + p.plane;
+    int8_t *d0p = reinterpret_cast<int8_t *>(areg), *d1p = d0p + plane, *d2p = d1p + plane;
     auto digits = [&](uint32_t j, float x) {
-      const uint32_t b = cw + j * kMvConsumers, k = b * 32u + lane;
+      const uint32_t b = blk(j), k = b * 32u + lane;
       const uint32_t mb = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(x)));
       int e = 0, q0 = 0, q1 = 0, q2 = 0;
       const bool nz = block_exponent(mb, e);
@@ -420,8 +447,11 @@ __global__ void __launch_bounds__(kMvThreads, 1) matvec_kernel(const __grid_cons
       for (uint32_t j = 0; j < MAXJ; ++j)
         if (j < J) digits(j, xr[j]);
     } else {
-      for (uint32_t j = 0; j < J; ++j) digits(j, xglobal((cw + j * kMvConsumers) * 32u + lane));
+      for (uint32_t j = 0; j < J; ++j) digits(j, xglobal(blk(j) * 32u + lane));
     }
+    // each warp consumes only its own blocks when tiles have a multiple of 4 segments
+    if ((cols_pad / (kSegSteps * 32u)) % kStageSegs != 0) named_bar(1, NCT);
+    else __syncwarp();
   } else {
     // whole-vector power-of-two scale, then fp16 hi + lo
     float m = 0.f;
@@ -429,7 +459,7 @@ __global__ void __launch_bounds__(kMvThreads, 1) matvec_kernel(const __grid_cons
 #pragma unroll
       for (uint32_t j = 0; j < MAXJ; ++j) m = fmaxf(m, fabsf(xr[j]));
     } else {
-      for (uint32_t j = 0; j < J; ++j) m = fmaxf(m, fabsf(xglobal((cw + j * kMvConsumers) * 32u + lane)));
+      for (uint32_t j = 0; j < J; ++j) m = fmaxf(m, fabsf(xglobal(blk(j) * 32u + lane)));
     }
     m = warp_max(m);
     named_bar(1, NCT);  // scr[] reuse after the RMSNorm reduction
@@ -441,9 +471,9 @@ __global__ void __launch_bounds__(kMvThreads, 1) matvec_kernel(const __grid_cons
     const uint32_t ef = (__float_as_uint(mx) >> 23) & 0xFFu;
     const int e = ef < 20 ? 0 : (int)ef - 127 - 13;  // max|x| * 2^-e < 2^14
     const float inv = pow2f(-e);
-    __half *hi = reinterpret_cast<__half *>(areg), *lo = reinterpret_cast<__half *>(areg + p.plane);
+    __half *hi = reinterpret_cast<__half *>(areg), *lo = reinterpret_cast<__half *>(areg + plane);
     auto halves = [&](uint32_t j, float x) {
-      const uint32_t k = (cw + j * kMvConsumers) * 32u + lane;
+      const uint32_t k = blk(j) * 32u + lane;
       const float v = x * inv;
       const __half h = __float2half_rn(v);
       hi[k] = h;
@@ -454,30 +484,47 @@ __global__ void __launch_bounds__(kMvThreads, 1) matvec_kernel(const __grid_cons
       for (uint32_t j = 0; j < MAXJ; ++j)
         if (j < J) halves(j, xr[j]);
     } else {
-      for (uint32_t j = 0; j < J; ++j) halves(j, xglobal((cw + j * kMvConsumers) * 32u + lane));
+      for (uint32_t j = 0; j < J; ++j) halves(j, xglobal(blk(j) * 32u + lane));
     }
-    if (threadIdx.x == 0) *xscale = pow2f(e);
+    if (cw == 0 && lane == 0) *xscale = pow2f(e);
+    named_bar(1, NCT);
   }
-  named_bar(1, NCT);
+}
 
-  // ---------------- consumers: K-steps ----------------
+// Consumes the n_items segments of this CTA's tile run from ring stages j, j+1,
+// ... (tile t0 first), writes per-(tile, warp) partials into red (zeroed by the
+// caller for the run's tiles), and after a consumer barrier runs the tile
+// reductions and the epilogue. Returns the next stage index; ok turns false
+// when a wait gave up (the partials are then incomplete and the error flag is
+// set).
+template <bool Q8, Mode M>
+__device__ __forceinline__ void mv_consume(const MvRing &R, RingPos &rp, uint32_t n_items, uint32_t NSEG,
+                                           uint32_t SEGB, const uint8_t *areg, uint32_t plane, float *red,
+                                           const MvParams &p, uint32_t t0, uint32_t pos, uint32_t cw, uint32_t lane,
+                                           const uint32_t *abort_flag, uint32_t *err, bool &ok) {
+  constexpr uint32_t NCT = kMvConsumers * 32;
+  const float *sx = reinterpret_cast<const float *>(areg + 3u * plane);
+  const float *xscale = reinterpret_cast<const float *>(areg + 2u * plane);
   // mma m16n8k32.s8 (Q8_0) / m16n8k16.f16 (F16) with the weights as A (16 rows
   // x one K-step) and the activation as B: column n of B is digit n (Q8_0) or
   // the hi/lo half n (F16); the other columns are zero (their lanes load plane
   // 0 and mask it). Lane (gq, tq) receives D rows gq and gq + 8, columns 2tq
   // and 2tq + 1.
-  const uint32_t pos = (M == Mode::QKV) ? p.ctrl[kCtrlPos] : 0u;
   const uint32_t gq = lane >> 2, tq = lane & 3u;
   const bool brow = Q8 ? (gq < 3) : (gq < 2);
-  const uint8_t *bplane = areg + (brow ? gq : 0u) * p.plane;
+  const uint8_t *bplane = areg + (brow ? gq : 0u) * plane;
   const uint32_t bmask = brow ? 0xFFFFFFFFu : 0u;
-  // Q8_0: lane tq=0 accumulates t = S0*128 + S1 (digits 0, 1), tq=1 t = S2*128,
-  // so the partial of a row is acc * 2^-7 (tq=0) + acc * 2^-21 (tq=1).
+  // Q8_0: the int32 accumulator of the MMA starts at the bit pattern of
+  // 1.5 * 2^23, so the result read as a float is 1.5 * 2^23 + S exactly
+  // (|S| <= 32 * 127 * 64 < 2^22) and one exact subtraction gives S. Lane tq=0
+  // combines digits 0 and 1 as S0 + S1 * 2^-7, lane tq=1 has S2 (column 3 is
+  // zero), so a row's partial is acc (tq=0) + acc * 2^-14 (tq=1).
   // F16: lane tq=0 holds hi (column 0) and lo (column 1).
-  const float lane_scale = Q8 ? (tq == 0 ? 0.0078125f : tq == 1 ? 4.76837158203125e-07f : 0.f) : (tq == 0 ? 1.f : 0.f);
+  constexpr int kMagicBits = 0x4B400000;
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  const float lane_scale = Q8 ? (tq == 0 ? 1.f : tq == 1 ? 6.103515625e-05f : 0.f) : (tq == 0 ? 1.f : 0.f);
   float acc0 = 0.f, acc1 = 0.f;
   float cf[2][4] = {};  // F16: two accumulator chains
-  bool ok = true;
 
   // This warp's partial of one tile: after the tq reduction, lane (gq, 0)
   // holds rows gq and gq + 8; they go to red[tile][warp][row].
@@ -509,34 +556,37 @@ __global__ void __launch_bounds__(kMvThreads, 1) matvec_kernel(const __grid_cons
       for (int b = 0; b < 4; ++b) cf[a][b] = 0.f;
   };
 
-  // Every warp reads every stage: stage j holds segments 4j..4j+3 and warp cw
-  // takes K-steps 4*(cw%2) .. 4*(cw%2)+3 of segment 4j + cw/2, so all 8 warps
-  // work on the stage at once. A segment never spans two tiles. Every warp
-  // waits for every stage and releases it (the empty barrier counts 8
+  // Every warp reads every stage: a stage holds 4 consecutive segments and
+  // warp cw takes K-steps 4*(cw%2) .. 4*(cw%2)+3 of segment cw/2 of it, so all
+  // 8 warps work on the stage at once. A segment never spans two tiles. Every
+  // warp waits for every stage and releases it (the empty barrier counts 8
   // arrivals), so no warp can run more than one ring phase ahead.
   const uint32_t sq = (cw & 1u) * kChunkSteps;  // first K-step of this warp within its segment
-  uint32_t cur = 0xFFFFFFFFu;                    // tile (relative) of the accumulated partial
-  for (uint32_t j = 0; j < n_st; ++j) {
-    const uint32_t slot = j % NST;
-    if (!mbar_wait_bounded(&full[slot], (j / NST) & 1u)) {
+  // this warp's segment of the current stage: index i in the run = tile rel, segment seg of the tile
+  uint32_t i = cw >> 1, rel = 0, seg = i;
+  while (seg >= NSEG) {
+    seg -= NSEG;
+    ++rel;
+  }
+  uint32_t cur = 0xFFFFFFFFu;  // tile (relative) of the accumulated partial
+  for (uint32_t s = 0; s < n_items && ok; s += kStageSegs) {
+    if (!mbar_wait_bounded(&R.full[rp.slot], rp.phase, abort_flag)) {
       set_error(err, kErrConsumerWait);
       ok = false;
       break;
     }
-    const uint32_t i = j * kStageSegs + (cw >> 1);  // this warp's segment
     if (i < n_items) {
-      const uint32_t rel = i / NSEG;
       if (rel != cur) {
         if (cur != 0xFFFFFFFFu) flush(cur);
         cur = rel;
       }
-      const uint8_t *seg = ring + slot * STB + (cw >> 1) * SEGB;
-      const uint32_t ks0 = (i % NSEG) * kSegSteps + sq;  // K-step index in the row
+      const uint8_t *sg = R.ring + rp.slot * R.slot + (cw >> 1) * SEGB;
+      const uint32_t ks0 = seg * kSegSteps + sq;  // K-step index in the row
       // all shared-memory loads first, then 4 independent MMAs, then the rescale
       uint32_t a[4][4], b0[4], b1[4];
 #pragma unroll
       for (uint32_t q = 0; q < 4; ++q) {
-        ldmatrix_x4(a[q], seg + (sq + q) * kStepBytes + lane * 16u);
+        ldmatrix_x4(a[q], sg + (sq + q) * kStepBytes + lane * 16u);
         const uint32_t kg = ks0 + q;
         if constexpr (Q8) {
           b0[q] = *reinterpret_cast<const uint32_t *>(bplane + kg * 32u + tq * 4u) & bmask;
@@ -551,18 +601,19 @@ __global__ void __launch_bounds__(kMvThreads, 1) matvec_kernel(const __grid_cons
         float xs[4];
 #pragma unroll
         for (uint32_t q = 0; q < 4; ++q) {
-          ws[q] = *reinterpret_cast<const __half2 *>(seg + kSegQsBytes + (sq + q) * 32u + gq * 4u);
+          ws[q] = *reinterpret_cast<const __half2 *>(sg + kSegQsBytes + (sq + q) * 32u + gq * 4u);
           xs[q] = sx[ks0 + q];
         }
         int r[4][4];
 #pragma unroll
-        for (uint32_t q = 0; q < 4; ++q) mma_s8(r[q], a[q], b0[q], b1[q]);
+        for (uint32_t q = 0; q < 4; ++q) mma_s8(r[q], a[q], b0[q], b1[q], kMagicBits);
 #pragma unroll
         for (uint32_t q = 0; q < 4; ++q) {
           const float2 w = __half22float2(ws[q]);
-          const int t0 = r[q][0] * 128 + r[q][1], t1 = r[q][2] * 128 + r[q][3];
-          acc0 = fmaf((float)t0, w.x * xs[q], acc0);
-          acc1 = fmaf((float)t1, w.y * xs[q], acc1);
+          const float v0 = fmaf(__int_as_float(r[q][1]) - kMagic, 0.0078125f, __int_as_float(r[q][0]) - kMagic);
+          const float v1 = fmaf(__int_as_float(r[q][3]) - kMagic, 0.0078125f, __int_as_float(r[q][2]) - kMagic);
+          acc0 = fmaf(v0, w.x * xs[q], acc0);
+          acc1 = fmaf(v1, w.y * xs[q], acc1);
         }
       } else {
 #pragma unroll
@@ -571,24 +622,84 @@ __global__ void __launch_bounds__(kMvThreads, 1) matvec_kernel(const __grid_cons
     }
     // release the stage
     __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[slot]);
+    if (lane == 0) mbar_arrive(&R.empty[rp.slot]);
+    rp.next(R.nst);
+    i += kStageSegs;
+    seg += kStageSegs;
+    while (seg >= NSEG) {
+      seg -= NSEG;
+      ++rel;
+    }
   }
   if (ok && cur != 0xFFFFFFFFu) flush(cur);
   named_bar(1, NCT);  // every partial written
 
   // Tile reduction and epilogue: tile rel goes to warp rel % 8, lanes 0-7
   // take rows (l, l + 8), summing the 8 warps' partials in order.
-  for (uint32_t rel = cw; rel < t1 - t0; rel += kMvConsumers) {
+  const uint32_t ntiles = (n_items + NSEG - 1) / NSEG;
+  for (uint32_t t = cw; t < ntiles; t += kMvConsumers) {
     if (lane < 8) {
       float a = 0.f, b = 0.f;
 #pragma unroll
       for (int w = 0; w < kMvConsumers; ++w) {
-        a += red[(rel * kMvConsumers + w) * kTileRows + lane];
-        b += red[(rel * kMvConsumers + w) * kTileRows + lane + 8u];
+        a += red[(t * kMvConsumers + w) * kTileRows + lane];
+        b += red[(t * kMvConsumers + w) * kTileRows + lane + 8u];
       }
-      mv_epilogue<M>(p, (t0 + rel) * kTileRows + lane, a, b, pos);
+      mv_epilogue<M>(p, (t0 + t) * kTileRows + lane, a, b, pos);
     }
   }
+}
+
+template <bool Q8, Mode M, Pro P>
+__global__ void __launch_bounds__(kMvThreads, 1) matvec_kernel(const __grid_constant__ MvParams p) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const MvSmem L(p);
+  const TileGeom g = p.g;
+  const uint32_t NSEG = g.nseg(), SEGB = g.seg_bytes();
+  MvRing R;
+  R.ring = smem + L.ring;
+  R.full = reinterpret_cast<uint64_t *>(smem + L.bars);
+  R.empty = R.full + p.stages;
+  R.nst = p.stages;
+  R.slot = kStageSegs * SEGB;
+  float *red = reinterpret_cast<float *>(smem + L.red);  // [tile][warp][row] partial sums
+  float *scr = reinterpret_cast<float *>(smem + L.scr);
+
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+  const uint32_t T = g.tiles();
+  const uint32_t t0 = (uint32_t)((uint64_t)blockIdx.x * T / gridDim.x);
+  const uint32_t t1 = (uint32_t)((uint64_t)(blockIdx.x + 1) * T / gridDim.x);
+  const uint32_t n_items = (t1 - t0) * NSEG;  // segments of this CTA
+  uint32_t *err = p.ctrl + kCtrlErr;
+
+  if (threadIdx.x == 0) {
+    for (uint32_t i = 0; i < R.nst; ++i) {
+      mbar_init(&R.full[i], 1);
+      mbar_init(&R.empty[i], kMvConsumers);  // every consumer warp releases every stage
+    }
+    fence_mbar_init();
+  }
+  for (uint32_t i = threadIdx.x; i < (t1 - t0) * kMvConsumers * kTileRows; i += blockDim.x) red[i] = 0.f;
+  __syncthreads();
+  pdl_launch_dependents();
+
+  if (warp == kMvConsumers) {
+    // producer: starts before griddepcontrol.wait, so the weights stream in
+    // while the previous kernel of the step is still running
+    if (lane == 0) {
+      RingPos rp;
+      if (mv_produce(R, p.w + (uint64_t)t0 * NSEG * SEGB, n_items, SEGB, rp, nullptr, err)) mv_drain(R, rp, err);
+    }
+    return;
+  }
+  const uint32_t cw = warp;
+  const float *xs = p.xsrc;
+  mv_activation<Q8, P>(g.cols, NSEG * g.seg_cols(), p.normw, p.eps, smem + L.a, p.plane, scr, cw, lane,
+                       [&](uint32_t k) { return __ldcg(xs + k); }, [] { pdl_wait(); }, nullptr);
+  const uint32_t pos = (M == Mode::QKV) ? p.ctrl[kCtrlPos] : 0u;
+  bool ok = true;
+  RingPos rp;
+  mv_consume<Q8, M>(R, rp, n_items, NSEG, SEGB, smem + L.a, p.plane, red, p, t0, pos, cw, lane, nullptr, err, ok);
 }
 
 // ---------------------------------------------------------------------------

@@ -19,6 +19,7 @@ enum : uint32_t {
   kErrDrainWait = 4u,      // bulk copies still in flight at kernel exit
   kErrBadToken = 8u,       // token id outside the vocabulary
   kErrPosition = 16u,      // position outside the KV cache
+  kErrGridWait = 32u,      // a CTA gave up waiting at a grid barrier
 };
 
 __device__ __forceinline__ uint64_t globaltimer() {
@@ -61,13 +62,51 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   return done != 0;
 }
 
-// Waits for the phase with the given parity to complete; false on timeout.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity) {
+__device__ __forceinline__ uint32_t ld_volatile_u32(const uint32_t *p) {
+  uint32_t v;
+  asm volatile("ld.volatile.global.u32 %0, [%1];" : "=r"(v) : "l"(p));
+  return v;
+}
+
+// Waits for the phase with the given parity to complete; false on timeout, or
+// as soon as *abort_flag (when given) is nonzero.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity,
+                                                  const uint32_t *abort_flag = nullptr) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer();
   for (uint32_t it = 0; it < kWaitMaxIters; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 255u) == 255u && globaltimer() - t0 > kWaitLimitNs) return false;
+    if ((it & 255u) == 255u) {
+      if (globaltimer() - t0 > kWaitLimitNs) return false;
+      if (abort_flag && ld_volatile_u32(abort_flag)) return false;
+    }
+  }
+  return false;
+}
+
+// Grid-wide barrier over a monotonically increasing 64-bit arrival counter:
+// grid_arrive adds one arrival with release semantics at GPU scope (the
+// caller first synchronises the arriving threads of its CTA); grid_wait spins
+// (bounded, acquire) until the counter reaches target. Both are called by one
+// thread per CTA; all CTAs of the grid must be resident (cooperative launch).
+__device__ __forceinline__ void grid_arrive(unsigned long long *ctr) {
+  asm volatile("red.release.gpu.global.add.u64 [%0], 1;" ::"l"(ctr) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long *p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ bool grid_wait(const unsigned long long *ctr, unsigned long long target,
+                                          const uint32_t *abort_flag) {
+  if (ld_acquire_u64(ctr) >= target) return true;
+  const uint64_t t0 = globaltimer();
+  for (uint32_t it = 0; it < kWaitMaxIters; ++it) {
+    if (ld_acquire_u64(ctr) >= target) return true;
+    if ((it & 63u) == 63u) {
+      if (globaltimer() - t0 > kWaitLimitNs) return false;
+      if (abort_flag && ld_volatile_u32(abort_flag)) return false;
+    }
   }
   return false;
 }
@@ -95,6 +134,13 @@ __device__ __forceinline__ void prefetch_l2(const void *p) {
 // Named barrier over `threads` threads (a multiple of 32), id 1..15.
 __device__ __forceinline__ void named_bar(uint32_t id, uint32_t threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// Atomic add with acquire-release semantics at GPU scope; returns the old value.
+__device__ __forceinline__ uint32_t atomic_add_acq_rel(uint32_t *p, uint32_t v) {
+  uint32_t old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
 }
 
 __device__ __forceinline__ void set_error(uint32_t *flag, uint32_t bits) {

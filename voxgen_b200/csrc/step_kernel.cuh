@@ -1,0 +1,548 @@
+// The persistent decode-step kernel: one launch per token for the whole
+// BaseLM step (record_transformer, src/baselm.rs:892-1052).
+//
+// One CTA per SM, all resident (cooperative launch). The step is a fixed
+// sequence of phases: per layer QKV (+RoPE, fp16 KV store), attention,
+// o_proj (+residual), gate/up (+SwiGLU), down (+residual); then the final
+// RMSNorm and, when asked, the LM head. A phase may only read what the
+// previous phases wrote, so consecutive phases are separated by a grid
+// barrier (a monotonically increasing arrival counter in global memory).
+//
+// The weights do not depend on anything computed in the step, so each CTA's
+// producer warp streams its share of every phase's weights (and the cached K/V
+// rows its attention units read) into the shared-memory ring in phase order,
+// without waiting for the barriers: while the consumer warps wait for a
+// phase's input the ring fills with the next phases' weights, and HBM stays
+// busy across phase boundaries. The consumer warps run the same matvec and
+// attention code as the standalone kernels, in phase order.
+//
+// Data produced inside the kernel by other CTAs is read with ld.global.cg
+// (L2), never through the non-coherent L1.
+#pragma once
+#include "kernels.cuh"
+
+namespace vg {
+
+struct StepLayer {
+  const uint8_t *qkv, *o, *gateup, *down;  // segmented tiles
+  const float *attn_norm, *ffn_norm;
+  __half *kc, *vc;                          // this layer's caches, [kv_head][ctx][head_dim]
+};
+
+struct StepParams {
+  const StepLayer *layers;  // [n_layers], copied into shared memory at start
+  uint32_t n_layers;
+  TileGeom g_qkv, g_o, g_gu, g_down, g_tok, g_head;
+  const uint8_t *tok;       // token table (segmented tiles)
+  const uint8_t *head;      // LM head (== tok when tied)
+  const float *out_norm;
+  float *hid_a, *hid_b;     // residual stream ping-pong (the layer input is hid_a)
+  float *q, *attn, *gate, *logits, *out;
+  float *part;              // attention partial outputs [kv_heads][max_chunks][G][head_dim]
+  float2 *part_ml;          // their running max and sum [kv_heads][max_chunks][G]
+  uint32_t *tickets;        // [kv_heads], zero between steps
+  const float *inv_freq, *ext;
+  float rope_scaling, eps, res_scale, emb_scale, logit_scale, attn_scale;
+  uint32_t H, F, heads, kv_heads, head_dim, ctx;
+  uint32_t chunk, max_chunks;  // attention positions per unit; partial slots per KV head
+  uint32_t token_input, want_logits;
+  uint32_t *ctrl;
+  unsigned long long *bar;  // grid barrier arrivals
+  // shared-memory plan (host and device agree through StepSmem)
+  uint32_t nst, slot;       // ring stages and bytes per stage slot
+  uint32_t a_bytes, plane;  // activation / attention scratch region and digit-plane stride
+  uint32_t rb;              // partial-sum tiles (largest per-CTA tile run of any phase)
+};
+
+struct StepSmem {
+  uint32_t ring, bars, aux, red, layers, scr, total;
+  __host__ __device__ StepSmem(const StepParams &p) {
+    ring = 0;
+    bars = ring + p.nst * p.slot;
+    aux = bars + p.nst * 16u;
+    red = aux + ((p.a_bytes + 127u) & ~127u);
+    layers = red + p.rb * kMvConsumers * kTileRows * 4u;
+    scr = layers + p.n_layers * (uint32_t)sizeof(StepLayer);
+    total = scr + 512u;
+  }
+};
+
+// Attention scratch inside the aux region: q of one KV group, then the scores
+// of a chunk or (when merging) the weights of every chunk.
+__host__ __device__ inline uint32_t step_attn_bytes(uint32_t G, uint32_t head_dim, uint32_t chunk,
+                                                    uint32_t max_chunks) {
+  return (G * head_dim + G * (chunk > max_chunks ? chunk : max_chunks)) * 4u;
+}
+
+enum : uint32_t { kPhQkv = 0, kPhAttn = 1, kPhO = 2, kPhGu = 3, kPhDown = 4, kPhasesPerLayer = 5 };
+
+__device__ __forceinline__ void tile_run(const TileGeom &g, uint32_t &t0, uint32_t &t1) {
+  const uint32_t T = g.tiles();
+  t0 = (uint32_t)((uint64_t)blockIdx.x * T / gridDim.x);
+  t1 = (uint32_t)((uint64_t)(blockIdx.x + 1) * T / gridDim.x);
+}
+
+// Attention unit u of a step: KV head, chunk, first row, rows, and the rows
+// below the current position (cached by earlier steps, bulk-copied).
+struct AttnUnit {
+  uint32_t kvh, c, r0, len, staged;
+};
+__device__ __forceinline__ AttnUnit attn_unit(const StepParams &p, uint32_t u, uint32_t nch, uint32_t pos) {
+  AttnUnit a;
+  a.kvh = u / nch;
+  a.c = u % nch;
+  a.r0 = a.c * p.chunk;
+  const uint32_t r1 = min(a.r0 + p.chunk, pos + 1u);
+  a.len = r1 - a.r0;
+  a.staged = min(r1, pos) - a.r0;
+  return a;
+}
+
+// Dequantised token-table element k of row tok times alpha (embedding.comp:28-47).
+__device__ __forceinline__ float embed_elem(const StepParams &p, uint32_t tok, uint32_t k) {
+  const TileGeom &g = p.g_tok;
+  float v;
+  if (g.q8) {
+    const float d = __half2float(*reinterpret_cast<const __half *>(p.tok + g.scale_off(tok, k / 32u)));
+    v = __fmul_rn(d, (float)(int8_t)p.tok[g.elem_off(tok, k)]);
+  } else {
+    v = __half2float(*reinterpret_cast<const __half *>(p.tok + g.elem_off(tok, k)));
+  }
+  return __fmul_rn(v, p.emb_scale);
+}
+
+template <bool Q8, int DPL>
+__global__ void __launch_bounds__(kMvThreads, 1) decode_step_kernel(const __grid_constant__ StepParams p) {
+  constexpr uint32_t NCT = kMvConsumers * 32;
+  constexpr uint32_t D = 32u * DPL;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const StepSmem L(p);
+  MvRing R;
+  R.ring = smem + L.ring;
+  R.full = reinterpret_cast<uint64_t *>(smem + L.bars);
+  R.empty = R.full + p.nst;
+  R.nst = p.nst;
+  R.slot = p.slot;
+  uint8_t *aux = smem + L.aux;
+  float *red = reinterpret_cast<float *>(smem + L.red);
+  StepLayer *layers = reinterpret_cast<StepLayer *>(smem + L.layers);
+  float *scr = reinterpret_cast<float *>(smem + L.scr);                       // 64 floats
+  uint32_t *sflags = reinterpret_cast<uint32_t *>(smem + L.scr + 256u);      // 8 words
+  unsigned long long *sbase = reinterpret_cast<unsigned long long *>(smem + L.scr + 384u);
+
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+  uint32_t *err = p.ctrl + kCtrlErr;
+  const uint32_t nb = p.n_layers * kPhasesPerLayer;  // barriers per step = arrivals per CTA
+  const uint32_t G = p.heads / p.kv_heads;
+
+  if (threadIdx.x == 0) {
+    for (uint32_t i = 0; i < R.nst; ++i) {
+      mbar_init(&R.full[i], 1);
+      mbar_init(&R.empty[i], kMvConsumers);
+    }
+    fence_mbar_init();
+    // Every CTA arrives exactly nb times per step, so at a step's start the
+    // counter is base + (arrivals of this step so far) with base a multiple of
+    // nb * gridDim.x and fewer than nb * gridDim.x arrivals counted.
+    const unsigned long long c = ld_acquire_u64(p.bar);
+    const unsigned long long unit = (unsigned long long)nb * gridDim.x;
+    *sbase = c - c % unit;
+  }
+  for (uint32_t i = threadIdx.x; i < p.n_layers * (uint32_t)sizeof(StepLayer) / 8u; i += blockDim.x)
+    reinterpret_cast<unsigned long long *>(layers)[i] = reinterpret_cast<const unsigned long long *>(p.layers)[i];
+  __syncthreads();
+  const unsigned long long base = *sbase;
+
+  uint32_t pos = p.ctrl[kCtrlPos];
+  if (pos >= p.ctx) {
+    if (threadIdx.x == 0) set_error(err, kErrPosition);
+    pos = p.ctx - 1;
+  }
+  const uint32_t nch = (pos + 1u + p.chunk - 1u) / p.chunk;  // attention chunks per KV head
+  const uint32_t n_units = p.kv_heads * nch;
+
+  // ---------------- producer ----------------
+  if (warp == kMvConsumers) {
+    if (lane == 0) {
+      RingPos rp;
+      bool live = true;
+      auto stream = [&](const uint8_t *w, const TileGeom &g) {
+        if (!live) return;
+        uint32_t t0, t1;
+        tile_run(g, t0, t1);
+        const uint32_t NSEG = g.nseg(), SEGB = g.seg_bytes();
+        live = mv_produce(R, w + (uint64_t)t0 * NSEG * SEGB, (t1 - t0) * NSEG, SEGB, rp, err, err);
+      };
+      auto rows = [&](const __half *src, uint32_t n) {  // one stage of n cached K or V rows
+        if (!live) return;
+        live = ring_claim(R, rp, n * D * 2u, err, err);
+        if (!live) return;
+        if (n) bulk_g2s(R.ring + rp.slot * R.slot, src, n * D * 2u, &R.full[rp.slot]);
+        rp.next(R.nst);
+      };
+      for (uint32_t l = 0; l < p.n_layers; ++l) {
+        const StepLayer &Ly = layers[l];
+        stream(Ly.qkv, p.g_qkv);
+        for (uint32_t u = blockIdx.x; u < n_units; u += gridDim.x) {
+          const AttnUnit a = attn_unit(p, u, nch, pos);
+          rows(Ly.kc + ((size_t)a.kvh * p.ctx + a.r0) * D, a.staged);
+          rows(Ly.vc + ((size_t)a.kvh * p.ctx + a.r0) * D, a.staged);
+        }
+        stream(Ly.o, p.g_o);
+        stream(Ly.gateup, p.g_gu);
+        stream(Ly.down, p.g_down);
+      }
+      if (p.want_logits) stream(p.head, p.g_head);
+      if (live) mv_drain(R, rp, err);
+    }
+    return;
+  }
+
+  // ---------------- consumers ----------------
+  const uint32_t cw = warp;
+  RingPos rp;  // next ring stage
+  bool ok = true;
+  // Grid barrier before phase ph: every CTA has finished phase ph - 1.
+  // ld.acquire.gpu in grid_wait, then the CTA barrier, orders every consumer
+  // thread's later loads after the other CTAs' writes; red.release.gpu in
+  // grid_arrive, after the CTA barrier, publishes every consumer thread's
+  // writes of the phase (release is cumulative over what the barrier ordered).
+  auto wait_phase = [&](uint32_t ph) {
+    if (cw == 0 && lane == 0 && ph > 0 &&
+        !grid_wait(p.bar, base + (unsigned long long)ph * gridDim.x, err))
+      set_error(err, kErrGridWait);
+    named_bar(1, NCT);
+  };
+  auto arrive = [&] {
+    named_bar(1, NCT);
+    if (cw == 0 && lane == 0) grid_arrive(p.bar);
+  };
+  auto zero_red = [&](uint32_t tiles) {
+    for (uint32_t i = cw * 32u + lane; i < tiles * kMvConsumers * kTileRows; i += NCT) red[i] = 0.f;
+  };
+  // One matvec phase over this CTA's tile run of g.
+  auto matvec = [&](auto q8c, auto mode, auto pro, uint32_t ph, const uint8_t *w, const TileGeom &g,
+                    const MvParams &mp, auto xload, float *xout) {
+    constexpr bool WQ8 = decltype(q8c)::value;
+    constexpr Mode M = decltype(mode)::value;
+    constexpr Pro P = decltype(pro)::value;
+    uint32_t t0, t1;
+    tile_run(g, t0, t1);
+    const uint32_t NSEG = g.nseg(), SEGB = g.seg_bytes();
+    zero_red(t1 - t0);
+    mv_activation<WQ8, P>(g.cols, NSEG * g.seg_cols(), mp.normw, mp.eps, aux, p.plane, scr, cw, lane, xload,
+                          [&] { wait_phase(ph); }, xout);
+    mv_consume<WQ8, M>(R, rp, (t1 - t0) * NSEG, NSEG, SEGB, aux, p.plane, red, mp, t0, pos, cw, lane, err, err,
+                       ok);
+    (void)w;
+  };
+  using QT = std::integral_constant<bool, Q8>;
+  using MQ = std::integral_constant<Mode, Mode::QKV>;
+  using MR = std::integral_constant<Mode, Mode::RESID>;
+  using MS = std::integral_constant<Mode, Mode::SWIGLU>;
+  using MP = std::integral_constant<Mode, Mode::PLAIN>;
+  using PN = std::integral_constant<Pro, Pro::RMSNORM>;
+  using PC = std::integral_constant<Pro, Pro::COPY>;
+
+  uint32_t tok = 0;
+  if (p.token_input) {
+    tok = p.ctrl[kCtrlToken];
+    if (tok >= p.g_tok.rows) {
+      if (cw == 0 && lane == 0) set_error(err, kErrBadToken);
+      tok = 0;
+    }
+  }
+
+  for (uint32_t l = 0; l < p.n_layers; ++l) {
+    const StepLayer &Ly = layers[l];
+    const uint32_t ph0 = l * kPhasesPerLayer;
+    MvParams mp{};
+    mp.ctrl = p.ctrl;
+    mp.eps = p.eps;
+
+    // ---- QKV + RoPE + KV store: input hid_a (or the token's embedding row) ----
+    mp.g = p.g_qkv;
+    mp.normw = Ly.attn_norm;
+    mp.out = p.q;
+    mp.q_rows = p.H;
+    mp.kv_rows = p.kv_heads * p.head_dim;
+    mp.head_dim = p.head_dim;
+    mp.ctx = p.ctx;
+    mp.kc = Ly.kc;
+    mp.vc = Ly.vc;
+    mp.inv_freq = p.inv_freq;
+    mp.ext = p.ext;
+    mp.rope_scaling = p.rope_scaling;
+    if (l == 0 && p.token_input) {
+      // every CTA dequantises the row itself; CTA 0 also stores it as the residual stream
+      if (blockIdx.x == 0)
+        for (uint32_t k = cw * 32u + lane; k < p.H; k += NCT) p.hid_a[k] = embed_elem(p, tok, k);
+      matvec(QT{}, MQ{}, PN{}, ph0, Ly.qkv, p.g_qkv, mp, [&](uint32_t k) { return embed_elem(p, tok, k); }, nullptr);
+    } else {
+      const float *x = p.hid_a;
+      matvec(QT{}, MQ{}, PN{}, ph0, Ly.qkv, p.g_qkv, mp, [&](uint32_t k) { return __ldcg(x + k); }, nullptr);
+    }
+    arrive();
+
+    // ---- attention: split-K units, the last unit of a KV head merges ----
+    {
+      wait_phase(ph0 + kPhAttn);
+      float *sQ = reinterpret_cast<float *>(aux);  // [G][D]
+      float *sS = sQ + G * D;                       // [G][chunk]
+      for (uint32_t u = blockIdx.x; u < n_units; u += gridDim.x) {
+        const AttnUnit a = attn_unit(p, u, nch, pos);
+        for (uint32_t i = cw * 32u + lane; i < G * D / 4u; i += NCT)
+          reinterpret_cast<float4 *>(sQ)[i] = __ldcg(reinterpret_cast<const float4 *>(p.q + (size_t)a.kvh * G * D) + i);
+        const uint32_t sK = rp.slot, pK = rp.phase;
+        rp.next(R.nst);
+        const uint32_t sV = rp.slot, pV = rp.phase;
+        rp.next(R.nst);
+        if (!mbar_wait_bounded(&R.full[sK], pK, err) || !mbar_wait_bounded(&R.full[sV], pV, err)) {
+          set_error(err, kErrConsumerWait);
+          ok = false;
+        }
+        __half *kS = reinterpret_cast<__half *>(R.ring + sK * R.slot);
+        __half *vS = reinterpret_cast<__half *>(R.ring + sV * R.slot);
+        if (a.staged < a.len) {
+          // the current position's row was stored by this step's QKV phase
+          const __half *kr = Ly.kc + ((size_t)a.kvh * p.ctx + pos) * D;
+          const __half *vr = Ly.vc + ((size_t)a.kvh * p.ctx + pos) * D;
+          for (uint32_t i = cw * 32u + lane; i < D / 2u; i += NCT) {
+            reinterpret_cast<uint32_t *>(kS + a.staged * D)[i] = __ldcg(reinterpret_cast<const unsigned int *>(kr) + i);
+            reinterpret_cast<uint32_t *>(vS + a.staged * D)[i] = __ldcg(reinterpret_cast<const unsigned int *>(vr) + i);
+          }
+        }
+        named_bar(1, NCT);
+        // scores (attn_scores.comp:27-44): warp per position, two positions at
+        // a time so their shuffle reductions overlap; lane holds DPL dims
+        auto kvec = [&](const __half *row, float (&f)[DPL]) {
+          if constexpr (DPL == 1) {
+            f[0] = __half2float(row[lane]);
+          } else {
+#pragma unroll
+            for (int d = 0; d < DPL; d += 2) {  // lane * DPL is even: 4-byte aligned pairs
+              const float2 v = __half22float2(*reinterpret_cast<const __half2 *>(row + lane * DPL + d));
+              f[d] = v.x;
+              f[d + 1] = v.y;
+            }
+          }
+        };
+        for (uint32_t t = cw; t < a.len; t += 2u * kMvConsumers) {
+          const uint32_t t2 = t + kMvConsumers;
+          const bool two = t2 < a.len;
+          float kf[DPL], kg2[DPL];
+          kvec(kS + t * D, kf);
+          if (two) kvec(kS + t2 * D, kg2);
+          else
+#pragma unroll
+            for (int d = 0; d < DPL; ++d) kg2[d] = 0.f;
+          for (uint32_t gb = 0; gb < G; gb += 8) {
+            float pa[8], pb[8];
+#pragma unroll
+            for (uint32_t i = 0; i < 8; ++i) {
+              float x = 0.f, y = 0.f;
+              if (gb + i < G) {
+                const float *qg = sQ + (gb + i) * D + lane * DPL;
+#pragma unroll
+                for (int d = 0; d < DPL; ++d) {
+                  x = fmaf(qg[d], kf[d], x);
+                  y = fmaf(qg[d], kg2[d], y);
+                }
+              }
+              pa[i] = x;
+              pb[i] = y;
+            }
+            const float ta = warp_sum8(pa, lane), tb = warp_sum8(pb, lane);
+            const uint32_t gi = gb + ((lane >> 2) & 7u);
+            if ((lane & 3u) == 0 && gi < G) {
+              sS[gi * p.chunk + t] = __fmul_rn(ta, p.attn_scale);
+              if (two) sS[gi * p.chunk + t2] = __fmul_rn(tb, p.attn_scale);
+            }
+          }
+        }
+        named_bar(1, NCT);
+        // chunk softmax and values (softmax.comp, attn_values.comp): warp per head
+        for (uint32_t g0 = cw; g0 < G; g0 += kMvConsumers) {
+          float *sg = sS + g0 * p.chunk;
+          float m = -INFINITY;
+          for (uint32_t t = lane; t < a.len; t += 32) m = fmaxf(m, sg[t]);
+          m = warp_max(m);
+          float lsum = 0.f;
+          for (uint32_t t = lane; t < a.len; t += 32) {
+            const float e = expf(sg[t] - m);
+            sg[t] = e;
+            lsum += e;
+          }
+          lsum = warp_sum(lsum);
+          __syncwarp();
+          float o[DPL];
+#pragma unroll
+          for (int d = 0; d < DPL; ++d) o[d] = 0.f;
+#pragma unroll 8
+          for (uint32_t t = 0; t < a.len; ++t) {
+            const float pw = sg[t];
+            float vf[DPL];
+            kvec(vS + t * D, vf);
+#pragma unroll
+            for (int d = 0; d < DPL; ++d) o[d] = fmaf(pw, vf[d], o[d]);
+          }
+          const size_t slot_i = ((size_t)a.kvh * p.max_chunks + a.c) * G + g0;
+          float *dst = p.part + slot_i * D + lane * DPL;
+          if constexpr (DPL % 4 == 0) {
+#pragma unroll
+            for (int d = 0; d < DPL; d += 4) *reinterpret_cast<float4 *>(dst + d) = make_float4(o[d], o[d + 1], o[d + 2], o[d + 3]);
+          } else {
+#pragma unroll
+            for (int d = 0; d < DPL; ++d) dst[d] = o[d];
+          }
+          if (lane == 0) p.part_ml[slot_i] = make_float2(m, lsum);
+        }
+        // release the K and V stages
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&R.empty[sK]);
+          mbar_arrive(&R.empty[sV]);
+        }
+        // the last unit of this KV head to finish merges all of its chunks
+        named_bar(1, NCT);
+        if (cw == 0 && lane == 0) sflags[0] = atomic_add_acq_rel(&p.tickets[a.kvh], 1u) == nch - 1u;
+        named_bar(1, NCT);
+        if (sflags[0]) {
+          // warp per query head: lanes hold the chunks' (max, sum) pairs, the
+          // weights go through shuffles, and 16 chunks' outputs are loaded at once
+          for (uint32_t g0 = cw; g0 < G; g0 += kMvConsumers) {
+            const size_t hb = (size_t)a.kvh * p.max_chunks * G + g0;  // slot of chunk 0
+            float M = -INFINITY;
+            for (uint32_t c = lane; c < nch; c += 32) M = fmaxf(M, __ldcg(&p.part_ml[hb + (size_t)c * G].x));
+            M = warp_max(M);
+            float o[DPL];
+#pragma unroll
+            for (int d = 0; d < DPL; ++d) o[d] = 0.f;
+            float Lp = 0.f;
+            const float *ob = p.part + hb * D + lane * DPL;
+            for (uint32_t c0 = 0; c0 < nch; c0 += 32) {
+              float wl = 0.f;
+              if (c0 + lane < nch) {
+                const float2 ml = __ldcg(&p.part_ml[hb + (size_t)(c0 + lane) * G]);
+                wl = ml.x == -INFINITY ? 0.f : expf(ml.x - M);
+                Lp = fmaf(wl, ml.y, Lp);
+              }
+              const uint32_t nc = min(32u, nch - c0);
+              constexpr uint32_t MB = DPL >= 8 ? 8u : 16u;  // chunks in flight (register budget)
+              for (uint32_t cb = 0; cb < nc; cb += MB) {
+                float4 v[MB][DPL / 4 > 0 ? DPL / 4 : 1];
+                float vs[MB][DPL];
+#pragma unroll
+                for (uint32_t k = 0; k < MB; ++k) {
+                  const float *oc = ob + (size_t)(c0 + cb + k) * G * D;
+                  if (cb + k < nc) {
+                    if constexpr (DPL % 4 == 0) {
+#pragma unroll
+                      for (int d = 0; d < DPL / 4; ++d) v[k][d] = __ldcg(reinterpret_cast<const float4 *>(oc) + d);
+                    } else {
+#pragma unroll
+                      for (int d = 0; d < DPL; ++d) vs[k][d] = __ldcg(oc + d);
+                    }
+                  }
+                }
+#pragma unroll
+                for (uint32_t k = 0; k < MB; ++k) {
+                  const float wc = __shfl_sync(0xffffffffu, wl, (cb + k) & 31u);
+                  if (cb + k < nc) {
+                    if constexpr (DPL % 4 == 0) {
+#pragma unroll
+                      for (int d = 0; d < DPL / 4; ++d) {
+                        o[4 * d] = fmaf(wc, v[k][d].x, o[4 * d]);
+                        o[4 * d + 1] = fmaf(wc, v[k][d].y, o[4 * d + 1]);
+                        o[4 * d + 2] = fmaf(wc, v[k][d].z, o[4 * d + 2]);
+                        o[4 * d + 3] = fmaf(wc, v[k][d].w, o[4 * d + 3]);
+                      }
+                    } else {
+#pragma unroll
+                      for (int d = 0; d < DPL; ++d) o[d] = fmaf(wc, vs[k][d], o[d]);
+                    }
+                  }
+                }
+              }
+            }
+            const float inv = 1.0f / warp_sum(Lp);
+#pragma unroll
+            for (int d = 0; d < DPL; ++d) p.attn[((size_t)a.kvh * G + g0) * D + lane * DPL + d] = o[d] * inv;
+          }
+          if (cw == 0 && lane == 0) p.tickets[a.kvh] = 0;
+        }
+        named_bar(1, NCT);  // sQ / sS / sflags reuse by the next unit
+      }
+      arrive();
+    }
+
+    // ---- o_proj + residual: hid_b = hid_a + scale * O attn ----
+    mp = MvParams{};
+    mp.ctrl = p.ctrl;
+    mp.g = p.g_o;
+    mp.out = p.hid_b;
+    mp.resid = p.hid_a;
+    mp.alpha = p.res_scale;
+    {
+      const float *x = p.attn;
+      matvec(QT{}, MR{}, PC{}, ph0 + kPhO, Ly.o, p.g_o, mp, [&](uint32_t k) { return __ldcg(x + k); }, nullptr);
+    }
+    arrive();
+
+    // ---- gate/up + SwiGLU on RMSNorm(hid_b) ----
+    mp = MvParams{};
+    mp.ctrl = p.ctrl;
+    mp.g = p.g_gu;
+    mp.normw = Ly.ffn_norm;
+    mp.eps = p.eps;
+    mp.out = p.gate;
+    {
+      const float *x = p.hid_b;
+      matvec(QT{}, MS{}, PN{}, ph0 + kPhGu, Ly.gateup, p.g_gu, mp, [&](uint32_t k) { return __ldcg(x + k); },
+             nullptr);
+    }
+    arrive();
+
+    // ---- down + residual: hid_a = hid_b + scale * Down gate ----
+    mp = MvParams{};
+    mp.ctrl = p.ctrl;
+    mp.g = p.g_down;
+    mp.out = p.hid_a;
+    mp.resid = p.hid_b;
+    mp.alpha = p.res_scale;
+    {
+      const float *x = p.gate;
+      matvec(QT{}, MR{}, PC{}, ph0 + kPhDown, Ly.down, p.g_down, mp, [&](uint32_t k) { return __ldcg(x + k); },
+             nullptr);
+    }
+    arrive();
+  }
+
+  // ---- final RMSNorm (output) and the optional LM head ----
+  const uint32_t phf = nb;
+  const float *hx = p.hid_a;
+  auto hload = [&](uint32_t k) { return __ldcg(hx + k); };
+  if (p.want_logits) {
+    MvParams mp{};
+    mp.ctrl = p.ctrl;
+    mp.g = p.g_head;
+    mp.normw = p.out_norm;
+    mp.eps = p.eps;
+    mp.out = p.logits;
+    mp.alpha = p.logit_scale;
+    float *xo = blockIdx.x == 0 ? p.out : nullptr;
+    if (p.g_head.q8)
+      matvec(std::integral_constant<bool, true>{}, MP{}, PN{}, phf, p.head, p.g_head, mp, hload, xo);
+    else
+      matvec(std::integral_constant<bool, false>{}, MP{}, PN{}, phf, p.head, p.g_head, mp, hload, xo);
+  } else if (blockIdx.x == 0) {
+    mv_activation<Q8, Pro::RMSNORM>(p.H, p.g_qkv.nseg() * p.g_qkv.seg_cols(), p.out_norm, p.eps, aux, p.plane, scr,
+                                    cw, lane, hload, [&] { wait_phase(phf); }, p.out);
+  }
+  if (blockIdx.x == 0) {
+    named_bar(1, NCT);
+    if (cw == 0 && lane == 0) p.ctrl[kCtrlPos] = pos + 1u;
+  }
+}
+
+}  // namespace vg
