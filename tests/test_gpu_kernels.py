@@ -57,7 +57,7 @@ def test_matvec(dtype, rows, cols):
 def tile_offsets(rows, cols, q8):
     """Byte offsets of the segmented 16-row tile layout (mirror of TileGeom in kernels.cuh): a
     K-step of 16 rows x 32 bytes is four 8x16-byte matrices [rows 0-7 | rows 8-15] x [bytes 0-15 |
-    bytes 16-31]; 8 K-steps and then (Q8_0) their scales [K-step][row % 8][row / 8] per segment."""
+    bytes 16-31]; 8 K-steps and then (Q8_0) their scales [row % 8][K-step][row / 8] per segment."""
     step = 32 if q8 else 16
     seg_cols = 8 * step
     nseg = -(-cols // seg_cols)
@@ -70,7 +70,7 @@ def tile_offsets(rows, cols, q8):
     base = ((r // 16) * nseg + seg) * seg_bytes
     elem = base + (kk // step) * 512 + ((kb >> 4) * 2 + (tr >> 3)) * 128 + (tr & 7) * 16 + (kb & 15)
     b = np.arange(cols // 32)[None, :]
-    scale = ((r // 16) * nseg + b // 8) * seg_bytes + 4096 + (b % 8) * 32 + (tr & 7) * 4 + (tr >> 3) * 2
+    scale = ((r // 16) * nseg + b // 8) * seg_bytes + 4096 + (tr & 7) * 32 + (b % 8) * 4 + (tr >> 3) * 2
     return elem, scale, (-(-rows // 16)) * nseg * seg_bytes
 
 

@@ -55,8 +55,8 @@ constexpr uint32_t kCtrlWords = 16;
 // matrices [rows 0-7, bytes 0-15][rows 8-15, bytes 0-15][rows 0-7, bytes
 // 16-31][rows 8-15, bytes 16-31], which is the order ldmatrix.x4 delivers the
 // A fragment of mma m16n8k32 (s8) / m16n8k16 (f16) in. A segment is kSegSteps
-// K-steps, followed for Q8_0 by their fp16 block scales laid [K-step][row % 8]
-// [row / 8] (rows r and r+8 adjacent). A tile is its segments back to back and
+// K-steps, followed for Q8_0 by their fp16 block scales laid [row % 8]
+// [K-step][row / 8] (rows r and r+8 adjacent, a row pair's K-steps contiguous). A tile is its segments back to back and
 // the tiles of a matrix follow each other, so a run of tiles is one contiguous
 // byte range. Padding rows and columns are zero.
 struct TileGeom {
@@ -80,7 +80,7 @@ struct TileGeom {
   // byte offset of the fp16 scale of Q8_0 block b of row r
   __host__ __device__ uint64_t scale_off(uint32_t r, uint32_t b) const {
     const uint32_t tr = r % kTileRows;
-    return seg_base(r, b / kSegSteps) + kSegQsBytes + (b % kSegSteps) * 32u + (tr & 7u) * 4u + (tr >> 3) * 2u;
+    return seg_base(r, b / kSegSteps) + kSegQsBytes + (tr & 7u) * 32u + (b % kSegSteps) * 4u + (tr >> 3) * 2u;
   }
 };
 
@@ -121,10 +121,21 @@ struct MvSmem {
 };
 
 __host__ __device__ inline uint32_t mv_a_plane(uint32_t q8, uint32_t cols_pad) {
-  // planes are offset by 16 bytes modulo 128 so the 12 (Q8_0) or 8 (F16) lanes
-  // that load A fragments from different planes hit different banks
+  // planes are offset by 32 bytes modulo 128 so the 8-byte B-fragment loads of
+  // the 12 (Q8_0) or 8 (F16) lanes that read different planes hit different banks
   const uint32_t b = q8 ? cols_pad : cols_pad * 2u;
-  return ((b + 127u) & ~127u) + 16u;
+  return ((b + 127u) & ~127u) + 32u;
+}
+
+// Byte of activation element kk (0..31 of a Q8_0 block, or 0..15 of an F16
+// K-step in 2-byte units) inside its 32-byte K-step of a digit / half plane:
+// the order of the B fragment, so lane tq finds its b0 and b1 as one 8-byte
+// word at tq * 8.
+__device__ __forceinline__ uint32_t bfrag_byte_q8(uint32_t kk) {
+  return kk < 16u ? (kk >> 2) * 8u + (kk & 3u) : ((kk - 16u) >> 2) * 8u + 4u + (kk & 3u);
+}
+__device__ __forceinline__ uint32_t bfrag_half_f16(uint32_t kk) {
+  return kk < 8u ? (kk >> 1) * 4u + (kk & 1u) : ((kk - 8u) >> 1) * 4u + 2u + (kk & 1u);
 }
 __host__ __device__ inline uint32_t mv_a_bytes(uint32_t q8, uint32_t cols_pad) {
   const uint32_t pl = mv_a_plane(q8, cols_pad);
@@ -425,7 +436,7 @@ __device__ __forceinline__ void mv_activation(uint32_t C, uint32_t cols_pad, con
     // int8 digits and the per-block exponent (warp-collective per block)
     int8_t *d0p = reinterpret_cast<int8_t *>(areg), *d1p = d0p + plane, *d2p = d1p + plane;
     auto digits = [&](uint32_t j, float x) {
-      const uint32_t b = blk(j), k = b * 32u + lane;
+      const uint32_t b = blk(j);
       const uint32_t mb = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(x)));
       int e = 0, q0 = 0, q1 = 0, q2 = 0;
       const bool nz = block_exponent(mb, e);
@@ -437,9 +448,10 @@ __device__ __forceinline__ void mv_activation(uint32_t C, uint32_t cols_pad, con
         q1 = (int)f1;
         q2 = (int)rintf(r1);
       }
-      d0p[k] = (int8_t)q0;
-      d1p[k] = (int8_t)q1;
-      d2p[k] = (int8_t)q2;
+      const uint32_t o = b * 32u + bfrag_byte_q8(lane);
+      d0p[o] = (int8_t)q0;
+      d1p[o] = (int8_t)q1;
+      d2p[o] = (int8_t)q2;
       if (lane == 0) sx[b] = nz ? pow2f(e) : 0.f;
     };
     if (regs) {
@@ -474,10 +486,11 @@ __device__ __forceinline__ void mv_activation(uint32_t C, uint32_t cols_pad, con
     __half *hi = reinterpret_cast<__half *>(areg), *lo = reinterpret_cast<__half *>(areg + plane);
     auto halves = [&](uint32_t j, float x) {
       const uint32_t k = blk(j) * 32u + lane;
+      const uint32_t o = (k & ~15u) + bfrag_half_f16(k & 15u);  // element k of K-step k / 16
       const float v = x * inv;
       const __half h = __float2half_rn(v);
-      hi[k] = h;
-      lo[k] = __float2half_rn(v - __half2float(h));
+      hi[o] = h;
+      lo[o] = __float2half_rn(v - __half2float(h));
     };
     if (regs) {
 #pragma unroll
@@ -587,23 +600,20 @@ __device__ __forceinline__ void mv_consume(const MvRing &R, RingPos &rp, uint32_
 #pragma unroll
       for (uint32_t q = 0; q < 4; ++q) {
         ldmatrix_x4(a[q], sg + (sq + q) * kStepBytes + lane * 16u);
-        const uint32_t kg = ks0 + q;
-        if constexpr (Q8) {
-          b0[q] = *reinterpret_cast<const uint32_t *>(bplane + kg * 32u + tq * 4u) & bmask;
-          b1[q] = *reinterpret_cast<const uint32_t *>(bplane + kg * 32u + 16u + tq * 4u) & bmask;
-        } else {
-          b0[q] = *reinterpret_cast<const uint32_t *>(bplane + (kg * 16u + tq * 2u) * 2u) & bmask;
-          b1[q] = *reinterpret_cast<const uint32_t *>(bplane + (kg * 16u + 8u + tq * 2u) * 2u) & bmask;
-        }
+        // B fragment: one 8-byte word per lane per K-step (planes in B-fragment order)
+        const uint2 bw = *reinterpret_cast<const uint2 *>(bplane + (ks0 + q) * 32u + tq * 8u);
+        b0[q] = bw.x & bmask;
+        b1[q] = bw.y & bmask;
       }
       if constexpr (Q8) {
+        // the scales of rows gq and gq + 8 for the 4 K-steps, and the 4 blocks' 2^e
+        const uint4 wsv = *reinterpret_cast<const uint4 *>(sg + kSegQsBytes + gq * 32u + sq * 4u);
+        const float4 xsv = *reinterpret_cast<const float4 *>(sx + ks0);
+        const uint32_t wsw[4] = {wsv.x, wsv.y, wsv.z, wsv.w};
+        const float xs[4] = {xsv.x, xsv.y, xsv.z, xsv.w};
         __half2 ws[4];
-        float xs[4];
 #pragma unroll
-        for (uint32_t q = 0; q < 4; ++q) {
-          ws[q] = *reinterpret_cast<const __half2 *>(sg + kSegQsBytes + (sq + q) * 32u + gq * 4u);
-          xs[q] = sx[ks0 + q];
-        }
+        for (uint32_t q = 0; q < 4; ++q) ws[q] = *reinterpret_cast<const __half2 *>(&wsw[q]);
         int r[4][4];
 #pragma unroll
         for (uint32_t q = 0; q < 4; ++q) mma_s8(r[q], a[q], b0[q], b1[q], kMagicBits);

@@ -63,7 +63,7 @@ struct StepSmem {
     red = aux + ((p.a_bytes + 127u) & ~127u);
     layers = red + p.rb * kMvConsumers * kTileRows * 4u;
     scr = layers + p.n_layers * (uint32_t)sizeof(StepLayer);
-    total = scr + 512u;
+    total = scr + 1024u;
   }
 };
 
@@ -126,9 +126,10 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_step_kernel(const __grid
   uint8_t *aux = smem + L.aux;
   float *red = reinterpret_cast<float *>(smem + L.red);
   StepLayer *layers = reinterpret_cast<StepLayer *>(smem + L.layers);
-  float *scr = reinterpret_cast<float *>(smem + L.scr);                       // 64 floats
-  uint32_t *sflags = reinterpret_cast<uint32_t *>(smem + L.scr + 256u);      // 8 words
-  unsigned long long *sbase = reinterpret_cast<unsigned long long *>(smem + L.scr + 384u);
+  float *scr = reinterpret_cast<float *>(smem + L.scr);                                 // 64 floats
+  unsigned long long *sbase = reinterpret_cast<unsigned long long *>(smem + L.scr + 256u);
+  uint32_t *sflags = reinterpret_cast<uint32_t *>(smem + L.scr + 264u);                // 8 words
+  float *sML = reinterpret_cast<float *>(smem + L.scr + 320u);                         // [G <= 32][2]
 
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
   uint32_t *err = p.ctrl + kCtrlErr;
@@ -327,27 +328,27 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_step_kernel(const __grid
             }
           }
         };
-        for (uint32_t t = cw; t < a.len; t += 2u * kMvConsumers) {
-          const uint32_t t2 = t + kMvConsumers;
-          const bool two = t2 < a.len;
-          float kf[DPL], kg2[DPL];
-          kvec(kS + t * D, kf);
-          if (two) kvec(kS + t2 * D, kg2);
-          else
+        for (uint32_t gb = 0; gb < G; gb += 8) {
+          // this lane's dims of q for 8 heads of the group, in registers
+          float qr[8][DPL];
 #pragma unroll
-            for (int d = 0; d < DPL; ++d) kg2[d] = 0.f;
-          for (uint32_t gb = 0; gb < G; gb += 8) {
+          for (uint32_t i = 0; i < 8; ++i)
+#pragma unroll
+            for (int d = 0; d < DPL; ++d) qr[i][d] = gb + i < G ? sQ[(gb + i) * D + lane * DPL + d] : 0.f;
+          for (uint32_t t = cw; t < a.len; t += 2u * kMvConsumers) {
+            const uint32_t t2 = t + kMvConsumers;
+            const bool two = t2 < a.len;
+            float kf[DPL], kg2[DPL];
+            kvec(kS + t * D, kf);
+            kvec(kS + (two ? t2 : t) * D, kg2);
             float pa[8], pb[8];
 #pragma unroll
             for (uint32_t i = 0; i < 8; ++i) {
               float x = 0.f, y = 0.f;
-              if (gb + i < G) {
-                const float *qg = sQ + (gb + i) * D + lane * DPL;
 #pragma unroll
-                for (int d = 0; d < DPL; ++d) {
-                  x = fmaf(qg[d], kf[d], x);
-                  y = fmaf(qg[d], kg2[d], y);
-                }
+              for (int d = 0; d < DPL; ++d) {
+                x = fmaf(qr[i][d], kf[d], x);
+                y = fmaf(qr[i][d], kg2[d], y);
               }
               pa[i] = x;
               pb[i] = y;
@@ -361,7 +362,7 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_step_kernel(const __grid
           }
         }
         named_bar(1, NCT);
-        // chunk softmax and values (softmax.comp, attn_values.comp): warp per head
+        // chunk softmax (softmax.comp): warp per head; exp(s - m) replaces s
         for (uint32_t g0 = cw; g0 < G; g0 += kMvConsumers) {
           float *sg = sS + g0 * p.chunk;
           float m = -INFINITY;
@@ -374,28 +375,53 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_step_kernel(const __grid
             lsum += e;
           }
           lsum = warp_sum(lsum);
-          __syncwarp();
-          float o[DPL];
+          if (lane == 0) {
+            sML[2 * g0] = m;
+            sML[2 * g0 + 1] = lsum;
+          }
+        }
+        named_bar(1, NCT);
+        // values (attn_values.comp): warp w takes positions w, w + 8, ... for HB
+        // heads at a time, so every V row is read once; the warps' partial sums
+        // (HB * D floats each) meet in the K and V stage slots (free once read)
+        constexpr uint32_t HB = DPL >= 8 ? 4u : 8u;
+        for (uint32_t gb = 0; gb < G; gb += HB) {
+          float o[HB][DPL];
 #pragma unroll
-          for (int d = 0; d < DPL; ++d) o[d] = 0.f;
-#pragma unroll 8
-          for (uint32_t t = 0; t < a.len; ++t) {
-            const float pw = sg[t];
+          for (uint32_t i = 0; i < HB; ++i)
+#pragma unroll
+            for (int d = 0; d < DPL; ++d) o[i][d] = 0.f;
+          for (uint32_t t = cw; t < a.len; t += kMvConsumers) {
             float vf[DPL];
             kvec(vS + t * D, vf);
 #pragma unroll
-            for (int d = 0; d < DPL; ++d) o[d] = fmaf(pw, vf[d], o[d]);
-          }
-          const size_t slot_i = ((size_t)a.kvh * p.max_chunks + a.c) * G + g0;
-          float *dst = p.part + slot_i * D + lane * DPL;
-          if constexpr (DPL % 4 == 0) {
+            for (uint32_t i = 0; i < HB; ++i) {
+              const float pw = gb + i < G ? sS[(gb + i) * p.chunk + t] : 0.f;
 #pragma unroll
-            for (int d = 0; d < DPL; d += 4) *reinterpret_cast<float4 *>(dst + d) = make_float4(o[d], o[d + 1], o[d + 2], o[d + 3]);
-          } else {
-#pragma unroll
-            for (int d = 0; d < DPL; ++d) dst[d] = o[d];
+              for (int d = 0; d < DPL; ++d) o[i][d] = fmaf(pw, vf[d], o[i][d]);
+            }
           }
-          if (lane == 0) p.part_ml[slot_i] = make_float2(m, lsum);
+          named_bar(1, NCT);  // every warp is done with V (and K)
+          // warp w's partials: [w][HB][D] floats, warps 0-3 in the K slot, 4-7 in the V slot
+          float *wp = reinterpret_cast<float *>((cw < 4u ? reinterpret_cast<uint8_t *>(kS) : reinterpret_cast<uint8_t *>(vS))) +
+                      (cw & 3u) * HB * D;
+#pragma unroll
+          for (uint32_t i = 0; i < HB; ++i)
+#pragma unroll
+            for (int d = 0; d < DPL; ++d) wp[i * D + lane * DPL + d] = o[i][d];
+          named_bar(1, NCT);
+          for (uint32_t e = cw * 32u + lane; e < HB * D; e += NCT) {
+            const uint32_t i = e / D;
+            if (gb + i >= G) continue;
+            float v = 0.f;
+#pragma unroll
+            for (uint32_t w = 0; w < kMvConsumers; ++w)
+              v += reinterpret_cast<const float *>(w < 4u ? reinterpret_cast<const uint8_t *>(kS) : reinterpret_cast<const uint8_t *>(vS))[(w & 3u) * HB * D + e];
+            const size_t slot_i = ((size_t)a.kvh * p.max_chunks + a.c) * G + gb + i;
+            p.part[slot_i * D + e % D] = v;
+            if (e % D == 0) p.part_ml[slot_i] = make_float2(sML[2 * (gb + i)], sML[2 * (gb + i) + 1]);
+          }
+          named_bar(1, NCT);  // slots reused by the next head group
         }
         // release the K and V stages
         __syncwarp();
