@@ -289,11 +289,28 @@ def main():
         dist.all_reduce(t_e, op=dist.ReduceOp.MAX)
     e_ms_max = float(t_e.item())
 
-    # ---- per-kernel roofline: one instrumented step (events around every launch) ----
+    # ---- roofline of the dominant kernel ----
+    # Persistent mode (kernel_mode 1): the step is one kernel launch, so the dominant kernel is
+    # the step kernel itself: algorithmic bytes of a step / its device time (the events above
+    # bracket exactly the K launches). Per-kernel mode: gate_up from one instrumented step.
     roof = None
     peak, peak_kind = measured_peaks()
+    peak_src = f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)" if peak_kind == "measured" else "fallback 6650 GB/s"
+    mode = eng.kernel_mode
     prof = None
-    if not args.no_profile:
+    traffic = {}
+    tr = ROOT / "profiles" / "traffic.json"
+    if tr.exists():
+        traffic = json.loads(tr.read_text()).get(args.workload, {})
+    if mode == 1:
+        byt = int(sum(algorithmic_bytes(info, positions)) / K)
+        avg_ms = ms_max / K
+        ach = byt / (avg_ms * 1e-3) / 1e9
+        roof = {"kernel": "decode_step_kernel (persistent, the whole decode step)", "bound": "hbm",
+                "achieved": round(ach, 1), "peak": peak, "unit": "GB/s", "frac": round(ach / peak, 4),
+                "traffic": traffic.get("decode_step_kernel"), "bytes_per_launch": byt,
+                "avg_launch_ms": round(avg_ms, 5), "peak_source": peak_src}
+    elif not args.no_profile:
         eng.write_kv(kpre, vpre)
         for t in toks[:3]:
             eng.profile_step(int(t))       # warm
@@ -304,15 +321,8 @@ def main():
         byt = rows[0]["bytes"]
         ach = byt / (avg_ms * 1e-3) / 1e9
         roof = {"kernel": "gate_up (fused gate/up matvec + SwiGLU)", "bound": "hbm", "achieved": round(ach, 1),
-                "peak": peak, "unit": "GB/s", "frac": round(ach / peak, 4), "traffic": None,
-                "bytes_per_launch": byt, "avg_launch_ms": round(avg_ms, 5),
-                "peak_source": f"{peak_kind} hbm_gbs (MEASURED_PEAKS.json)" if peak_kind == "measured"
-                else "fallback 6650 GB/s"}
-        tr = ROOT / "profiles" / "traffic.json"
-        if tr.exists():
-            t = json.loads(tr.read_text()).get(args.workload, {}).get("gate_up")
-            if t:
-                roof["traffic"] = t
+                "peak": peak, "unit": "GB/s", "frac": round(ach / peak, 4), "traffic": traffic.get("gate_up"),
+                "bytes_per_launch": byt, "avg_launch_ms": round(avg_ms, 5), "peak_source": peak_src}
 
     # ---- whole-step numbers ----
     bytes_tok = algorithmic_bytes(info, positions)
@@ -341,7 +351,8 @@ def main():
         "roofline": roof,
         "e2e": {"value": round(e2e_val, 2), "unit": "tok/s", "steps": KE, "h2d_bytes_per_step": 4,
                 "d2h_bytes_per_step": info["embedding_length"] * 4 + 64},
-        "gpu_launches": K * (5 * info["block_count"] + 2),
+        "gpu_launches": K * (1 if mode == 1 else 5 * info["block_count"] + 2),
+        "kernel_mode": "persistent step kernel" if mode == 1 else "one kernel per projection / attention / norm",
         "clocks": clk,
     }
     if prof:

@@ -150,7 +150,9 @@ int vg_stream_position(const vg_stream *stream, uint32_t *position);
  * record_transformer, src/baselm.rs:892-1052). Chosen at vg_stream_create:
  * the persistent kernel needs one weight format for all projections and
  * cooperative launch; the environment variable VOXGEN_STEP_KERNEL=0 selects
- * the per-kernel program. */
+ * the per-kernel program, and VOXGEN_STEP_KERNEL=1 makes vg_stream_create
+ * fail with VG_EUNSUPPORTED (and the reason) when the persistent kernel
+ * cannot be used. */
 int vg_stream_kernel_mode(const vg_stream *stream, int *mode);
 /* The cudaStream_t every call of this stream is enqueued on. */
 int vg_stream_cuda_stream(const vg_stream *stream, void **cuda_stream);

@@ -597,19 +597,19 @@ StepFn pick_step_dpl(uint32_t head_dim) {
 // in by vg_stream_create). False when the model or the device does not fit it:
 // the projections must share one weight format, the device must support
 // cooperative launch, and one CTA with its plan must fit on an SM.
-bool plan_step(vg_stream *s) {
+std::string plan_step(vg_stream *s) {
   vg_model *m = s->m;
   const BaseLmConfig &c = m->cfg;
   const char *env = getenv("VOXGEN_STEP_KERNEL");
-  if (env && env[0] == '0') return false;
+  if (env && env[0] == '0') return "disabled by VOXGEN_STEP_KERNEL=0";
   const uint32_t type = m->layers[0].qkv.type;
   for (const Layer &L : m->layers)
     for (const DevMat *d : {&L.qkv, &L.o, &L.gateup, &L.down})
-      if (d->type != type) return false;
+      if (d->type != type) return "the projections do not share one weight format";
   const int dev = m->ctx->device;
   int coop = 0;
   CK(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev));
-  if (!coop) return false;
+  if (!coop) return "the device has no cooperative launch";
   const uint32_t D = c.head_dim, G = c.head_count / c.head_count_kv;
   StepParams &p = s->sp;
   p = StepParams{};
@@ -638,17 +638,17 @@ bool plan_step(vg_stream *s) {
   p.rb = rb;
   p.nst = 0;
   const uint32_t fixed = StepSmem(p).total;
-  if (fixed + 2u * (p.slot + 16u) > kSmemMax) return false;
+  if (fixed + 2u * (p.slot + 16u) > kSmemMax) return strf("shared-memory plan of %u bytes does not fit", fixed);
   p.nst = std::min<uint32_t>(16u, (kSmemMax - fixed) / (p.slot + 16u));
   s->step_smem = StepSmem(p).total;
   s->step_fn = type == GGML_Q8_0 ? pick_step_dpl<true>(D) : pick_step_dpl<false>(D);
-  if (!s->step_fn) return false;
+  if (!s->step_fn) return strf("head_dim %u", D);
   ensure_smem((const void *)s->step_fn, dev, s->step_smem);
   int per_sm = 0;
   CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, s->step_fn, kMvThreads, s->step_smem));
-  if (per_sm < 1) return false;
+  if (per_sm < 1) return strf("no CTA of %u threads with %u bytes of shared memory fits on an SM", kMvThreads, s->step_smem);
   s->step_grid = grid;
-  return true;
+  return "";
 }
 
 cudaError_t launch_step_kernel(vg_stream *s, bool token_input, bool logits) {
@@ -921,7 +921,11 @@ int vg_stream_create(vg_model *m, uint32_t max_context, vg_stream **out) {
     s->max_ctx = max_context;
     const uint32_t H = c.embedding_length, D = c.head_dim, G = c.head_count / c.head_count_kv;
     plan_attention(max_context, s->nsplit, s->chunk_cap);
-    s->use_step = plan_step(s);
+    const std::string why = plan_step(s);
+    s->use_step = why.empty();
+    const char *want = getenv("VOXGEN_STEP_KERNEL");
+    if (!s->use_step && want && want[0] == '1')
+      fail(VG_EUNSUPPORTED, "persistent step kernel required by VOXGEN_STEP_KERNEL=1 but unavailable: " + why);
     const uint32_t nch = s->use_step ? s->sp.max_chunks : 0u;
     const size_t kv_elems = (size_t)c.block_count * c.head_count_kv * max_context * D;
     CK(cudaMalloc(&s->kc, kv_elems * 2 * sizeof(__half)));

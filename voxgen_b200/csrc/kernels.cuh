@@ -359,40 +359,51 @@ __device__ __forceinline__ void mv_activation(uint32_t C, uint32_t cols_pad, con
   constexpr uint32_t NCT = kMvConsumers * 32;
   float *sx = reinterpret_cast<float *>(areg + 3u * plane);      // Q8: per-block 2^e
   float *xscale = reinterpret_cast<float *>(areg + 2u * plane);  // F16: 2^e of the whole vector
-  // Warp cw handles the 32-element blocks b with (b / 4) % 8 == cw, one
-  // element per lane, so a block's max is one redux. When a tile has a
-  // multiple of 4 segments (kStageSegs) these are exactly the Q8_0 K-steps
-  // that warp cw consumes in mv_consume, so no barrier is needed between the
-  // digits and the MMAs. Every activation load is issued up front (one round
-  // trip); the RMSNorm weight does not depend on the producer of the input
-  // and is loaded before the wait. Register path for up to 4096 (RMSNorm
+  // Warp cw handles the groups of 4 consecutive 32-element blocks b with
+  // (b / 4) % 8 == cw, i.e. 128 consecutive elements per group, 4 per lane:
+  // block q of a group is lanes 8q..8q+7, so a block's max takes 3 shuffles
+  // and each lane writes its 4 digits of a plane as one 32-bit word. When a
+  // tile has a multiple of 4 segments (kStageSegs) these are exactly the Q8_0
+  // K-steps that warp cw consumes in mv_consume, so no barrier is needed
+  // between the digits and the MMAs. Every activation load is issued up front
+  // (one round trip); the RMSNorm weight does not depend on the producer of the
+  // input and is loaded before the wait. Register path for up to 4096 (RMSNorm
   // inputs) or 6144 (copied inputs) columns.
-  constexpr uint32_t MAXJ = P == Pro::RMSNORM ? 16 : 24;
-  const uint32_t NBLK = cols_pad / 32u;
-  auto blk = [&](uint32_t j) { return ((j >> 2) * kMvConsumers + cw) * 4u + (j & 3u); };
-  const uint32_t J = (NBLK / 32u) * 4u + min(4u, (NBLK % 32u > cw * 4u) ? NBLK % 32u - cw * 4u : 0u);
-  float xr[MAXJ], wr[MAXJ];
-  const bool regs = (NBLK / 32u) * 4u + min(4u, NBLK % 32u) <= MAXJ;  // warp 0 has the most blocks
+  constexpr uint32_t MAXG = P == Pro::RMSNORM ? 4 : 6;
+  const uint32_t NGRP = (cols_pad / 32u + 3u) / 4u;                     // groups of 4 blocks
+  const uint32_t JG = NGRP > cw ? (NGRP - cw + kMvConsumers - 1) / kMvConsumers : 0u;  // groups of this warp
+  auto elem0 = [&](uint32_t g) { return (g * kMvConsumers + cw) * 128u + lane * 4u; };  // first element of lane
+  const bool regs = (NGRP + kMvConsumers - 1) / kMvConsumers <= MAXG;
+  auto load4 = [&](uint32_t k0, auto fetch) {
+    float4 v;
+    v.x = k0 < C ? fetch(k0) : 0.f;
+    v.y = k0 + 1u < C ? fetch(k0 + 1u) : 0.f;
+    v.z = k0 + 2u < C ? fetch(k0 + 2u) : 0.f;
+    v.w = k0 + 3u < C ? fetch(k0 + 3u) : 0.f;
+    return v;
+  };
+  float4 xr[MAXG], wr[MAXG];
   if constexpr (P == Pro::RMSNORM) {
 #pragma unroll
-    for (uint32_t j = 0; j < MAXJ; ++j) {
-      const uint32_t k = blk(j) * 32u + lane;
-      wr[j] = (regs && j < J && k < C) ? normw[k] : 0.f;
-    }
+    for (uint32_t g = 0; g < MAXG; ++g)
+      wr[g] = (regs && g < JG) ? load4(elem0(g), [&](uint32_t k) { return normw[k]; }) : make_float4(0.f, 0.f, 0.f, 0.f);
   }
   wait_input();
 #pragma unroll
-  for (uint32_t j = 0; j < MAXJ; ++j) {
-    const uint32_t k = blk(j) * 32u + lane;
-    xr[j] = (regs && j < J && k < C) ? xload(k) : 0.f;
-  }
+  for (uint32_t g = 0; g < MAXG; ++g)
+    xr[g] = (regs && g < JG) ? load4(elem0(g), xload) : make_float4(0.f, 0.f, 0.f, 0.f);
+  // RMSNorm (rmsnorm.comp:21-42, inversesqrt taken as 1/sqrt): x = h * inv_rms * w.
+  // Without xout the factor inv_rms is deferred: the operand is h * w and the
+  // consumer scales each output row by inv_rms (W (inv_rms h w) = inv_rms W (h w)),
+  // so the sum of squares needs no barrier here; this warp's partial goes to
+  // scr[8 + cw] for mv_consume. With xout the normalised x itself is formed.
+  const bool defer = P == Pro::RMSNORM && xout == nullptr;
   float inv_rms = 1.0f;
   if constexpr (P == Pro::RMSNORM) {
-    // rmsnorm.comp:21-42 (inversesqrt taken as 1/sqrt); x = h * inv_rms * w.
     float ss = 0.f;
     if (regs) {
 #pragma unroll
-      for (uint32_t j = 0; j < MAXJ; ++j) ss += xr[j] * xr[j];
+      for (uint32_t g = 0; g < MAXG; ++g) ss += xr[g].x * xr[g].x + xr[g].y * xr[g].y + xr[g].z * xr[g].z + xr[g].w * xr[g].w;
     } else {
       for (uint32_t i = cw * 32u + lane; i < C; i += NCT) {
         const float v = xload(i);
@@ -400,15 +411,24 @@ __device__ __forceinline__ void mv_activation(uint32_t C, uint32_t cols_pad, con
       }
     }
     ss = warp_sum(ss);
-    if (lane == 0) scr[cw] = ss;
-    named_bar(1, NCT);
-    float tot = 0.f;
+    if (defer) {
+      if (lane == 0) scr[8 + cw] = ss;
+    } else {
+      if (lane == 0) scr[cw] = ss;
+      named_bar(1, NCT);
+      float tot = 0.f;
 #pragma unroll
-    for (int w = 0; w < kMvConsumers; ++w) tot += scr[w];
-    inv_rms = 1.0f / sqrtf(tot / (float)C + eps);
+      for (int w = 0; w < kMvConsumers; ++w) tot += scr[w];
+      inv_rms = 1.0f / sqrtf(tot / (float)C + eps);
+    }
     if (regs) {
 #pragma unroll
-      for (uint32_t j = 0; j < MAXJ; ++j) xr[j] = __fmul_rn(__fmul_rn(xr[j], inv_rms), wr[j]);
+      for (uint32_t g = 0; g < MAXG; ++g) {
+        xr[g].x = __fmul_rn(__fmul_rn(xr[g].x, inv_rms), wr[g].x);
+        xr[g].y = __fmul_rn(__fmul_rn(xr[g].y, inv_rms), wr[g].y);
+        xr[g].z = __fmul_rn(__fmul_rn(xr[g].z, inv_rms), wr[g].z);
+        xr[g].w = __fmul_rn(__fmul_rn(xr[g].w, inv_rms), wr[g].w);
+      }
     }
   }
   // element k when the row is too long for the register path
@@ -418,61 +438,79 @@ __device__ __forceinline__ void mv_activation(uint32_t C, uint32_t cols_pad, con
     if constexpr (P == Pro::RMSNORM) return __fmul_rn(__fmul_rn(v, inv_rms), normw[k]);
     return v;
   };
-  if (xout) {
+  // f(g, v) for every group of this warp (register path fully unrolled)
+  auto each_group = [&](auto f) {
     if (regs) {
 #pragma unroll
-      for (uint32_t j = 0; j < MAXJ; ++j) {
-        const uint32_t k = blk(j) * 32u + lane;
-        if (j < J && k < C) xout[k] = xr[j];
-      }
+      for (uint32_t g = 0; g < MAXG; ++g)
+        if (g < JG) f(g, xr[g]);
     } else {
-      for (uint32_t j = 0; j < J; ++j) {
-        const uint32_t k = blk(j) * 32u + lane;
-        if (k < C) xout[k] = xglobal(k);
-      }
+      for (uint32_t g = 0; g < JG; ++g) f(g, load4(elem0(g), xglobal));
     }
+  };
+  if (xout) {
+    each_group([&](uint32_t g, const float4 &v) {
+      const uint32_t k0 = elem0(g);
+      if (k0 < C) xout[k0] = v.x;
+      if (k0 + 1u < C) xout[k0 + 1u] = v.y;
+      if (k0 + 2u < C) xout[k0 + 2u] = v.z;
+      if (k0 + 3u < C) xout[k0 + 3u] = v.w;
+    });
   }
   if constexpr (Q8) {
-    // int8 digits and the per-block exponent (warp-collective per block)
-    int8_t *d0p = reinterpret_cast<int8_t *>(areg), *d1p = d0p + plane, *d2p = d1p + plane;
-    auto digits = [&](uint32_t j, float x) {
-      const uint32_t b = blk(j);
-      const uint32_t mb = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(x)));
-      int e = 0, q0 = 0, q1 = 0, q2 = 0;
-      const bool nz = block_exponent(mb, e);
-      if (nz) {
-        const float v = x * pow2f(-e);  // exact, |v| < 64
-        const float f0 = rintf(v), r0 = (v - f0) * 128.0f;
-        const float f1 = rintf(r0), r1 = (r0 - f1) * 128.0f;
-        q0 = (int)f0;
-        q1 = (int)f1;
-        q2 = (int)rintf(r1);
-      }
-      const uint32_t o = b * 32u + bfrag_byte_q8(lane);
-      d0p[o] = (int8_t)q0;
-      d1p[o] = (int8_t)q1;
-      d2p[o] = (int8_t)q2;
-      if (lane == 0) sx[b] = nz ? pow2f(e) : 0.f;
+    // int8 digits and the per-block power of two 2^e: v = x * 2^-e (|v| < 64,
+    // exact), n = round(v * 2^14) through the 1.5 * 2^23 constant (for |t| <
+    // 2^22, t + 1.5 * 2^23 rounds t to an integer and its bit pattern minus
+    // 0x4B400000 is that integer), then n = d0 * 2^14 + d1 * 2^7 + d2 with
+    // every digit in [-64, 64] by integer shifts.
+    constexpr float kRnd = 12582912.0f;
+    constexpr int kRndBits = 0x4B400000;
+    auto split = [&](float x, float inv, int &q0, int &q1, int &q2) {
+      const int n = __float_as_int(fmaf(x * inv, 16384.0f, kRnd)) - kRndBits;
+      q0 = (n + 8192) >> 14;
+      const int r = n - (q0 << 14);
+      q1 = (r + 64) >> 7;
+      q2 = r - (q1 << 7);
     };
-    if (regs) {
+    auto digits = [&](uint32_t g, const float4 &v) {
+      // block of this lane: group block q = lane / 8; max over its 8 lanes
+      uint32_t mb = max(max(__float_as_uint(fabsf(v.x)), __float_as_uint(fabsf(v.y))),
+                        max(__float_as_uint(fabsf(v.z)), __float_as_uint(fabsf(v.w))));
+      mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, 1));
+      mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, 2));
+      mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, 4));
+      int e = 0;
+      const bool nz = block_exponent(mb, e);
+      int q[3][4] = {};
+      if (nz) {
+        const float inv = pow2f(-e);
+        split(v.x, inv, q[0][0], q[1][0], q[2][0]);
+        split(v.y, inv, q[0][1], q[1][1], q[2][1]);
+        split(v.z, inv, q[0][2], q[1][2], q[2][2]);
+        split(v.w, inv, q[0][3], q[1][3], q[2][3]);
+      }
+      const uint32_t k0 = elem0(g), b = k0 >> 5;
+      if (b * 32u < cols_pad) {
+        const uint32_t o = b * 32u + bfrag_byte_q8(k0 & 31u);  // 4 consecutive bytes
 #pragma unroll
-      for (uint32_t j = 0; j < MAXJ; ++j)
-        if (j < J) digits(j, xr[j]);
-    } else {
-      for (uint32_t j = 0; j < J; ++j) digits(j, xglobal(blk(j) * 32u + lane));
-    }
+        for (int d = 0; d < 3; ++d) {
+          const uint32_t w = __byte_perm(__byte_perm((uint32_t)q[d][0], (uint32_t)q[d][1], 0x0040u),
+                                         __byte_perm((uint32_t)q[d][2], (uint32_t)q[d][3], 0x0040u), 0x5410u);
+          *reinterpret_cast<uint32_t *>(areg + d * plane + o) = w;
+        }
+        if ((lane & 7u) == 0) sx[b] = nz ? pow2f(e) : 0.f;
+      }
+    };
+    each_group(digits);
     // each warp consumes only its own blocks when tiles have a multiple of 4 segments
     if ((cols_pad / (kSegSteps * 32u)) % kStageSegs != 0) named_bar(1, NCT);
     else __syncwarp();
   } else {
     // whole-vector power-of-two scale, then fp16 hi + lo
     float m = 0.f;
-    if (regs) {
-#pragma unroll
-      for (uint32_t j = 0; j < MAXJ; ++j) m = fmaxf(m, fabsf(xr[j]));
-    } else {
-      for (uint32_t j = 0; j < J; ++j) m = fmaxf(m, fabsf(xglobal(blk(j) * 32u + lane)));
-    }
+    each_group([&](uint32_t, const float4 &v) {
+      m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    });
     m = warp_max(m);
     named_bar(1, NCT);  // scr[] reuse after the RMSNorm reduction
     if (lane == 0) scr[cw] = m;
@@ -484,21 +522,21 @@ __device__ __forceinline__ void mv_activation(uint32_t C, uint32_t cols_pad, con
     const int e = ef < 20 ? 0 : (int)ef - 127 - 13;  // max|x| * 2^-e < 2^14
     const float inv = pow2f(-e);
     __half *hi = reinterpret_cast<__half *>(areg), *lo = reinterpret_cast<__half *>(areg + plane);
-    auto halves = [&](uint32_t j, float x) {
-      const uint32_t k = blk(j) * 32u + lane;
-      const uint32_t o = (k & ~15u) + bfrag_half_f16(k & 15u);  // element k of K-step k / 16
-      const float v = x * inv;
-      const __half h = __float2half_rn(v);
-      hi[o] = h;
-      lo[o] = __float2half_rn(v - __half2float(h));
-    };
-    if (regs) {
+    auto halves = [&](uint32_t g, const float4 &v4) {
+      const uint32_t k0 = elem0(g);
+      const float vv[4] = {v4.x, v4.y, v4.z, v4.w};
 #pragma unroll
-      for (uint32_t j = 0; j < MAXJ; ++j)
-        if (j < J) halves(j, xr[j]);
-    } else {
-      for (uint32_t j = 0; j < J; ++j) halves(j, xglobal(blk(j) * 32u + lane));
-    }
+      for (uint32_t i = 0; i < 4; ++i) {
+        const uint32_t k = k0 + i;
+        if (k >= cols_pad) continue;
+        const uint32_t o = (k & ~15u) + bfrag_half_f16(k & 15u);  // element k of K-step k / 16
+        const float v = vv[i] * inv;
+        const __half h = __float2half_rn(v);
+        hi[o] = h;
+        lo[o] = __float2half_rn(v - __half2float(h));
+      }
+    };
+    each_group(halves);
     if (cw == 0 && lane == 0) *xscale = pow2f(e);
     named_bar(1, NCT);
   }
@@ -514,7 +552,8 @@ template <bool Q8, Mode M>
 __device__ __forceinline__ void mv_consume(const MvRing &R, RingPos &rp, uint32_t n_items, uint32_t NSEG,
                                            uint32_t SEGB, const uint8_t *areg, uint32_t plane, float *red,
                                            const MvParams &p, uint32_t t0, uint32_t pos, uint32_t cw, uint32_t lane,
-                                           const uint32_t *abort_flag, uint32_t *err, bool &ok) {
+                                           const uint32_t *abort_flag, uint32_t *err, bool &ok,
+                                           const float *defer_ss) {
   constexpr uint32_t NCT = kMvConsumers * 32;
   const float *sx = reinterpret_cast<const float *>(areg + 3u * plane);
   const float *xscale = reinterpret_cast<const float *>(areg + 2u * plane);
@@ -644,6 +683,16 @@ __device__ __forceinline__ void mv_consume(const MvRing &R, RingPos &rp, uint32_
   if (ok && cur != 0xFFFFFFFFu) flush(cur);
   named_bar(1, NCT);  // every partial written
 
+  // Deferred RMSNorm (mv_activation without xout): the rows are scaled by
+  // 1/sqrt(sum of squares / C + eps), the warps' partial sums of squares being
+  // in defer_ss[0..7].
+  float row_scale = 1.0f;
+  if (defer_ss) {
+    float tot = 0.f;
+#pragma unroll
+    for (int w = 0; w < kMvConsumers; ++w) tot += defer_ss[w];
+    row_scale = 1.0f / sqrtf(tot / (float)p.g.cols + p.eps);
+  }
   // Tile reduction and epilogue: tile rel goes to warp rel % 8, lanes 0-7
   // take rows (l, l + 8), summing the 8 warps' partials in order.
   const uint32_t ntiles = (n_items + NSEG - 1) / NSEG;
@@ -655,7 +704,7 @@ __device__ __forceinline__ void mv_consume(const MvRing &R, RingPos &rp, uint32_
         a += red[(t * kMvConsumers + w) * kTileRows + lane];
         b += red[(t * kMvConsumers + w) * kTileRows + lane + 8u];
       }
-      mv_epilogue<M>(p, (t0 + t) * kTileRows + lane, a, b, pos);
+      mv_epilogue<M>(p, (t0 + t) * kTileRows + lane, a * row_scale, b * row_scale, pos);
     }
   }
 }
@@ -709,7 +758,8 @@ __global__ void __launch_bounds__(kMvThreads, 1) matvec_kernel(const __grid_cons
   const uint32_t pos = (M == Mode::QKV) ? p.ctrl[kCtrlPos] : 0u;
   bool ok = true;
   RingPos rp;
-  mv_consume<Q8, M>(R, rp, n_items, NSEG, SEGB, smem + L.a, p.plane, red, p, t0, pos, cw, lane, nullptr, err, ok);
+  mv_consume<Q8, M>(R, rp, n_items, NSEG, SEGB, smem + L.a, p.plane, red, p, t0, pos, cw, lane, nullptr, err, ok,
+                    P == Pro::RMSNORM ? scr + 8 : nullptr);
 }
 
 // ---------------------------------------------------------------------------

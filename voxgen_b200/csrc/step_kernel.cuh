@@ -111,6 +111,8 @@ __device__ __forceinline__ float embed_elem(const StepParams &p, uint32_t tok, u
   return __fmul_rn(v, p.emb_scale);
 }
 
+// One CTA of kMvThreads (9 warps) per SM. Three warps share one SM
+// sub-partition's 16K registers, so a thread may use at most 168.
 template <bool Q8, int DPL>
 __global__ void __launch_bounds__(kMvThreads, 1) decode_step_kernel(const __grid_constant__ StepParams p) {
   constexpr uint32_t NCT = kMvConsumers * 32;
@@ -234,7 +236,7 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_step_kernel(const __grid
     mv_activation<WQ8, P>(g.cols, NSEG * g.seg_cols(), mp.normw, mp.eps, aux, p.plane, scr, cw, lane, xload,
                           [&] { wait_phase(ph); }, xout);
     mv_consume<WQ8, M>(R, rp, (t1 - t0) * NSEG, NSEG, SEGB, aux, p.plane, red, mp, t0, pos, cw, lane, err, err,
-                       ok);
+                       ok, (P == Pro::RMSNORM && xout == nullptr) ? scr + 8 : nullptr);
     (void)w;
   };
   using QT = std::integral_constant<bool, Q8>;
@@ -319,22 +321,51 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_step_kernel(const __grid
         auto kvec = [&](const __half *row, float (&f)[DPL]) {
           if constexpr (DPL == 1) {
             f[0] = __half2float(row[lane]);
+          } else if constexpr (DPL == 2) {
+            const float2 v = __half22float2(*reinterpret_cast<const __half2 *>(row + lane * 2));
+            f[0] = v.x;
+            f[1] = v.y;
           } else {
 #pragma unroll
-            for (int d = 0; d < DPL; d += 2) {  // lane * DPL is even: 4-byte aligned pairs
-              const float2 v = __half22float2(*reinterpret_cast<const __half2 *>(row + lane * DPL + d));
+            for (int d = 0; d < DPL; d += 4) {  // 8-byte aligned groups of 4 halves
+              const uint2 w = *reinterpret_cast<const uint2 *>(row + lane * DPL + d);
+              const float2 lo = __half22float2(*reinterpret_cast<const __half2 *>(&w.x));
+              const float2 hi = __half22float2(*reinterpret_cast<const __half2 *>(&w.y));
+              f[d] = lo.x;
+              f[d + 1] = lo.y;
+              f[d + 2] = hi.x;
+              f[d + 3] = hi.y;
+            }
+          }
+        };
+        // DPL consecutive floats at p (16-byte aligned when DPL % 4 == 0)
+        auto ld_f = [&](const float *src, float (&f)[DPL]) {
+          if constexpr (DPL % 4 == 0) {
+#pragma unroll
+            for (int d = 0; d < DPL; d += 4) {
+              const float4 v = *reinterpret_cast<const float4 *>(src + d);
               f[d] = v.x;
               f[d + 1] = v.y;
+              f[d + 2] = v.z;
+              f[d + 3] = v.w;
             }
+          } else {
+#pragma unroll
+            for (int d = 0; d < DPL; ++d) f[d] = src[d];
           }
         };
         for (uint32_t gb = 0; gb < G; gb += 8) {
           // this lane's dims of q for 8 heads of the group, in registers
           float qr[8][DPL];
 #pragma unroll
-          for (uint32_t i = 0; i < 8; ++i)
+          for (uint32_t i = 0; i < 8; ++i) {
+            if (gb + i < G) {
+              ld_f(sQ + (gb + i) * D + lane * DPL, qr[i]);
+            } else {
 #pragma unroll
-            for (int d = 0; d < DPL; ++d) qr[i][d] = gb + i < G ? sQ[(gb + i) * D + lane * DPL + d] : 0.f;
+              for (int d = 0; d < DPL; ++d) qr[i][d] = 0.f;
+            }
+          }
           for (uint32_t t = cw; t < a.len; t += 2u * kMvConsumers) {
             const uint32_t t2 = t + kMvConsumers;
             const bool two = t2 < a.len;
@@ -406,9 +437,17 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_step_kernel(const __grid
           float *wp = reinterpret_cast<float *>((cw < 4u ? reinterpret_cast<uint8_t *>(kS) : reinterpret_cast<uint8_t *>(vS))) +
                       (cw & 3u) * HB * D;
 #pragma unroll
-          for (uint32_t i = 0; i < HB; ++i)
+          for (uint32_t i = 0; i < HB; ++i) {
+            float *dst = wp + i * D + lane * DPL;
+            if constexpr (DPL % 4 == 0) {
 #pragma unroll
-            for (int d = 0; d < DPL; ++d) wp[i * D + lane * DPL + d] = o[i][d];
+              for (int d = 0; d < DPL; d += 4)
+                *reinterpret_cast<float4 *>(dst + d) = make_float4(o[i][d], o[i][d + 1], o[i][d + 2], o[i][d + 3]);
+            } else {
+#pragma unroll
+              for (int d = 0; d < DPL; ++d) dst[d] = o[i][d];
+            }
+          }
           named_bar(1, NCT);
           for (uint32_t e = cw * 32u + lane; e < HB * D; e += NCT) {
             const uint32_t i = e / D;
