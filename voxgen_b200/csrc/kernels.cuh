@@ -22,6 +22,7 @@
 // fp32. For F16 weights x is scaled by a power of two and split into fp16
 // hi + lo, accumulated in fp32 by m16n8k16.
 #pragma once
+#include <type_traits>
 #include <cuda_fp16.h>
 
 #include <cstdint>
@@ -310,7 +311,7 @@ struct RingPos {
 // has been released, then announces `bytes` for it. False when the wait gave up.
 __device__ __forceinline__ bool ring_claim(const MvRing &R, const RingPos &rp, uint32_t bytes,
                                            const uint32_t *abort_flag, uint32_t *err) {
-  if (rp.n >= R.nst && !mbar_wait_bounded(&R.empty[rp.slot], rp.phase ^ 1u, abort_flag)) {
+  if (rp.n >= R.nst && !mbar_wait_backoff(&R.empty[rp.slot], rp.phase ^ 1u, abort_flag)) {
     set_error(err, kErrConsumerWait);
     return false;
   }
@@ -576,6 +577,7 @@ __device__ __forceinline__ void mv_consume(const MvRing &R, RingPos &rp, uint32_
   constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
   const float lane_scale = Q8 ? (tq == 0 ? 1.f : tq == 1 ? 6.103515625e-05f : 0.f) : (tq == 0 ? 1.f : 0.f);
   float acc0 = 0.f, acc1 = 0.f;
+  float acc0b = 0.f, acc1b = 0.f;  // Q8_0: second chain when two stages are processed together
   float cf[2][4] = {};  // F16: two accumulator chains
 
   // This warp's partial of one tile: after the tq reduction, lane (gq, 0)
@@ -583,8 +585,8 @@ __device__ __forceinline__ void mv_consume(const MvRing &R, RingPos &rp, uint32_
   auto flush = [&](uint32_t rel) {
     float v0, v1;
     if constexpr (Q8) {
-      v0 = acc0 * lane_scale;
-      v1 = acc1 * lane_scale;
+      v0 = (acc0 + acc0b) * lane_scale;
+      v1 = (acc1 + acc1b) * lane_scale;
     } else {
       v0 = (cf[0][0] + cf[0][1] + cf[1][0] + cf[1][1]) * lane_scale;
       v1 = (cf[0][2] + cf[0][3] + cf[1][2] + cf[1][3]) * lane_scale;
@@ -601,7 +603,7 @@ __device__ __forceinline__ void mv_consume(const MvRing &R, RingPos &rp, uint32_
       red[(rel * kMvConsumers + cw) * kTileRows + gq] = v0;
       red[(rel * kMvConsumers + cw) * kTileRows + gq + 8u] = v1;
     }
-    acc0 = acc1 = 0.f;
+    acc0 = acc1 = acc0b = acc1b = 0.f;
 #pragma unroll
     for (int a = 0; a < 2; ++a)
 #pragma unroll
@@ -621,63 +623,107 @@ __device__ __forceinline__ void mv_consume(const MvRing &R, RingPos &rp, uint32_
     ++rel;
   }
   uint32_t cur = 0xFFFFFFFFu;  // tile (relative) of the accumulated partial
-  for (uint32_t s = 0; s < n_items && ok; s += kStageSegs) {
-    if (!mbar_wait_bounded(&R.full[rp.slot], rp.phase, abort_flag)) {
-      set_error(err, kErrConsumerWait);
-      ok = false;
-      break;
-    }
-    if (i < n_items) {
-      if (rel != cur) {
-        if (cur != 0xFFFFFFFFu) flush(cur);
-        cur = rel;
-      }
-      const uint8_t *sg = R.ring + rp.slot * R.slot + (cw >> 1) * SEGB;
-      const uint32_t ks0 = seg * kSegSteps + sq;  // K-step index in the row
-      // all shared-memory loads first, then 4 independent MMAs, then the rescale
-      uint32_t a[4][4], b0[4], b1[4];
+  // K-steps of NB stages (segment bases sgs, first K-steps kss): all
+  // shared-memory loads first, then the NB * 4 independent MMAs, then the rescale
+  auto run = [&](auto nbc, const uint8_t *const (&sgs)[2], const uint32_t (&kss)[2]) {
+    constexpr int NB = decltype(nbc)::value;
+    uint32_t a[NB][4][4], b0[NB][4], b1[NB][4];
+#pragma unroll
+    for (int nb = 0; nb < NB; ++nb)
 #pragma unroll
       for (uint32_t q = 0; q < 4; ++q) {
-        ldmatrix_x4(a[q], sg + (sq + q) * kStepBytes + lane * 16u);
+        ldmatrix_x4(a[nb][q], sgs[nb] + (sq + q) * kStepBytes + lane * 16u);
         // B fragment: one 8-byte word per lane per K-step (planes in B-fragment order)
-        const uint2 bw = *reinterpret_cast<const uint2 *>(bplane + (ks0 + q) * 32u + tq * 8u);
-        b0[q] = bw.x & bmask;
-        b1[q] = bw.y & bmask;
+        const uint2 bw = *reinterpret_cast<const uint2 *>(bplane + (kss[nb] + q) * 32u + tq * 8u);
+        b0[nb][q] = bw.x & bmask;
+        b1[nb][q] = bw.y & bmask;
       }
-      if constexpr (Q8) {
-        // the scales of rows gq and gq + 8 for the 4 K-steps, and the 4 blocks' 2^e
-        const uint4 wsv = *reinterpret_cast<const uint4 *>(sg + kSegQsBytes + gq * 32u + sq * 4u);
-        const float4 xsv = *reinterpret_cast<const float4 *>(sx + ks0);
-        const uint32_t wsw[4] = {wsv.x, wsv.y, wsv.z, wsv.w};
-        const float xs[4] = {xsv.x, xsv.y, xsv.z, xsv.w};
-        __half2 ws[4];
+    if constexpr (Q8) {
+      // the scales of rows gq and gq + 8 for the 4 K-steps, and the 4 blocks' 2^e
+      uint4 wsv[NB];
+      float4 xsv[NB];
 #pragma unroll
-        for (uint32_t q = 0; q < 4; ++q) ws[q] = *reinterpret_cast<const __half2 *>(&wsw[q]);
-        int r[4][4];
+      for (int nb = 0; nb < NB; ++nb) {
+        wsv[nb] = *reinterpret_cast<const uint4 *>(sgs[nb] + kSegQsBytes + gq * 32u + sq * 4u);
+        xsv[nb] = *reinterpret_cast<const float4 *>(sx + kss[nb]);
+      }
+      int r[NB][4][4];
 #pragma unroll
-        for (uint32_t q = 0; q < 4; ++q) mma_s8(r[q], a[q], b0[q], b1[q], kMagicBits);
+      for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+        for (uint32_t q = 0; q < 4; ++q) mma_s8(r[nb][q], a[nb][q], b0[nb][q], b1[nb][q], kMagicBits);
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb) {
+        const uint32_t wsw[4] = {wsv[nb].x, wsv[nb].y, wsv[nb].z, wsv[nb].w};
+        const float xs[4] = {xsv[nb].x, xsv[nb].y, xsv[nb].z, xsv[nb].w};
+        float &A0 = nb == 0 ? acc0 : acc0b, &A1 = nb == 0 ? acc1 : acc1b;
 #pragma unroll
         for (uint32_t q = 0; q < 4; ++q) {
-          const float2 w = __half22float2(ws[q]);
-          const float v0 = fmaf(__int_as_float(r[q][1]) - kMagic, 0.0078125f, __int_as_float(r[q][0]) - kMagic);
-          const float v1 = fmaf(__int_as_float(r[q][3]) - kMagic, 0.0078125f, __int_as_float(r[q][2]) - kMagic);
-          acc0 = fmaf(v0, w.x * xs[q], acc0);
-          acc1 = fmaf(v1, w.y * xs[q], acc1);
+          const float2 w = __half22float2(*reinterpret_cast<const __half2 *>(&wsw[q]));
+          const float v0 = fmaf(__int_as_float(r[nb][q][1]) - kMagic, 0.0078125f, __int_as_float(r[nb][q][0]) - kMagic);
+          const float v1 = fmaf(__int_as_float(r[nb][q][3]) - kMagic, 0.0078125f, __int_as_float(r[nb][q][2]) - kMagic);
+          A0 = fmaf(v0, w.x * xs[q], A0);
+          A1 = fmaf(v1, w.y * xs[q], A1);
         }
-      } else {
-#pragma unroll
-        for (uint32_t q = 0; q < 4; ++q) mma_f16(cf[q & 1], a[q], b0[q], b1[q]);
       }
+    } else {
+#pragma unroll
+      for (int nb = 0; nb < NB; ++nb)
+#pragma unroll
+        for (uint32_t q = 0; q < 4; ++q) mma_f16(cf[q & 1], a[nb][q], b0[nb][q], b1[nb][q]);
     }
-    // release the stage
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&R.empty[rp.slot]);
+  };
+  auto advance = [&] {
     rp.next(R.nst);
     i += kStageSegs;
     seg += kStageSegs;
     while (seg >= NSEG) {
       seg -= NSEG;
       ++rel;
+    }
+  };
+  for (uint32_t s = 0; s < n_items && ok; s += kStageSegs) {
+    const uint32_t slot0 = rp.slot;
+    if (!mbar_wait_bounded(&R.full[slot0], rp.phase, abort_flag)) {
+      set_error(err, kErrConsumerWait);
+      ok = false;
+      break;
+    }
+    // Two stages at once when this warp's segment of the next stage continues
+    // the same tile: twice the work per wait, and the two batches overlap.
+    const bool pair = i < n_items && i + kStageSegs < n_items && seg + kStageSegs < NSEG;
+    if (i < n_items) {
+      if (rel != cur) {
+        if (cur != 0xFFFFFFFFu) flush(cur);
+        cur = rel;
+      }
+      const uint32_t ks0 = seg * kSegSteps + sq;  // K-step index in the row
+      const uint8_t *sg0 = R.ring + slot0 * R.slot + (cw >> 1) * SEGB;
+      if (pair) {
+        RingPos nx = rp;
+        nx.next(R.nst);
+        if (!mbar_wait_bounded(&R.full[nx.slot], nx.phase, abort_flag)) {
+          set_error(err, kErrConsumerWait);
+          ok = false;
+          break;
+        }
+        const uint8_t *const sgs[2] = {sg0, R.ring + nx.slot * R.slot + (cw >> 1) * SEGB};
+        const uint32_t kss[2] = {ks0, ks0 + kStageSegs * kSegSteps};
+        run(std::integral_constant<int, 2>{}, sgs, kss);
+      } else {
+        const uint8_t *const sgs[2] = {sg0, sg0};
+        const uint32_t kss[2] = {ks0, ks0};
+        run(std::integral_constant<int, 1>{}, sgs, kss);
+      }
+    }
+    // release the stage (or both)
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&R.empty[slot0]);
+    advance();
+    if (pair) {
+      if (lane == 0) mbar_arrive(&R.empty[rp.slot]);
+      advance();
+      s += kStageSegs;
     }
   }
   if (ok && cur != 0xFFFFFFFFu) flush(cur);

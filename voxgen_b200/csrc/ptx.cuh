@@ -84,6 +84,24 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
   return false;
 }
 
+// The same wait with a short sleep between polls, for a thread that is not on
+// the critical path (the producer waiting for a free ring slot): it then
+// leaves the issue slots of its SM sub-partition to the consumer warps.
+__device__ __forceinline__ bool mbar_wait_backoff(uint64_t *bar, uint32_t parity,
+                                                  const uint32_t *abort_flag = nullptr) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer();
+  for (uint32_t it = 0; it < kWaitMaxIters; ++it) {
+    __nanosleep(128);
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 15u) == 15u) {
+      if (globaltimer() - t0 > kWaitLimitNs) return false;
+      if (abort_flag && ld_volatile_u32(abort_flag)) return false;
+    }
+  }
+  return false;
+}
+
 // Grid-wide barrier over a monotonically increasing 64-bit arrival counter:
 // grid_arrive adds one arrival with release semantics at GPU scope (the
 // caller first synchronises the arriving threads of its CTA); grid_wait spins
