@@ -56,10 +56,8 @@ def parse():
 
 
 def dist_env():
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    local = int(os.environ.get("LOCAL_RANK", str(rank)))
-    return rank, world, local
+    from voxgen_b200 import replicas
+    return replicas.env()
 
 
 def model_cache() -> Path:
@@ -211,20 +209,15 @@ def main():
         return
 
     import torch
-    import torch.distributed as dist
 
-    from voxgen_b200 import api, synth
+    from voxgen_b200 import api, replicas, synth
 
     torch.cuda.set_device(local)
-    pg = None
-    if world > 1:
-        from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=600), device_id=torch.device("cuda", local))
-        pg = dist.group.WORLD
+    dev = torch.device("cuda", local)
+    pg = replicas.init("nccl", world, timeout_s=600, device=dev)
 
     def barrier():
-        if pg is not None:
-            dist.barrier()
+        replicas.barrier(pg)
 
     wl = WORKLOADS[args.workload]
     spec = synth.preset(wl["preset"])
@@ -260,10 +253,7 @@ def main():
     barrier()
     clk = clocks.stop()
     ms = start.elapsed_time(end)
-    t_max = torch.tensor([ms], dtype=torch.float64, device="cuda")
-    if pg is not None:
-        dist.all_reduce(t_max, op=dist.ReduceOp.MAX)
-    ms_max = float(t_max.item())
+    ms_max = replicas.max_over_ranks(ms, pg, dev)
     positions = list(range(p0, p0 + K))
 
     # ---- e2e through the C ABI with host buffers ----
@@ -284,10 +274,7 @@ def main():
     torch.cuda.synchronize()
     barrier()
     e_ms = e_start.elapsed_time(e_end)
-    t_e = torch.tensor([e_ms], dtype=torch.float64, device="cuda")
-    if pg is not None:
-        dist.all_reduce(t_e, op=dist.ReduceOp.MAX)
-    e_ms_max = float(t_e.item())
+    e_ms_max = replicas.max_over_ranks(e_ms, pg, dev)
 
     # ---- roofline of the dominant kernel ----
     # Persistent mode (kernel_mode 1): the step is one kernel launch, so the dominant kernel is
@@ -329,8 +316,8 @@ def main():
     emb_row = info["embedding_length"] * 2
     avg_bytes = (sum(bytes_tok) / K) + emb_row
     step_ms = ms_max / K
-    value = world * K / (ms_max / 1e3)
-    e2e_val = world * KE / (e_ms_max / 1e3)
+    value = replicas.aggregate_rate(K, world, ms_max)
+    e2e_val = replicas.aggregate_rate(KE, world, e_ms_max)
     line = {
         "metric": "decode tok/s", "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": K,
         "warmup": W, "ms_per_step": round(step_ms, 5), "higher_is_better": True, "scaling": "weak",
@@ -372,9 +359,8 @@ def main():
     ctx.close()
     if rank == 0:
         print(json.dumps(line), flush=True)
-    if pg is not None:
-        dist.barrier()
-        dist.destroy_process_group()
+    replicas.barrier(pg)
+    replicas.shutdown(pg)
 
 
 if __name__ == "__main__":
