@@ -6,6 +6,7 @@ Workloads (seeded synthetic models):
                   KV prefilled to 1023 positions, decoding towards a 4096 context
   cfg3            cfg2 with F16 projections
   cfg1            24 layers at H=1024 (config[0]'s layer), F16 token table, 128-token prefill
+  cfg0            config[0]: one layer at H=1024, 512 prior positions
 
 A step is one decode token of one stream. `value` is the whole-job aggregate tok/s over all
 GPUs (independent replicas, weights replicated, no collectives on the data path), device-timed
@@ -38,6 +39,7 @@ WORKLOADS = {
     "cfg2": dict(preset="cfg2", prefill=1023, ctx=4096, desc="BaseLM 28L H2048 16x128 GQA 2 KV F6144 Q8_0"),
     "cfg3": dict(preset="cfg3", prefill=1023, ctx=4096, desc="BaseLM 28L H2048 16x128 GQA 2 KV F6144 F16"),
     "cfg1": dict(preset="cfg1", prefill=128, ctx=512, desc="BaseLM 24L H1024 16x64 GQA 2 KV F4096 Q8_0"),
+    "cfg0": dict(preset="cfg0", prefill=512, ctx=1024, desc="one BaseLM layer H1024 16x64 GQA 2 KV F4096 Q8_0"),
 }
 
 

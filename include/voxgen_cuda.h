@@ -224,11 +224,13 @@ int vg_stream_profile_step(vg_stream *stream, uint32_t token, int want_logits,
                            vg_kernel_time *out, uint32_t capacity, uint32_t *n_out);
 
 /* ---- multi-stream step --------------------------------------------------- */
-/* One decode step for n streams of the same model in one batched launch
- * sequence (weights read once for all n tokens). tokens[i] feeds streams[i].
- * Each stream advances by one position. n <= 16. The reference serialises
- * independent engines behind a Mutex (src/runtime.rs:177); this is the
- * batched replacement. */
+/* One decode step (decode_token_gpu_only semantics, no logits) for n distinct
+ * streams of the same model: tokens[i] feeds streams[i] and each stream
+ * advances by one position. n <= 16. Every argument is checked before any
+ * stream is advanced. The steps are enqueued on the streams' own CUDA streams
+ * (asynchronous, like vg_decode_token); each reads the weights once, i.e. the
+ * weight pass is not yet shared between streams. The reference serialises
+ * independent engines behind a Mutex (src/runtime.rs:177). */
 int vg_decode_batch(vg_stream *const *streams, int n, const uint32_t *tokens);
 
 /* ---- kernel-level entry points (parity tests and integration) ----------- */

@@ -219,3 +219,34 @@ def test_backbone_long_context(ctx, model_dir, name):
         p.eng.decode_embedding_gpu_only(hs[3])
     assert e.value.code == -6
     p.close()
+
+
+def test_decode_batch_matches_single_streams(ctx, model_dir):
+    """vg_decode_batch: every stream advances as if decoded alone (ragged positions)."""
+    spec = synth.preset("tiny")
+    path = spec_path(model_dir, "tiny")
+    m = api.Model(ctx, path)
+    engines = [api.BaseLmEngine(m, 64) for _ in range(3)]
+    solo = [api.BaseLmEngine(m, 64) for _ in range(3)]
+    for i, (e, s) in enumerate(zip(engines, solo)):
+        k, v = synth.kv_prefill(spec, 5 + 7 * i, seed_index=1100 + i)
+        e.write_kv(k, v)
+        s.write_kv(k, v)
+    toks = synth.token_ids(spec, 12).reshape(4, 3)
+    for row in toks:
+        api.decode_batch(engines, [int(t) for t in row])
+        for s, t in zip(solo, row):
+            s.decode_token_gpu_only(int(t))
+    for e, s in zip(engines, solo):
+        assert e.position == s.position
+        assert np.array_equal(e.output(), s.output())
+    with pytest.raises(api.VoxGenError) as err:
+        api.decode_batch([engines[0], engines[0]], [1, 2])
+    assert err.value.code == -1
+    with pytest.raises(api.VoxGenError) as err:
+        api.decode_batch(engines, [1, spec.vocab, 2])
+    assert err.value.code == -5
+    assert [e.position for e in engines] == [s.position for s in solo], "a failed batch advanced a stream"
+    for e in engines + solo:
+        e.close()
+    m.close()

@@ -1348,8 +1348,30 @@ int vg_decode_batch(vg_stream *const *streams, int n, const uint32_t *tokens) {
   if (!streams || !tokens || n <= 0 || n > 16) return VG_EINVAL;
   for (int i = 0; i < n; ++i)
     if (!live(streams[i])) return VG_ESTATE;
-  set_err(streams[0]->m->ctx, "vg_decode_batch is not implemented yet");
-  return VG_EUNSUPPORTED;
+  vg_model *m = streams[0]->m;
+  return guard(m->ctx, [&] {
+    // all streams are checked before any is advanced, so a failure leaves every position unchanged
+    std::set<const vg_stream *> seen;
+    for (int i = 0; i < n; ++i) {
+      vg_stream *s = streams[i];
+      if (s->m != m) fail(VG_EINVAL, "vg_decode_batch: streams of different models");
+      if (!seen.insert(s).second) fail(VG_EINVAL, "vg_decode_batch: a stream appears twice");
+      if (tokens[i] >= m->cfg.vocab_size)
+        fail(VG_ERANGE, strf("token id %u is outside vocabulary 0..%u", tokens[i], m->cfg.vocab_size));
+      check_step(s);
+    }
+    CK(cudaSetDevice(m->ctx->device));
+    // one step per stream, each on its own CUDA stream (the weights are read once per stream)
+    for (int i = 0; i < n; ++i) {
+      vg_stream *s = streams[i];
+      uint8_t *slot = staging_slot(s);
+      std::memcpy(slot, &tokens[i], 4);
+      CK(cudaMemcpyAsync(s->ctrl + kCtrlToken, slot, 4, cudaMemcpyHostToDevice, s->st));
+      CK(cudaEventRecord(staging_event(s), s->st));
+      launch_step(s, true, false);
+    }
+    return VG_OK;
+  });
 }
 
 // ---- kernel-level entry points --------------------------------------------
