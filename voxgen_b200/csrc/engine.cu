@@ -280,6 +280,8 @@ struct vg_stream {
   StepParams sp{};           // token_input / want_logits set per launch
   void (*step_fn)(StepParams) = nullptr;
   uint32_t step_smem = 0, step_grid = 0;
+  bool step_head_apart = false;  // the LM head is stored in another format: own launch after the step
+  MvPlan step_head{};
 };
 
 namespace {
@@ -623,7 +625,10 @@ std::string plan_step(vg_stream *s) {
   p.n_layers = c.block_count;
   const uint32_t grid = (uint32_t)m->ctx->sms;
   uint32_t segb = 0, plane = 0, cpad = 0, rb = 1;
+  s->step_head_apart = m->out.type != type;
+  if (s->step_head_apart) s->step_head = plan_matvec<Mode::PLAIN, Pro::COPY>(m->out, dev, (uint32_t)m->ctx->sms);
   for (const TileGeom *g : {&p.g_qkv, &p.g_o, &p.g_gu, &p.g_down, &p.g_head}) {
+    if (g == &p.g_head && s->step_head_apart) continue;
     segb = std::max(segb, g->seg_bytes());
     const uint32_t cp = g->nseg() * g->seg_cols();
     cpad = std::max(cpad, cp);
@@ -654,7 +659,7 @@ std::string plan_step(vg_stream *s) {
 cudaError_t launch_step_kernel(vg_stream *s, bool token_input, bool logits) {
   StepParams p = s->sp;
   p.token_input = token_input;
-  p.want_logits = logits;
+  p.want_logits = logits && !s->step_head_apart;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(s->step_grid);
   cfg.blockDim = dim3(kMvThreads);
@@ -665,7 +670,9 @@ cudaError_t launch_step_kernel(vg_stream *s, bool token_input, bool logits) {
   at[0].val.cooperative = 1;
   cfg.attrs = at;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, s->step_fn, p);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, s->step_fn, p);
+  if (e == cudaSuccess && logits && s->step_head_apart) e = run_matvec(s->step_head, s->st, false);
+  return e;
 }
 
 cudaGraphExec_t get_graph(vg_stream *s, bool token_input, bool logits) {
@@ -981,6 +988,13 @@ int vg_stream_create(vg_model *m, uint32_t max_context, vg_stream **out) {
       p.gate = s->gate;
       p.logits = s->logits;
       p.out = s->out_norm;
+      if (s->step_head_apart) {
+        MvParams &hp = s->step_head.p;
+        hp.xsrc = s->out_norm;
+        hp.out = s->logits;
+        hp.alpha = eff_scale(c.logit_scale);
+        hp.ctrl = s->ctrl;
+      }
       p.part = (float *)(b + o_sp);
       p.part_ml = (float2 *)(b + o_sml);
       p.tickets = (uint32_t *)(b + o_stk);

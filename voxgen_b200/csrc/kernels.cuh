@@ -346,18 +346,60 @@ __device__ __forceinline__ void mv_drain(const MvRing &R, const RingPos &rp, uin
   }
 }
 
+// Where a matvec's input vector comes from: an fp32 vector written earlier
+// (read through L2), or row `token` of a token table times alpha
+// (embedding.comp:28-47).
+struct XSrc {
+  const float *x;      // fp32 input, or nullptr for a token-table row
+  const uint8_t *tab;  // token table (segmented tiles) when x == nullptr
+  TileGeom g;
+  uint32_t token;
+  float alpha;
+};
+template <bool TAB>
+__device__ __forceinline__ float xsrc_elem(const XSrc &s, uint32_t k) {
+  if constexpr (!TAB) return __ldcg(s.x + k);
+  float v;
+  if (s.g.q8) {
+    const float d = __half2float(*reinterpret_cast<const __half *>(s.tab + s.g.scale_off(s.token, k / 32u)));
+    v = __fmul_rn(d, (float)(int8_t)s.tab[s.g.elem_off(s.token, k)]);
+  } else {
+    v = __half2float(*reinterpret_cast<const __half *>(s.tab + s.g.elem_off(s.token, k)));
+  }
+  return __fmul_rn(v, s.alpha);
+}
+
+// What the consumer warps wait for before they read the input vector.
+struct WaitSpec {
+  uint32_t kind;                  // kWaitNone, kWaitPdl (griddepcontrol.wait), kWaitGrid
+  const unsigned long long *bar;  // kWaitGrid: arrival counter, and the count to reach
+  unsigned long long target;
+  uint32_t *err;
+};
+enum : uint32_t { kWaitNone = 0, kWaitPdl = 1, kWaitGrid = 2 };
+__device__ __forceinline__ void consumer_wait(const WaitSpec &w, uint32_t cw, uint32_t lane) {
+  if (w.kind == kWaitPdl) {
+    pdl_wait();
+  } else if (w.kind == kWaitGrid) {
+    if (cw == 0 && lane == 0 && !grid_wait(w.bar, w.target, w.err)) set_error(w.err, kErrGridWait);
+    named_bar(1, kMvConsumers * 32);
+  }
+}
+
 // Activation operand of a matvec in shared memory: Q8_0 -> three int8 digit
 // planes and the per-32-block power of two sx[]; F16 -> fp16 hi and lo planes
 // and the whole-vector power of two *xscale. Run by the kMvConsumers consumer
-// warps (named barrier 1). xload(k) returns input element k < C (the hidden
-// state for RMSNORM, the input vector for COPY); wait_input() is called after
-// the RMSNorm weights are loaded and before the first xload. With xout set,
-// the (normalised) input vector is also written there.
-template <bool Q8, Pro P, class XLoad, class Wait>
+// warps (named barrier 1). The input vector (C elements) comes from src (its
+// token table when TAB); with RMS it is RMSNormed with normw, else copied. The wait comes after the RMSNorm
+// weights are loaded and before the first input load. With xout set, the
+// (normalised) input vector is also written there.
+template <bool Q8, bool RMS, bool TAB>
 __device__ __forceinline__ void mv_activation(uint32_t C, uint32_t cols_pad, const float *normw, float eps,
                                               uint8_t *areg, uint32_t plane, float *scr, uint32_t cw, uint32_t lane,
-                                              XLoad xload, Wait wait_input, float *xout) {
+                                              const XSrc &src, const WaitSpec &wait, float *xout) {
   constexpr uint32_t NCT = kMvConsumers * 32;
+  constexpr bool rms = RMS;
+  auto xload = [&](uint32_t k) { return xsrc_elem<TAB>(src, k); };
   float *sx = reinterpret_cast<float *>(areg + 3u * plane);      // Q8: per-block 2^e
   float *xscale = reinterpret_cast<float *>(areg + 2u * plane);  // F16: 2^e of the whole vector
   // Warp cw handles the groups of 4 consecutive 32-element blocks b with
@@ -370,7 +412,7 @@ __device__ __forceinline__ void mv_activation(uint32_t C, uint32_t cols_pad, con
   // (one round trip); the RMSNorm weight does not depend on the producer of the
   // input and is loaded before the wait. Register path for up to 4096 (RMSNorm
   // inputs) or 6144 (copied inputs) columns.
-  constexpr uint32_t MAXG = P == Pro::RMSNORM ? 4 : 6;
+  constexpr uint32_t MAXG = RMS ? 4 : 6;
   const uint32_t NGRP = (cols_pad / 32u + 3u) / 4u;                     // groups of 4 blocks
   const uint32_t JG = NGRP > cw ? (NGRP - cw + kMvConsumers - 1) / kMvConsumers : 0u;  // groups of this warp
   auto elem0 = [&](uint32_t g) { return (g * kMvConsumers + cw) * 128u + lane * 4u; };  // first element of lane
@@ -384,12 +426,12 @@ __device__ __forceinline__ void mv_activation(uint32_t C, uint32_t cols_pad, con
     return v;
   };
   float4 xr[MAXG], wr[MAXG];
-  if constexpr (P == Pro::RMSNORM) {
+  if constexpr (RMS) {
 #pragma unroll
     for (uint32_t g = 0; g < MAXG; ++g)
       wr[g] = (regs && g < JG) ? load4(elem0(g), [&](uint32_t k) { return normw[k]; }) : make_float4(0.f, 0.f, 0.f, 0.f);
   }
-  wait_input();
+  consumer_wait(wait, cw, lane);
 #pragma unroll
   for (uint32_t g = 0; g < MAXG; ++g)
     xr[g] = (regs && g < JG) ? load4(elem0(g), xload) : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -398,9 +440,9 @@ __device__ __forceinline__ void mv_activation(uint32_t C, uint32_t cols_pad, con
   // consumer scales each output row by inv_rms (W (inv_rms h w) = inv_rms W (h w)),
   // so the sum of squares needs no barrier here; this warp's partial goes to
   // scr[8 + cw] for mv_consume. With xout the normalised x itself is formed.
-  const bool defer = P == Pro::RMSNORM && xout == nullptr;
+  const bool defer = RMS && xout == nullptr;
   float inv_rms = 1.0f;
-  if constexpr (P == Pro::RMSNORM) {
+  if constexpr (RMS) {
     float ss = 0.f;
     if (regs) {
 #pragma unroll
@@ -436,7 +478,7 @@ __device__ __forceinline__ void mv_activation(uint32_t C, uint32_t cols_pad, con
   auto xglobal = [&](uint32_t k) -> float {
     if (k >= C) return 0.f;
     const float v = xload(k);
-    if constexpr (P == Pro::RMSNORM) return __fmul_rn(__fmul_rn(v, inv_rms), normw[k]);
+    if constexpr (RMS) return __fmul_rn(__fmul_rn(v, inv_rms), normw[k]);
     return v;
   };
   // f(g, v) for every group of this warp (register path fully unrolled)
@@ -549,12 +591,26 @@ __device__ __forceinline__ void mv_activation(uint32_t C, uint32_t cols_pad, con
 // reductions and the epilogue. Returns the next stage index; ok turns false
 // when a wait gave up (the partials are then incomplete and the error flag is
 // set).
-template <bool Q8, Mode M>
+// The epilogue with the mode chosen at run time, as one out-of-line copy: the
+// persistent step kernel runs every mode from a single call site.
+__device__ __noinline__ void mv_epilogue_rt(Mode mode, const MvParams &p, uint32_t R, float a, float b,
+                                            uint32_t pos) {
+  switch (mode) {
+    case Mode::PLAIN: mv_epilogue<Mode::PLAIN>(p, R, a, b, pos); break;
+    case Mode::RESID: mv_epilogue<Mode::RESID>(p, R, a, b, pos); break;
+    case Mode::SWIGLU: mv_epilogue<Mode::SWIGLU>(p, R, a, b, pos); break;
+    case Mode::QKV: mv_epilogue<Mode::QKV>(p, R, a, b, pos); break;
+  }
+}
+
+// Consumer side of a matvec over n_items ring segments (tiles t0.. of this
+// CTA's run). epilogue(R, a, b) receives the finished rows R and R + 8.
+template <bool Q8, class Epilogue>
 __device__ __forceinline__ void mv_consume(const MvRing &R, RingPos &rp, uint32_t n_items, uint32_t NSEG,
                                            uint32_t SEGB, const uint8_t *areg, uint32_t plane, float *red,
-                                           const MvParams &p, uint32_t t0, uint32_t pos, uint32_t cw, uint32_t lane,
+                                           const MvParams &p, uint32_t t0, uint32_t cw, uint32_t lane,
                                            const uint32_t *abort_flag, uint32_t *err, bool &ok,
-                                           const float *defer_ss) {
+                                           const float *defer_ss, Epilogue epilogue) {
   constexpr uint32_t NCT = kMvConsumers * 32;
   const float *sx = reinterpret_cast<const float *>(areg + 3u * plane);
   const float *xscale = reinterpret_cast<const float *>(areg + 2u * plane);
@@ -750,7 +806,7 @@ __device__ __forceinline__ void mv_consume(const MvRing &R, RingPos &rp, uint32_
         a += red[(t * kMvConsumers + w) * kTileRows + lane];
         b += red[(t * kMvConsumers + w) * kTileRows + lane + 8u];
       }
-      mv_epilogue<M>(p, (t0 + t) * kTileRows + lane, a * row_scale, b * row_scale, pos);
+      epilogue((t0 + t) * kTileRows + lane, a * row_scale, b * row_scale);
     }
   }
 }
@@ -798,14 +854,18 @@ __global__ void __launch_bounds__(kMvThreads, 1) matvec_kernel(const __grid_cons
     return;
   }
   const uint32_t cw = warp;
-  const float *xs = p.xsrc;
-  mv_activation<Q8, P>(g.cols, NSEG * g.seg_cols(), p.normw, p.eps, smem + L.a, p.plane, scr, cw, lane,
-                       [&](uint32_t k) { return __ldcg(xs + k); }, [] { pdl_wait(); }, nullptr);
+  XSrc src{};
+  src.x = p.xsrc;
+  WaitSpec wait{};
+  wait.kind = kWaitPdl;
+  mv_activation<Q8, P == Pro::RMSNORM, false>(g.cols, NSEG * g.seg_cols(), p.normw, p.eps, smem + L.a, p.plane, scr,
+                                              cw, lane, src, wait, nullptr);
   const uint32_t pos = (M == Mode::QKV) ? p.ctrl[kCtrlPos] : 0u;
   bool ok = true;
   RingPos rp;
-  mv_consume<Q8, M>(R, rp, n_items, NSEG, SEGB, smem + L.a, p.plane, red, p, t0, pos, cw, lane, nullptr, err, ok,
-                    P == Pro::RMSNORM ? scr + 8 : nullptr);
+  mv_consume<Q8>(R, rp, n_items, NSEG, SEGB, smem + L.a, p.plane, red, p, t0, cw, lane, nullptr, err, ok,
+                 P == Pro::RMSNORM ? scr + 8 : nullptr,
+                 [&](uint32_t R0, float a, float b) { mv_epilogue<M>(p, R0, a, b, pos); });
 }
 
 // ---------------------------------------------------------------------------

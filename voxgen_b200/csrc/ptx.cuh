@@ -20,6 +20,7 @@ enum : uint32_t {
   kErrBadToken = 8u,       // token id outside the vocabulary
   kErrPosition = 16u,      // position outside the KV cache
   kErrGridWait = 32u,      // a CTA gave up waiting at a grid barrier
+  kErrPlan = 64u,          // launch parameters the kernel was not built for
 };
 
 __device__ __forceinline__ uint64_t globaltimer() {

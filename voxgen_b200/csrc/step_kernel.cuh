@@ -98,19 +98,6 @@ __device__ __forceinline__ AttnUnit attn_unit(const StepParams &p, uint32_t u, u
   return a;
 }
 
-// Dequantised token-table element k of row tok times alpha (embedding.comp:28-47).
-__device__ __forceinline__ float embed_elem(const StepParams &p, uint32_t tok, uint32_t k) {
-  const TileGeom &g = p.g_tok;
-  float v;
-  if (g.q8) {
-    const float d = __half2float(*reinterpret_cast<const __half *>(p.tok + g.scale_off(tok, k / 32u)));
-    v = __fmul_rn(d, (float)(int8_t)p.tok[g.elem_off(tok, k)]);
-  } else {
-    v = __half2float(*reinterpret_cast<const __half *>(p.tok + g.elem_off(tok, k)));
-  }
-  return __fmul_rn(v, p.emb_scale);
-}
-
 // One CTA of kMvThreads (9 warps) per SM. Three warps share one SM
 // sub-partition's 16K registers, so a thread may use at most 168.
 template <bool Q8, int DPL>
@@ -223,29 +210,40 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_step_kernel(const __grid
   auto zero_red = [&](uint32_t tiles) {
     for (uint32_t i = cw * 32u + lane; i < tiles * kMvConsumers * kTileRows; i += NCT) red[i] = 0.f;
   };
-  // One matvec phase over this CTA's tile run of g.
-  auto matvec = [&](auto q8c, auto mode, auto pro, uint32_t ph, const uint8_t *w, const TileGeom &g,
-                    const MvParams &mp, auto xload, float *xout) {
+  // One matvec phase over this CTA's tile run of g. Every matvec phase of the
+  // step (and the final RMSNorm) goes through this one call site per weight
+  // type, so the consumer code is a single copy that stays in the instruction
+  // cache from phase to phase; the epilogue, the prologue and the input source
+  // are runtime values.
+  auto matvec = [&](auto q8c, Mode mode, bool rms, uint32_t ph, const MvParams &mp, const XSrc &src, float *xout,
+                    bool consume) {
     constexpr bool WQ8 = decltype(q8c)::value;
-    constexpr Mode M = decltype(mode)::value;
-    constexpr Pro P = decltype(pro)::value;
+    const TileGeom &g = mp.g;
     uint32_t t0, t1;
     tile_run(g, t0, t1);
     const uint32_t NSEG = g.nseg(), SEGB = g.seg_bytes();
-    zero_red(t1 - t0);
-    mv_activation<WQ8, P>(g.cols, NSEG * g.seg_cols(), mp.normw, mp.eps, aux, p.plane, scr, cw, lane, xload,
-                          [&] { wait_phase(ph); }, xout);
-    mv_consume<WQ8, M>(R, rp, (t1 - t0) * NSEG, NSEG, SEGB, aux, p.plane, red, mp, t0, pos, cw, lane, err, err,
-                       ok, (P == Pro::RMSNORM && xout == nullptr) ? scr + 8 : nullptr);
-    (void)w;
+    if (consume) zero_red(t1 - t0);
+    WaitSpec ws{};
+    ws.kind = kWaitGrid;  // at phase 0 the target is already reached
+    ws.bar = p.bar;
+    ws.target = base + (unsigned long long)ph * gridDim.x;
+    ws.err = err;
+    // three prologue variants: the phases alternate between RMSNorm and copied
+    // inputs; the token-table source is only the first layer's QKV
+    if (src.x == nullptr)
+      mv_activation<WQ8, true, true>(g.cols, NSEG * g.seg_cols(), mp.normw, mp.eps, aux, p.plane, scr, cw, lane, src,
+                                     ws, xout);
+    else if (rms)
+      mv_activation<WQ8, true, false>(g.cols, NSEG * g.seg_cols(), mp.normw, mp.eps, aux, p.plane, scr, cw, lane, src,
+                                      ws, xout);
+    else
+      mv_activation<WQ8, false, false>(g.cols, NSEG * g.seg_cols(), mp.normw, mp.eps, aux, p.plane, scr, cw, lane,
+                                       src, ws, xout);
+    if (consume)
+      mv_consume<WQ8>(R, rp, (t1 - t0) * NSEG, NSEG, SEGB, aux, p.plane, red, mp, t0, cw, lane, err, err, ok,
+                      (rms && xout == nullptr) ? scr + 8 : nullptr,
+                      [&](uint32_t R0, float a, float b) { mv_epilogue_rt(mode, mp, R0, a, b, pos); });
   };
-  using QT = std::integral_constant<bool, Q8>;
-  using MQ = std::integral_constant<Mode, Mode::QKV>;
-  using MR = std::integral_constant<Mode, Mode::RESID>;
-  using MS = std::integral_constant<Mode, Mode::SWIGLU>;
-  using MP = std::integral_constant<Mode, Mode::PLAIN>;
-  using PN = std::integral_constant<Pro, Pro::RMSNORM>;
-  using PC = std::integral_constant<Pro, Pro::COPY>;
 
   uint32_t tok = 0;
   if (p.token_input) {
@@ -256,40 +254,15 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_step_kernel(const __grid
     }
   }
 
-  for (uint32_t l = 0; l < p.n_layers; ++l) {
-    const StepLayer &Ly = layers[l];
-    const uint32_t ph0 = l * kPhasesPerLayer;
-    MvParams mp{};
-    mp.ctrl = p.ctrl;
-    mp.eps = p.eps;
-
-    // ---- QKV + RoPE + KV store: input hid_a (or the token's embedding row) ----
-    mp.g = p.g_qkv;
-    mp.normw = Ly.attn_norm;
-    mp.out = p.q;
-    mp.q_rows = p.H;
-    mp.kv_rows = p.kv_heads * p.head_dim;
-    mp.head_dim = p.head_dim;
-    mp.ctx = p.ctx;
-    mp.kc = Ly.kc;
-    mp.vc = Ly.vc;
-    mp.inv_freq = p.inv_freq;
-    mp.ext = p.ext;
-    mp.rope_scaling = p.rope_scaling;
-    if (l == 0 && p.token_input) {
-      // every CTA dequantises the row itself; CTA 0 also stores it as the residual stream
-      if (blockIdx.x == 0)
-        for (uint32_t k = cw * 32u + lane; k < p.H; k += NCT) p.hid_a[k] = embed_elem(p, tok, k);
-      matvec(QT{}, MQ{}, PN{}, ph0, Ly.qkv, p.g_qkv, mp, [&](uint32_t k) { return embed_elem(p, tok, k); }, nullptr);
-    } else {
-      const float *x = p.hid_a;
-      matvec(QT{}, MQ{}, PN{}, ph0, Ly.qkv, p.g_qkv, mp, [&](uint32_t k) { return __ldcg(x + k); }, nullptr);
-    }
-    arrive();
+  // Phases nb * layer + kind, then phase nb: the final RMSNorm and the optional LM head.
+  for (uint32_t ph = 0; ph <= nb; ++ph) {
+    const uint32_t l = ph / kPhasesPerLayer;
+    const uint32_t kind = ph - l * kPhasesPerLayer;
+    const StepLayer &Ly = layers[l < p.n_layers ? l : 0u];
 
     // ---- attention: split-K units, the last unit of a KV head merges ----
-    {
-      wait_phase(ph0 + kPhAttn);
+    if (ph < nb && kind == kPhAttn) {
+      wait_phase(ph);
       float *sQ = reinterpret_cast<float *>(aux);  // [G][D]
       float *sS = sQ + G * D;                       // [G][chunk]
       for (uint32_t u = blockIdx.x; u < n_units; u += gridDim.x) {
@@ -539,70 +512,87 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_step_kernel(const __grid
         named_bar(1, NCT);  // sQ / sS / sflags reuse by the next unit
       }
       arrive();
+      continue;
     }
 
-    // ---- o_proj + residual: hid_b = hid_a + scale * O attn ----
-    mp = MvParams{};
-    mp.ctrl = p.ctrl;
-    mp.g = p.g_o;
-    mp.out = p.hid_b;
-    mp.resid = p.hid_a;
-    mp.alpha = p.res_scale;
-    {
-      const float *x = p.attn;
-      matvec(QT{}, MR{}, PC{}, ph0 + kPhO, Ly.o, p.g_o, mp, [&](uint32_t k) { return __ldcg(x + k); }, nullptr);
-    }
-    arrive();
-
-    // ---- gate/up + SwiGLU on RMSNorm(hid_b) ----
-    mp = MvParams{};
-    mp.ctrl = p.ctrl;
-    mp.g = p.g_gu;
-    mp.normw = Ly.ffn_norm;
-    mp.eps = p.eps;
-    mp.out = p.gate;
-    {
-      const float *x = p.hid_b;
-      matvec(QT{}, MS{}, PN{}, ph0 + kPhGu, Ly.gateup, p.g_gu, mp, [&](uint32_t k) { return __ldcg(x + k); },
-             nullptr);
-    }
-    arrive();
-
-    // ---- down + residual: hid_a = hid_b + scale * Down gate ----
-    mp = MvParams{};
-    mp.ctrl = p.ctrl;
-    mp.g = p.g_down;
-    mp.out = p.hid_a;
-    mp.resid = p.hid_b;
-    mp.alpha = p.res_scale;
-    {
-      const float *x = p.gate;
-      matvec(QT{}, MR{}, PC{}, ph0 + kPhDown, Ly.down, p.g_down, mp, [&](uint32_t k) { return __ldcg(x + k); },
-             nullptr);
-    }
-    arrive();
-  }
-
-  // ---- final RMSNorm (output) and the optional LM head ----
-  const uint32_t phf = nb;
-  const float *hx = p.hid_a;
-  auto hload = [&](uint32_t k) { return __ldcg(hx + k); };
-  if (p.want_logits) {
     MvParams mp{};
     mp.ctrl = p.ctrl;
-    mp.g = p.g_head;
-    mp.normw = p.out_norm;
     mp.eps = p.eps;
-    mp.out = p.logits;
-    mp.alpha = p.logit_scale;
-    float *xo = blockIdx.x == 0 ? p.out : nullptr;
-    if (p.g_head.q8)
-      matvec(std::integral_constant<bool, true>{}, MP{}, PN{}, phf, p.head, p.g_head, mp, hload, xo);
-    else
-      matvec(std::integral_constant<bool, false>{}, MP{}, PN{}, phf, p.head, p.g_head, mp, hload, xo);
-  } else if (blockIdx.x == 0) {
-    mv_activation<Q8, Pro::RMSNORM>(p.H, p.g_qkv.nseg() * p.g_qkv.seg_cols(), p.out_norm, p.eps, aux, p.plane, scr,
-                                    cw, lane, hload, [&] { wait_phase(phf); }, p.out);
+    XSrc src{};
+    Mode mode = Mode::PLAIN;
+    bool rms = false, consume = true;
+    float *xout = nullptr;
+    if (ph == nb) {
+      // final RMSNorm into out (CTA 0), and the LM head on it when logits are wanted
+      if (!p.want_logits && blockIdx.x != 0) break;
+      mp.g = p.want_logits ? p.g_head : p.g_qkv;
+      mp.normw = p.out_norm;
+      mp.out = p.logits;
+      mp.alpha = p.logit_scale;
+      src.x = p.hid_a;
+      rms = true;
+      consume = p.want_logits != 0;
+      xout = blockIdx.x == 0 ? p.out : nullptr;
+    } else if (kind == kPhQkv) {
+      // QKV + RoPE + KV store on RMSNorm(hid_a), or of the token's embedding row
+      mp.g = p.g_qkv;
+      mp.normw = Ly.attn_norm;
+      mp.out = p.q;
+      mp.q_rows = p.H;
+      mp.kv_rows = p.kv_heads * p.head_dim;
+      mp.head_dim = p.head_dim;
+      mp.ctx = p.ctx;
+      mp.kc = Ly.kc;
+      mp.vc = Ly.vc;
+      mp.inv_freq = p.inv_freq;
+      mp.ext = p.ext;
+      mp.rope_scaling = p.rope_scaling;
+      mode = Mode::QKV;
+      rms = true;
+      if (l == 0 && p.token_input) {
+        src.tab = p.tok;
+        src.g = p.g_tok;
+        src.token = tok;
+        src.alpha = p.emb_scale;
+        // every CTA dequantises the row itself; CTA 0 also stores it as the residual stream
+        if (blockIdx.x == 0)
+          for (uint32_t k = cw * 32u + lane; k < p.H; k += NCT) p.hid_a[k] = xsrc_elem<true>(src, k);
+      } else {
+        src.x = p.hid_a;
+      }
+    } else if (kind == kPhO) {
+      // o_proj + residual: hid_b = hid_a + scale * O attn
+      mp.g = p.g_o;
+      mp.out = p.hid_b;
+      mp.resid = p.hid_a;
+      mp.alpha = p.res_scale;
+      src.x = p.attn;
+      mode = Mode::RESID;
+    } else if (kind == kPhGu) {
+      // gate/up + SwiGLU on RMSNorm(hid_b)
+      mp.g = p.g_gu;
+      mp.normw = Ly.ffn_norm;
+      mp.out = p.gate;
+      src.x = p.hid_b;
+      mode = Mode::SWIGLU;
+      rms = true;
+    } else {
+      // down + residual: hid_a = hid_b + scale * Down gate
+      mp.g = p.g_down;
+      mp.out = p.hid_a;
+      mp.resid = p.hid_b;
+      mp.alpha = p.res_scale;
+      src.x = p.gate;
+      mode = Mode::RESID;
+    }
+    if (mp.g.q8 != Q8) {
+      // an LM head in the other weight format runs as its own launch after this one
+      if (cw == 0 && lane == 0) set_error(err, kErrPlan);
+      mp.g = p.g_qkv;
+      consume = false;
+    }
+    matvec(std::integral_constant<bool, Q8>{}, mode, rms, ph, mp, src, xout, consume);
+    if (ph < nb) arrive();
   }
   if (blockIdx.x == 0) {
     named_bar(1, NCT);
