@@ -623,6 +623,12 @@ std::string plan_step(vg_stream *s) {
   p.g_tok = m->tok.g;
   p.g_head = m->out.g;
   p.n_layers = c.block_count;
+  p.H = c.embedding_length;
+  p.xcols = 0;
+  for (const TileGeom *g : {&p.g_qkv, &p.g_o, &p.g_gu, &p.g_down, &p.g_head}) {
+    if (g->cols % 4u) return strf("a matvec input of %u columns is not a whole number of 16-byte copies", g->cols);
+    p.xcols = std::max(p.xcols, g->cols);
+  }
   const uint32_t grid = (uint32_t)m->ctx->sms;
   uint32_t segb = 0, plane = 0, cpad = 0, rb = 1;
   s->step_head_apart = m->out.type != type;

@@ -398,7 +398,6 @@ __device__ __forceinline__ void mv_activation(uint32_t C, uint32_t cols_pad, con
                                               uint8_t *areg, uint32_t plane, float *scr, uint32_t cw, uint32_t lane,
                                               const XSrc &src, const WaitSpec &wait, float *xout) {
   constexpr uint32_t NCT = kMvConsumers * 32;
-  constexpr bool rms = RMS;
   auto xload = [&](uint32_t k) { return xsrc_elem<TAB>(src, k); };
   float *sx = reinterpret_cast<float *>(areg + 3u * plane);      // Q8: per-block 2^e
   float *xscale = reinterpret_cast<float *>(areg + 2u * plane);  // F16: 2^e of the whole vector

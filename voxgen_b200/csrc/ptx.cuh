@@ -130,6 +130,12 @@ __device__ __forceinline__ bool grid_wait(const unsigned long long *ctr, unsigne
   return false;
 }
 
+// Orders this thread's earlier generic-proxy accesses (an acquire of other
+// CTAs' writes included) before its later async-proxy ones (bulk copies).
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
 // Bulk copy global -> shared (cp.async.bulk, TMA engine, no tensor map, no
 // multicast). dst, src and bytes must be multiples of 16.
 __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {

@@ -52,20 +52,179 @@ struct StepParams {
   uint32_t nst, slot;       // ring stages and bytes per stage slot
   uint32_t a_bytes, plane;  // activation / attention scratch region and digit-plane stride
   uint32_t rb;              // partial-sum tiles (largest per-CTA tile run of any phase)
+  uint32_t xcols;           // longest matvec input (columns)
 };
 
+// Shared memory of a step CTA: the ring and its barriers (then the two
+// staging barriers), the activation operand / attention scratch, the tile
+// partial sums, the staged input vector and RMSNorm weight, the layer table
+// and a small scratch.
 struct StepSmem {
-  uint32_t ring, bars, aux, red, layers, scr, total;
+  uint32_t ring, bars, sbar, aux, red, stg, stw, layers, scr, total;
   __host__ __device__ StepSmem(const StepParams &p) {
     ring = 0;
     bars = ring + p.nst * p.slot;
-    aux = bars + p.nst * 16u;
+    sbar = bars + p.nst * 16u;
+    aux = sbar + 16u;
     red = aux + ((p.a_bytes + 127u) & ~127u);
-    layers = red + p.rb * kMvConsumers * kTileRows * 4u;
+    stg = red + p.rb * kMvConsumers * kTileRows * 4u;
+    stw = stg + ((p.xcols * 4u + 127u) & ~127u);
+    layers = stw + ((p.H * 4u + 127u) & ~127u);
     scr = layers + p.n_layers * (uint32_t)sizeof(StepLayer);
     total = scr + 1024u;
   }
 };
+
+// Activation operand of a step matvec (mv_activation's arithmetic) from the
+// input staged in shared memory (stg, C floats) and, with rms, the staged
+// RMSNorm weight (stw): the groups are looped over instead of unrolled, so
+// every phase runs one small copy of this code.
+template <bool Q8>
+__device__ __forceinline__ void step_activation(uint32_t C, uint32_t cols_pad, bool rms, const float *stg,
+                                                const float *stw, float eps, uint8_t *areg, uint32_t plane,
+                                                float *scr, uint32_t cw, uint32_t lane, float *xout) {
+  constexpr uint32_t NCT = kMvConsumers * 32;
+  float *sx = reinterpret_cast<float *>(areg + 3u * plane);      // Q8: per-block 2^e
+  float *xscale = reinterpret_cast<float *>(areg + 2u * plane);  // F16: 2^e of the whole vector
+  // warp cw takes the groups of 128 elements g * 8 + cw, 4 per lane (mv_activation)
+  const uint32_t NGRP = (cols_pad / 32u + 3u) / 4u;
+  const uint32_t JG = NGRP > cw ? (NGRP - cw + kMvConsumers - 1) / kMvConsumers : 0u;
+  auto elem0 = [&](uint32_t g) { return (g * kMvConsumers + cw) * 128u + lane * 4u; };
+  auto ld4 = [&](const float *v, uint32_t k0) {
+    if (k0 + 3u < C) return *reinterpret_cast<const float4 *>(v + k0);
+    float4 r;
+    r.x = k0 < C ? v[k0] : 0.f;
+    r.y = k0 + 1u < C ? v[k0 + 1u] : 0.f;
+    r.z = k0 + 2u < C ? v[k0 + 2u] : 0.f;
+    r.w = k0 + 3u < C ? v[k0 + 3u] : 0.f;
+    return r;
+  };
+  // RMSNorm (rmsnorm.comp:21-42) with the 1/rms factor deferred to the rows
+  // when there is no xout (mv_activation)
+  const bool defer = rms && xout == nullptr;
+  float inv_rms = 1.0f;
+  if (rms) {
+    float ss = 0.f;
+#pragma unroll 1
+    for (uint32_t g = 0; g < JG; ++g) {
+      const float4 v = ld4(stg, elem0(g));
+      ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+    }
+    ss = warp_sum(ss);
+    if (defer) {
+      if (lane == 0) scr[8 + cw] = ss;
+    } else {
+      if (lane == 0) scr[cw] = ss;
+      named_bar(1, NCT);
+      float tot = 0.f;
+#pragma unroll
+      for (int w = 0; w < kMvConsumers; ++w) tot += scr[w];
+      inv_rms = 1.0f / sqrtf(tot / (float)C + eps);
+    }
+  }
+  auto xval = [&](uint32_t k0) {
+    float4 v = ld4(stg, k0);
+    if (rms) {
+      const float4 w = ld4(stw, k0);
+      v.x = __fmul_rn(__fmul_rn(v.x, inv_rms), w.x);
+      v.y = __fmul_rn(__fmul_rn(v.y, inv_rms), w.y);
+      v.z = __fmul_rn(__fmul_rn(v.z, inv_rms), w.z);
+      v.w = __fmul_rn(__fmul_rn(v.w, inv_rms), w.w);
+    }
+    return v;
+  };
+  auto put_xout = [&](uint32_t k0, const float4 &v) {
+    if (!xout) return;
+    if (k0 < C) xout[k0] = v.x;
+    if (k0 + 1u < C) xout[k0 + 1u] = v.y;
+    if (k0 + 2u < C) xout[k0 + 2u] = v.z;
+    if (k0 + 3u < C) xout[k0 + 3u] = v.w;
+  };
+  if constexpr (Q8) {
+    // int8 digits and the per-block 2^e (mv_activation)
+    constexpr float kRnd = 12582912.0f;
+    constexpr int kRndBits = 0x4B400000;
+    auto split = [&](float x, float inv, int &q0, int &q1, int &q2) {
+      const int n = __float_as_int(fmaf(x * inv, 16384.0f, kRnd)) - kRndBits;
+      q0 = (n + 8192) >> 14;
+      const int r = n - (q0 << 14);
+      q1 = (r + 64) >> 7;
+      q2 = r - (q1 << 7);
+    };
+#pragma unroll 1
+    for (uint32_t g = 0; g < JG; ++g) {
+      const uint32_t k0 = elem0(g), b = k0 >> 5;
+      const float4 v = xval(k0);
+      put_xout(k0, v);
+      uint32_t mb = max(max(__float_as_uint(fabsf(v.x)), __float_as_uint(fabsf(v.y))),
+                        max(__float_as_uint(fabsf(v.z)), __float_as_uint(fabsf(v.w))));
+      mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, 1));
+      mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, 2));
+      mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, 4));
+      int e = 0;
+      const bool nz = block_exponent(mb, e);
+      int q[3][4] = {};
+      if (nz) {
+        const float inv = pow2f(-e);
+        split(v.x, inv, q[0][0], q[1][0], q[2][0]);
+        split(v.y, inv, q[0][1], q[1][1], q[2][1]);
+        split(v.z, inv, q[0][2], q[1][2], q[2][2]);
+        split(v.w, inv, q[0][3], q[1][3], q[2][3]);
+      }
+      if (b * 32u < cols_pad) {
+        const uint32_t o = b * 32u + bfrag_byte_q8(k0 & 31u);  // 4 consecutive bytes
+#pragma unroll
+        for (int d = 0; d < 3; ++d) {
+          const uint32_t w = __byte_perm(__byte_perm((uint32_t)q[d][0], (uint32_t)q[d][1], 0x0040u),
+                                         __byte_perm((uint32_t)q[d][2], (uint32_t)q[d][3], 0x0040u), 0x5410u);
+          *reinterpret_cast<uint32_t *>(areg + d * plane + o) = w;
+        }
+        if ((lane & 7u) == 0) sx[b] = nz ? pow2f(e) : 0.f;
+      }
+    }
+    // each warp consumes only its own blocks when tiles have a multiple of 4 segments
+    if ((cols_pad / (kSegSteps * 32u)) % kStageSegs != 0) named_bar(1, NCT);
+    else __syncwarp();
+  } else {
+    // whole-vector power-of-two scale, then fp16 hi + lo (mv_activation)
+    float m = 0.f;
+#pragma unroll 1
+    for (uint32_t g = 0; g < JG; ++g) {
+      const float4 v = xval(elem0(g));
+      m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    }
+    m = warp_max(m);
+    named_bar(1, NCT);  // scr[] reuse after the RMSNorm reduction
+    if (lane == 0) scr[cw] = m;
+    named_bar(1, NCT);
+    float mx = 0.f;
+#pragma unroll
+    for (int w = 0; w < kMvConsumers; ++w) mx = fmaxf(mx, scr[w]);
+    const uint32_t ef = (__float_as_uint(mx) >> 23) & 0xFFu;
+    const int e = ef < 20 ? 0 : (int)ef - 127 - 13;  // max|x| * 2^-e < 2^14
+    const float inv = pow2f(-e);
+    __half *hi = reinterpret_cast<__half *>(areg), *lo = reinterpret_cast<__half *>(areg + plane);
+#pragma unroll 1
+    for (uint32_t g = 0; g < JG; ++g) {
+      const uint32_t k0 = elem0(g);
+      const float4 v4 = xval(k0);
+      put_xout(k0, v4);
+      const float vv[4] = {v4.x, v4.y, v4.z, v4.w};
+#pragma unroll
+      for (uint32_t i = 0; i < 4; ++i) {
+        const uint32_t k = k0 + i;
+        if (k >= cols_pad) continue;
+        const uint32_t o = (k & ~15u) + bfrag_half_f16(k & 15u);  // element k of K-step k / 16
+        const float v = vv[i] * inv;
+        const __half h = __float2half_rn(v);
+        hi[o] = h;
+        lo[o] = __float2half_rn(v - __half2float(h));
+      }
+    }
+    if (cw == 0 && lane == 0) *xscale = pow2f(e);
+    named_bar(1, NCT);
+  }
+}
 
 // Attention scratch inside the aux region: q of one KV group, then the scores
 // of a chunk or (when merging) the weights of every chunk.
@@ -115,6 +274,9 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_step_kernel(const __grid
   uint8_t *aux = smem + L.aux;
   float *red = reinterpret_cast<float *>(smem + L.red);
   StepLayer *layers = reinterpret_cast<StepLayer *>(smem + L.layers);
+  uint64_t *sbar = reinterpret_cast<uint64_t *>(smem + L.sbar);  // staging barriers: input, RMSNorm weight
+  float *stg = reinterpret_cast<float *>(smem + L.stg);
+  float *stw = reinterpret_cast<float *>(smem + L.stw);
   float *scr = reinterpret_cast<float *>(smem + L.scr);                                 // 64 floats
   unsigned long long *sbase = reinterpret_cast<unsigned long long *>(smem + L.scr + 256u);
   uint32_t *sflags = reinterpret_cast<uint32_t *>(smem + L.scr + 264u);                // 8 words
@@ -130,6 +292,8 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_step_kernel(const __grid
       mbar_init(&R.full[i], 1);
       mbar_init(&R.empty[i], kMvConsumers);
     }
+    mbar_init(&sbar[0], 1);
+    mbar_init(&sbar[1], 1);
     fence_mbar_init();
     // Every CTA arrives exactly nb times per step, so at a step's start the
     // counter is base + (arrivals of this step so far) with base a multiple of
@@ -189,7 +353,7 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_step_kernel(const __grid
   }
 
   // ---------------- consumers ----------------
-  const uint32_t cw = warp;
+  const uint32_t cw = warp, tid = cw * 32u + lane;
   RingPos rp;  // next ring stage
   bool ok = true;
   // Grid barrier before phase ph: every CTA has finished phase ph - 1.
@@ -207,6 +371,7 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_step_kernel(const __grid
     named_bar(1, NCT);
     if (cw == 0 && lane == 0) grid_arrive(p.bar);
   };
+  uint32_t spar = 0;  // parities of the two staging barriers (bit 0 input, bit 1 RMSNorm weight)
   auto zero_red = [&](uint32_t tiles) {
     for (uint32_t i = cw * 32u + lane; i < tiles * kMvConsumers * kTileRows; i += NCT) red[i] = 0.f;
   };
@@ -223,22 +388,38 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_step_kernel(const __grid
     tile_run(g, t0, t1);
     const uint32_t NSEG = g.nseg(), SEGB = g.seg_bytes();
     if (consume) zero_red(t1 - t0);
-    WaitSpec ws{};
-    ws.kind = kWaitGrid;  // at phase 0 the target is already reached
-    ws.bar = p.bar;
-    ws.target = base + (unsigned long long)ph * gridDim.x;
-    ws.err = err;
-    // three prologue variants: the phases alternate between RMSNorm and copied
-    // inputs; the token-table source is only the first layer's QKV
-    if (src.x == nullptr)
-      mv_activation<WQ8, true, true>(g.cols, NSEG * g.seg_cols(), mp.normw, mp.eps, aux, p.plane, scr, cw, lane, src,
-                                     ws, xout);
-    else if (rms)
-      mv_activation<WQ8, true, false>(g.cols, NSEG * g.seg_cols(), mp.normw, mp.eps, aux, p.plane, scr, cw, lane, src,
-                                      ws, xout);
-    else
-      mv_activation<WQ8, false, false>(g.cols, NSEG * g.seg_cols(), mp.normw, mp.eps, aux, p.plane, scr, cw, lane,
-                                       src, ws, xout);
+    const uint32_t C = g.cols;
+    // the RMSNorm weight does not depend on the step: its copy starts before the wait
+    if (rms && tid == 0) {
+      mbar_arrive_expect_tx(sbar + 1, C * 4u);
+      bulk_g2s(stw, mp.normw, C * 4u, sbar + 1);
+    }
+    wait_phase(ph);
+    if (src.x == nullptr) {
+      for (uint32_t k = tid; k < C; k += NCT) stg[k] = xsrc_elem<true>(src, k);  // token-table row
+      named_bar(1, NCT);
+    } else {
+      // one bulk copy of the input; the thread that acquired the other CTAs'
+      // writes at the grid barrier orders them before its async-proxy read
+      if (tid == 0) {
+        fence_proxy_async_global();
+        mbar_arrive_expect_tx(sbar, C * 4u);
+        bulk_g2s(stg, src.x, C * 4u, sbar);
+      }
+      if (!mbar_wait_bounded(sbar, spar & 1u, err)) {
+        set_error(err, kErrConsumerWait);
+        ok = false;
+      }
+      spar ^= 1u;
+    }
+    if (rms) {
+      if (!mbar_wait_bounded(sbar + 1, (spar >> 1) & 1u, err)) {
+        set_error(err, kErrConsumerWait);
+        ok = false;
+      }
+      spar ^= 2u;
+    }
+    step_activation<WQ8>(C, NSEG * g.seg_cols(), rms, stg, stw, mp.eps, aux, p.plane, scr, cw, lane, xout);
     if (consume)
       mv_consume<WQ8>(R, rp, (t1 - t0) * NSEG, NSEG, SEGB, aux, p.plane, red, mp, t0, cw, lane, err, err, ok,
                       (rms && xout == nullptr) ? scr + 8 : nullptr,
