@@ -642,7 +642,9 @@ std::string plan_step(vg_stream *s) {
     rb = std::max(rb, (g->tiles() + grid - 1) / grid);
   }
   p.slot = kStageSegs * segb;
-  p.chunk = std::min<uint32_t>(64u, p.slot / (2u * D));
+  // positions per attention unit: a whole number of 16-row MMA tiles of K (or V) rows in a stage slot
+  p.chunk = std::min<uint32_t>(64u, p.slot / (2u * D)) & ~15u;
+  if (p.chunk == 0) return strf("a stage slot of %u bytes holds no 16 rows of head_dim %u", p.slot, D);
   p.max_chunks = (s->max_ctx + p.chunk - 1) / p.chunk;
   p.plane = plane;
   p.a_bytes = std::max(round_up(3u * plane + cpad / 32u * 4u + 16u, 128u), step_attn_bytes(G, D, p.chunk, p.max_chunks));

@@ -185,6 +185,16 @@ __device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], const void *p) {
                : "r"(smem_u32(p)));
 }
 
+// The same four 8x8 matrices, each transposed on the way in.
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t (&r)[4], const void *p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ uint32_t pack_half2(__half lo, __half hi) {
+  return (uint32_t)__half_as_ushort(lo) | ((uint32_t)__half_as_ushort(hi) << 16);
+}
+
 // D = A(16x32 s8, row) * B(32x8 s8, col) + c (every element), A fragment as
 // ldmatrix.x4 delivers it.
 __device__ __forceinline__ void mma_s8(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1, int c) {

@@ -226,11 +226,12 @@ __device__ __forceinline__ void step_activation(uint32_t C, uint32_t cols_pad, b
   }
 }
 
-// Attention scratch inside the aux region: q of one KV group, then the scores
-// of a chunk or (when merging) the weights of every chunk.
+// Attention scratch inside the aux region: the q fragments of one KV group,
+// then the scores of a chunk (rows padded by 4 floats).
 __host__ __device__ inline uint32_t step_attn_bytes(uint32_t G, uint32_t head_dim, uint32_t chunk,
                                                     uint32_t max_chunks) {
-  return (G * head_dim + G * (chunk > max_chunks ? chunk : max_chunks)) * 4u;
+  const uint32_t q_frag = (G + 7u) / 8u * (head_dim / 16u) * 2u * 32u * 8u;
+  return q_frag + G * ((chunk > max_chunks ? chunk : max_chunks) + 4u) * 4u;
 }
 
 enum : uint32_t { kPhQkv = 0, kPhAttn = 1, kPhO = 2, kPhGu = 3, kPhDown = 4, kPhasesPerLayer = 5 };
@@ -280,7 +281,6 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_step_kernel(const __grid
   float *scr = reinterpret_cast<float *>(smem + L.scr);                                 // 64 floats
   unsigned long long *sbase = reinterpret_cast<unsigned long long *>(smem + L.scr + 256u);
   uint32_t *sflags = reinterpret_cast<uint32_t *>(smem + L.scr + 264u);                // 8 words
-  float *sML = reinterpret_cast<float *>(smem + L.scr + 320u);                         // [G <= 32][2]
 
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
   uint32_t *err = p.ctrl + kCtrlErr;
@@ -444,12 +444,40 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_step_kernel(const __grid
     // ---- attention: split-K units, the last unit of a KV head merges ----
     if (ph < nb && kind == kPhAttn) {
       wait_phase(ph);
-      float *sQ = reinterpret_cast<float *>(aux);  // [G][D]
-      float *sS = sQ + G * D;                       // [G][chunk]
+      constexpr uint32_t KS = D / 16u;              // K-steps of a head row
+      const uint32_t HT = (G + 7u) / 8u;            // tiles of 8 heads
+      const uint32_t SST = p.chunk + 4u;            // row stride of sS (padded)
+      uint2 *sQB = reinterpret_cast<uint2 *>(aux);  // [HT][KS][2][32] q fragments
+      float *sS = reinterpret_cast<float *>(aux + HT * KS * 2u * 32u * 8u);  // [G][SST]
       for (uint32_t u = blockIdx.x; u < n_units; u += gridDim.x) {
         const AttnUnit a = attn_unit(p, u, nch, pos);
-        for (uint32_t i = cw * 32u + lane; i < G * D / 4u; i += NCT)
-          reinterpret_cast<float4 *>(sQ)[i] = __ldcg(reinterpret_cast<const float4 *>(p.q + (size_t)a.kvh * G * D) + i);
+        // q of the group as the B operand of the score MMAs (K = dims, N = 8
+        // heads per tile), split into fp16 hi + lo: entry [ht][ks][h][lane] =
+        // the lane's b0/b1 words (rows 2tq, 2tq+1 and 2tq+8, 2tq+9 of K-step
+        // ks, column gq = head ht * 8 + gq); heads beyond G are zero
+        for (uint32_t e = tid; e < HT * KS * 32u; e += NCT) {
+          const uint32_t ln = e & 31u, ks = (e >> 5) % KS, ht = (e >> 5) / KS;
+          const uint32_t g = ht * 8u + (ln >> 2), d0 = ks * 16u + (ln & 3u) * 2u;
+          float v[4] = {0.f, 0.f, 0.f, 0.f};
+          if (g < G) {
+            const float *qg = p.q + ((size_t)a.kvh * G + g) * D + d0;
+            v[0] = __ldcg(qg);
+            v[1] = __ldcg(qg + 1);
+            v[2] = __ldcg(qg + 8);
+            v[3] = __ldcg(qg + 9);
+          }
+          uint32_t hw[2], lw[2];
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const __half h0 = __float2half_rn(v[2 * j]), h1 = __float2half_rn(v[2 * j + 1]);
+            const __half l0 = __float2half_rn(v[2 * j] - __half2float(h0));
+            const __half l1 = __float2half_rn(v[2 * j + 1] - __half2float(h1));
+            hw[j] = pack_half2(h0, h1);
+            lw[j] = pack_half2(l0, l1);
+          }
+          sQB[((ht * KS + ks) * 2u + 0u) * 32u + ln] = make_uint2(hw[0], hw[1]);
+          sQB[((ht * KS + ks) * 2u + 1u) * 32u + ln] = make_uint2(lw[0], lw[1]);
+        }
         const uint32_t sK = rp.slot, pK = rp.phase;
         rp.next(R.nst);
         const uint32_t sV = rp.slot, pV = rp.phase;
@@ -460,96 +488,46 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_step_kernel(const __grid
         }
         __half *kS = reinterpret_cast<__half *>(R.ring + sK * R.slot);
         __half *vS = reinterpret_cast<__half *>(R.ring + sV * R.slot);
+        const uint32_t len16 = (a.len + 15u) & ~15u;
         if (a.staged < a.len) {
           // the current position's row was stored by this step's QKV phase
           const __half *kr = Ly.kc + ((size_t)a.kvh * p.ctx + pos) * D;
           const __half *vr = Ly.vc + ((size_t)a.kvh * p.ctx + pos) * D;
-          for (uint32_t i = cw * 32u + lane; i < D / 2u; i += NCT) {
+          for (uint32_t i = tid; i < D / 2u; i += NCT) {
             reinterpret_cast<uint32_t *>(kS + a.staged * D)[i] = __ldcg(reinterpret_cast<const unsigned int *>(kr) + i);
             reinterpret_cast<uint32_t *>(vS + a.staged * D)[i] = __ldcg(reinterpret_cast<const unsigned int *>(vr) + i);
           }
         }
+        // V rows past the chunk's end meet zero weights; make them zero too (not
+        // stale bytes, which may be NaN)
+        for (uint32_t i = a.len * D / 2u + tid; i < len16 * D / 2u; i += NCT) reinterpret_cast<uint32_t *>(vS)[i] = 0u;
         named_bar(1, NCT);
-        // scores (attn_scores.comp:27-44): warp per position, two positions at
-        // a time so their shuffle reductions overlap; lane holds DPL dims
-        auto kvec = [&](const __half *row, float (&f)[DPL]) {
-          if constexpr (DPL == 1) {
-            f[0] = __half2float(row[lane]);
-          } else if constexpr (DPL == 2) {
-            const float2 v = __half22float2(*reinterpret_cast<const __half2 *>(row + lane * 2));
-            f[0] = v.x;
-            f[1] = v.y;
-          } else {
-#pragma unroll
-            for (int d = 0; d < DPL; d += 4) {  // 8-byte aligned groups of 4 halves
-              const uint2 w = *reinterpret_cast<const uint2 *>(row + lane * DPL + d);
-              const float2 lo = __half22float2(*reinterpret_cast<const __half2 *>(&w.x));
-              const float2 hi = __half22float2(*reinterpret_cast<const __half2 *>(&w.y));
-              f[d] = lo.x;
-              f[d + 1] = lo.y;
-              f[d + 2] = hi.x;
-              f[d + 3] = hi.y;
-            }
+        // scores (attn_scores.comp:27-44): S[t][g] = K[t] . q[g] on the tensor
+        // cores, a warp per (16 positions, 8 heads) tile
+        for (uint32_t it = cw; it < (len16 / 16u) * HT; it += kMvConsumers) {
+          const uint32_t pt = it / HT, ht = it % HT;
+          float c[4] = {0.f, 0.f, 0.f, 0.f};
+          const __half *kb = kS + (pt * 16u + (lane & 15u)) * D + (lane >> 4) * 8u;
+#pragma unroll 4
+          for (uint32_t ks = 0; ks < KS; ++ks) {
+            uint32_t af[4];
+            ldmatrix_x4(af, kb + ks * 16u);
+            const uint2 bh = sQB[((ht * KS + ks) * 2u + 0u) * 32u + lane];
+            const uint2 bl = sQB[((ht * KS + ks) * 2u + 1u) * 32u + lane];
+            mma_f16(c, af, bh.x, bh.y);
+            mma_f16(c, af, bl.x, bl.y);
           }
-        };
-        // DPL consecutive floats at p (16-byte aligned when DPL % 4 == 0)
-        auto ld_f = [&](const float *src, float (&f)[DPL]) {
-          if constexpr (DPL % 4 == 0) {
+          const uint32_t t = pt * 16u + (lane >> 2), g = ht * 8u + (lane & 3u) * 2u;
 #pragma unroll
-            for (int d = 0; d < DPL; d += 4) {
-              const float4 v = *reinterpret_cast<const float4 *>(src + d);
-              f[d] = v.x;
-              f[d + 1] = v.y;
-              f[d + 2] = v.z;
-              f[d + 3] = v.w;
-            }
-          } else {
-#pragma unroll
-            for (int d = 0; d < DPL; ++d) f[d] = src[d];
-          }
-        };
-        for (uint32_t gb = 0; gb < G; gb += 8) {
-          // this lane's dims of q for 8 heads of the group, in registers
-          float qr[8][DPL];
-#pragma unroll
-          for (uint32_t i = 0; i < 8; ++i) {
-            if (gb + i < G) {
-              ld_f(sQ + (gb + i) * D + lane * DPL, qr[i]);
-            } else {
-#pragma unroll
-              for (int d = 0; d < DPL; ++d) qr[i][d] = 0.f;
-            }
-          }
-          for (uint32_t t = cw; t < a.len; t += 2u * kMvConsumers) {
-            const uint32_t t2 = t + kMvConsumers;
-            const bool two = t2 < a.len;
-            float kf[DPL], kg2[DPL];
-            kvec(kS + t * D, kf);
-            kvec(kS + (two ? t2 : t) * D, kg2);
-            float pa[8], pb[8];
-#pragma unroll
-            for (uint32_t i = 0; i < 8; ++i) {
-              float x = 0.f, y = 0.f;
-#pragma unroll
-              for (int d = 0; d < DPL; ++d) {
-                x = fmaf(qr[i][d], kf[d], x);
-                y = fmaf(qr[i][d], kg2[d], y);
-              }
-              pa[i] = x;
-              pb[i] = y;
-            }
-            const float ta = warp_sum8(pa, lane), tb = warp_sum8(pb, lane);
-            const uint32_t gi = gb + ((lane >> 2) & 7u);
-            if ((lane & 3u) == 0 && gi < G) {
-              sS[gi * p.chunk + t] = __fmul_rn(ta, p.attn_scale);
-              if (two) sS[gi * p.chunk + t2] = __fmul_rn(tb, p.attn_scale);
-            }
+          for (int j = 0; j < 4; ++j) {
+            const uint32_t tt = t + (j >> 1) * 8u, gg = g + (j & 1);
+            if (tt < a.len && gg < G) sS[gg * SST + tt] = __fmul_rn(c[j], p.attn_scale);
           }
         }
         named_bar(1, NCT);
         // chunk softmax (softmax.comp): warp per head; exp(s - m) replaces s
         for (uint32_t g0 = cw; g0 < G; g0 += kMvConsumers) {
-          float *sg = sS + g0 * p.chunk;
+          float *sg = sS + g0 * SST;
           float m = -INFINITY;
           for (uint32_t t = lane; t < a.len; t += 32) m = fmaxf(m, sg[t]);
           m = warp_max(m);
@@ -561,63 +539,51 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_step_kernel(const __grid
           }
           lsum = warp_sum(lsum);
           if (lane == 0) {
-            sML[2 * g0] = m;
-            sML[2 * g0 + 1] = lsum;
+            const size_t slot_i = ((size_t)a.kvh * p.max_chunks + a.c) * G + g0;
+            p.part_ml[slot_i] = make_float2(m, lsum);
           }
         }
         named_bar(1, NCT);
-        // values (attn_values.comp): warp w takes positions w, w + 8, ... for HB
-        // heads at a time, so every V row is read once; the warps' partial sums
-        // (HB * D floats each) meet in the K and V stage slots (free once read)
-        constexpr uint32_t HB = DPL >= 8 ? 4u : 8u;
-        for (uint32_t gb = 0; gb < G; gb += HB) {
-          float o[HB][DPL];
+        // values (attn_values.comp): O[g][d] = sum_t P[g][t] V[t][d] as
+        // (V^T)(P^T) on the tensor cores, a warp per (16 dims, 8 heads) tile;
+        // A = V^T from the V rows by transposing loads, B = P^T in fp16 hi + lo
+        for (uint32_t it = cw; it < KS * HT; it += kMvConsumers) {
+          const uint32_t dt = it / HT, ht = it % HT;
+          float c[4] = {0.f, 0.f, 0.f, 0.f};
+          const uint32_t gb = ht * 8u + (lane >> 2);  // head of this lane's B column
+          const float *pg = sS + (gb < G ? gb : 0u) * SST;
+          const __half *vb = vS + (((lane >> 4) & 1u) * 8u + (lane & 7u)) * D + dt * 16u + ((lane >> 3) & 1u) * 8u;
+          for (uint32_t kk = 0; kk < len16 / 16u; ++kk) {
+            uint32_t af[4];
+            ldmatrix_x4_trans(af, vb + kk * 16u * D);
+            float w[4];
+            const uint32_t t0w = kk * 16u + (lane & 3u) * 2u;
 #pragma unroll
-          for (uint32_t i = 0; i < HB; ++i)
-#pragma unroll
-            for (int d = 0; d < DPL; ++d) o[i][d] = 0.f;
-          for (uint32_t t = cw; t < a.len; t += kMvConsumers) {
-            float vf[DPL];
-            kvec(vS + t * D, vf);
-#pragma unroll
-            for (uint32_t i = 0; i < HB; ++i) {
-              const float pw = gb + i < G ? sS[(gb + i) * p.chunk + t] : 0.f;
-#pragma unroll
-              for (int d = 0; d < DPL; ++d) o[i][d] = fmaf(pw, vf[d], o[i][d]);
+            for (int j = 0; j < 4; ++j) {
+              const uint32_t tt = t0w + (j & 1) + (j >> 1) * 8u;
+              w[j] = (gb < G && tt < a.len) ? pg[tt] : 0.f;
             }
-          }
-          named_bar(1, NCT);  // every warp is done with V (and K)
-          // warp w's partials: [w][HB][D] floats, warps 0-3 in the K slot, 4-7 in the V slot
-          float *wp = reinterpret_cast<float *>((cw < 4u ? reinterpret_cast<uint8_t *>(kS) : reinterpret_cast<uint8_t *>(vS))) +
-                      (cw & 3u) * HB * D;
+            uint32_t bh[2], bl[2];
 #pragma unroll
-          for (uint32_t i = 0; i < HB; ++i) {
-            float *dst = wp + i * D + lane * DPL;
-            if constexpr (DPL % 4 == 0) {
-#pragma unroll
-              for (int d = 0; d < DPL; d += 4)
-                *reinterpret_cast<float4 *>(dst + d) = make_float4(o[i][d], o[i][d + 1], o[i][d + 2], o[i][d + 3]);
-            } else {
-#pragma unroll
-              for (int d = 0; d < DPL; ++d) dst[d] = o[i][d];
+            for (int j = 0; j < 2; ++j) {
+              const __half h0 = __float2half_rn(w[2 * j]), h1 = __float2half_rn(w[2 * j + 1]);
+              bh[j] = pack_half2(h0, h1);
+              bl[j] = pack_half2(__float2half_rn(w[2 * j] - __half2float(h0)),
+                                 __float2half_rn(w[2 * j + 1] - __half2float(h1)));
             }
+            mma_f16(c, af, bh[0], bh[1]);
+            mma_f16(c, af, bl[0], bl[1]);
           }
-          named_bar(1, NCT);
-          for (uint32_t e = cw * 32u + lane; e < HB * D; e += NCT) {
-            const uint32_t i = e / D;
-            if (gb + i >= G) continue;
-            float v = 0.f;
+          // c: dims dt * 16 + gq (+ 8), heads ht * 8 + 2tq (+ 1)
+          const uint32_t d = dt * 16u + (lane >> 2), g = ht * 8u + (lane & 3u) * 2u;
 #pragma unroll
-            for (uint32_t w = 0; w < kMvConsumers; ++w)
-              v += reinterpret_cast<const float *>(w < 4u ? reinterpret_cast<const uint8_t *>(kS) : reinterpret_cast<const uint8_t *>(vS))[(w & 3u) * HB * D + e];
-            const size_t slot_i = ((size_t)a.kvh * p.max_chunks + a.c) * G + gb + i;
-            p.part[slot_i * D + e % D] = v;
-            if (e % D == 0) p.part_ml[slot_i] = make_float2(sML[2 * (gb + i)], sML[2 * (gb + i) + 1]);
+          for (int j = 0; j < 4; ++j) {
+            const uint32_t dd = d + (j >> 1) * 8u, gg = g + (j & 1);
+            if (gg < G) p.part[(((size_t)a.kvh * p.max_chunks + a.c) * G + gg) * D + dd] = c[j];
           }
-          named_bar(1, NCT);  // slots reused by the next head group
         }
+        named_bar(1, NCT);  // every warp is done with the K and V stages
         // release the K and V stages
-        __syncwarp();
         if (lane == 0) {
           mbar_arrive(&R.empty[sK]);
           mbar_arrive(&R.empty[sV]);
@@ -628,58 +594,62 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_step_kernel(const __grid
         named_bar(1, NCT);
         if (sflags[0]) {
           // warp per query head: lanes hold the chunks' (max, sum) pairs, the
-          // weights go through shuffles, and 16 chunks' outputs are loaded at once
+          // weights go through shuffles, MB chunks' partial rows are loaded at
+          // once; the first MB rows and the first 64 pairs are loaded together
+          // (the rows do not depend on the max), then the chunks are summed in order
           for (uint32_t g0 = cw; g0 < G; g0 += kMvConsumers) {
             const size_t hb = (size_t)a.kvh * p.max_chunks * G + g0;  // slot of chunk 0
-            float M = -INFINITY;
-            for (uint32_t c = lane; c < nch; c += 32) M = fmaxf(M, __ldcg(&p.part_ml[hb + (size_t)c * G].x));
+            const float *ob = p.part + hb * D + lane * DPL;
+            constexpr uint32_t MB = DPL >= 8 ? 8u : 16u;  // chunks in flight (register budget)
+            float vs[MB][DPL];
+            auto load_rows = [&](uint32_t cb) {
+#pragma unroll
+              for (uint32_t k = 0; k < MB; ++k) {
+                const float *oc = ob + (size_t)(cb + k) * G * D;
+                if (cb + k < nch) {
+                  if constexpr (DPL % 4 == 0) {
+#pragma unroll
+                    for (int d = 0; d < DPL; d += 4) {
+                      const float4 v = __ldcg(reinterpret_cast<const float4 *>(oc + d));
+                      vs[k][d] = v.x;
+                      vs[k][d + 1] = v.y;
+                      vs[k][d + 2] = v.z;
+                      vs[k][d + 3] = v.w;
+                    }
+                  } else {
+#pragma unroll
+                    for (int d = 0; d < DPL; ++d) vs[k][d] = __ldcg(oc + d);
+                  }
+                }
+              }
+            };
+            auto ml_of = [&](uint32_t c) { return __ldcg(&p.part_ml[hb + (size_t)c * G]); };
+            load_rows(0);
+            const float2 mla = lane < nch ? ml_of(lane) : make_float2(-INFINITY, 0.f);
+            const float2 mlb = lane + 32u < nch ? ml_of(lane + 32u) : make_float2(-INFINITY, 0.f);
+            float M = fmaxf(mla.x, mlb.x);
+            for (uint32_t c = lane + 64u; c < nch; c += 32) M = fmaxf(M, ml_of(c).x);
             M = warp_max(M);
             float o[DPL];
 #pragma unroll
             for (int d = 0; d < DPL; ++d) o[d] = 0.f;
             float Lp = 0.f;
-            const float *ob = p.part + hb * D + lane * DPL;
             for (uint32_t c0 = 0; c0 < nch; c0 += 32) {
               float wl = 0.f;
               if (c0 + lane < nch) {
-                const float2 ml = __ldcg(&p.part_ml[hb + (size_t)(c0 + lane) * G]);
+                const float2 ml = c0 == 0 ? mla : c0 == 32 ? mlb : ml_of(c0 + lane);
                 wl = ml.x == -INFINITY ? 0.f : expf(ml.x - M);
                 Lp = fmaf(wl, ml.y, Lp);
               }
               const uint32_t nc = min(32u, nch - c0);
-              constexpr uint32_t MB = DPL >= 8 ? 8u : 16u;  // chunks in flight (register budget)
               for (uint32_t cb = 0; cb < nc; cb += MB) {
-                float4 v[MB][DPL / 4 > 0 ? DPL / 4 : 1];
-                float vs[MB][DPL];
-#pragma unroll
-                for (uint32_t k = 0; k < MB; ++k) {
-                  const float *oc = ob + (size_t)(c0 + cb + k) * G * D;
-                  if (cb + k < nc) {
-                    if constexpr (DPL % 4 == 0) {
-#pragma unroll
-                      for (int d = 0; d < DPL / 4; ++d) v[k][d] = __ldcg(reinterpret_cast<const float4 *>(oc) + d);
-                    } else {
-#pragma unroll
-                      for (int d = 0; d < DPL; ++d) vs[k][d] = __ldcg(oc + d);
-                    }
-                  }
-                }
+                if (c0 + cb != 0) load_rows(c0 + cb);
 #pragma unroll
                 for (uint32_t k = 0; k < MB; ++k) {
                   const float wc = __shfl_sync(0xffffffffu, wl, (cb + k) & 31u);
                   if (cb + k < nc) {
-                    if constexpr (DPL % 4 == 0) {
 #pragma unroll
-                      for (int d = 0; d < DPL / 4; ++d) {
-                        o[4 * d] = fmaf(wc, v[k][d].x, o[4 * d]);
-                        o[4 * d + 1] = fmaf(wc, v[k][d].y, o[4 * d + 1]);
-                        o[4 * d + 2] = fmaf(wc, v[k][d].z, o[4 * d + 2]);
-                        o[4 * d + 3] = fmaf(wc, v[k][d].w, o[4 * d + 3]);
-                      }
-                    } else {
-#pragma unroll
-                      for (int d = 0; d < DPL; ++d) o[d] = fmaf(wc, vs[k][d], o[d]);
-                    }
+                    for (int d = 0; d < DPL; ++d) o[d] = fmaf(wc, vs[k][d], o[d]);
                   }
                 }
               }
@@ -690,7 +660,7 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_step_kernel(const __grid
           }
           if (cw == 0 && lane == 0) p.tickets[a.kvh] = 0;
         }
-        named_bar(1, NCT);  // sQ / sS / sflags reuse by the next unit
+        named_bar(1, NCT);  // sQB / sS / sflags reuse by the next unit
       }
       arrive();
       continue;
