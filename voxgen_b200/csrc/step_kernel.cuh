@@ -334,19 +334,26 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_step_kernel(const __grid
         if (n) bulk_g2s(R.ring + rp.slot * R.slot, src, n * D * 2u, &R.full[rp.slot]);
         rp.next(R.nst);
       };
-      for (uint32_t l = 0; l < p.n_layers; ++l) {
-        const StepLayer &Ly = layers[l];
-        stream(Ly.qkv, p.g_qkv);
-        for (uint32_t u = blockIdx.x; u < n_units; u += gridDim.x) {
-          const AttnUnit a = attn_unit(p, u, nch, pos);
-          rows(Ly.kc + ((size_t)a.kvh * p.ctx + a.r0) * D, a.staged);
-          rows(Ly.vc + ((size_t)a.kvh * p.ctx + a.r0) * D, a.staged);
+      // the phases in order, each through one call site
+      for (uint32_t ph = 0; ph <= nb && live; ++ph) {
+        const uint32_t l = ph / kPhasesPerLayer, kind = ph - l * kPhasesPerLayer;
+        const StepLayer &Ly = layers[l < p.n_layers ? l : 0u];
+        if (ph < nb && kind == kPhAttn) {
+          for (uint32_t u = blockIdx.x; u < n_units; u += gridDim.x) {
+            const AttnUnit a = attn_unit(p, u, nch, pos);
+            for (uint32_t h = 0; h < 2; ++h) rows((h ? Ly.vc : Ly.kc) + ((size_t)a.kvh * p.ctx + a.r0) * D, a.staged);
+          }
+          continue;
         }
-        stream(Ly.o, p.g_o);
-        stream(Ly.gateup, p.g_gu);
-        stream(Ly.down, p.g_down);
+        if (ph == nb && !p.want_logits) break;
+        const uint8_t *w = p.head;
+        TileGeom g = p.g_head;
+        if (ph < nb) {
+          w = kind == kPhQkv ? Ly.qkv : kind == kPhO ? Ly.o : kind == kPhGu ? Ly.gateup : Ly.down;
+          g = kind == kPhQkv ? p.g_qkv : kind == kPhO ? p.g_o : kind == kPhGu ? p.g_gu : p.g_down;
+        }
+        stream(w, g);
       }
-      if (p.want_logits) stream(p.head, p.g_head);
       if (live) mv_drain(R, rp, err);
     }
     return;
@@ -423,7 +430,14 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_step_kernel(const __grid
     if (consume)
       mv_consume<WQ8>(R, rp, (t1 - t0) * NSEG, NSEG, SEGB, aux, p.plane, red, mp, t0, cw, lane, err, err, ok,
                       (rms && xout == nullptr) ? scr + 8 : nullptr,
-                      [&](uint32_t R0, float a, float b) { mv_epilogue_rt(mode, mp, R0, a, b, pos); });
+                      [&](uint32_t R0, float a, float b) {
+                        switch (mode) {
+                          case Mode::PLAIN: mv_epilogue<Mode::PLAIN>(mp, R0, a, b, pos); break;
+                          case Mode::RESID: mv_epilogue<Mode::RESID>(mp, R0, a, b, pos); break;
+                          case Mode::SWIGLU: mv_epilogue<Mode::SWIGLU>(mp, R0, a, b, pos); break;
+                          case Mode::QKV: mv_epilogue<Mode::QKV>(mp, R0, a, b, pos); break;
+                        }
+                      });
   };
 
   uint32_t tok = 0;
