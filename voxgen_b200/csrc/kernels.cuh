@@ -397,7 +397,7 @@ __device__ __forceinline__ void consumer_wait(const WaitSpec &w, uint32_t cw, ui
 }
 
 // Activation operand of a matvec in shared memory: Q8_0 -> three int8 digit
-// planes and the per-32-block power of two sx[]; F16 -> fp16 hi and lo planes
+// planes and the whole-vector power of two *sx; F16 -> fp16 hi and lo planes
 // and the whole-vector power of two *xscale. Run by the kMvConsumers consumer
 // warps (named barrier 1). The input vector (C elements) comes from src (its
 // token table when TAB); with RMS it is RMSNormed with normw, else copied. The wait comes after the RMSNorm
@@ -409,7 +409,7 @@ __device__ __forceinline__ void mv_activation(uint32_t C, uint32_t cols_pad, con
                                               const XSrc &src, const WaitSpec &wait, float *xout) {
   constexpr uint32_t NCT = kMvConsumers * 32;
   auto xload = [&](uint32_t k) { return xsrc_elem<TAB>(src, k); };
-  float *sx = reinterpret_cast<float *>(areg + 3u * plane);      // Q8: per-block 2^e
+  float *sx = reinterpret_cast<float *>(areg + 3u * plane);      // Q8: 2^e of the whole vector
   float *xscale = reinterpret_cast<float *>(areg + 2u * plane);  // F16: 2^e of the whole vector
   // Warp cw handles the groups of 4 consecutive 32-element blocks b with
   // (b / 4) % 8 == cw, i.e. 128 consecutive elements per group, 4 per lane:
@@ -510,14 +510,28 @@ __device__ __forceinline__ void mv_activation(uint32_t C, uint32_t cols_pad, con
     });
   }
   if constexpr (Q8) {
-    // int8 digits and the per-block power of two 2^e: v = x * 2^-e (|v| < 64,
-    // exact), n = round(v * 2^14) through the 1.5 * 2^23 constant (for |t| <
-    // 2^22, t + 1.5 * 2^23 rounds t to an integer and its bit pattern minus
-    // 0x4B400000 is that integer), then n = d0 * 2^14 + d1 * 2^7 + d2 with
-    // every digit in [-64, 64] by integer shifts.
+    // int8 digits and the whole-vector power of two 2^e (max|x| * 2^-e in
+    // [32, 64)): v = x * 2^-e (|v| < 64, exact), n = round(v * 2^14) through
+    // the 1.5 * 2^23 constant (for |t| < 2^22, t + 1.5 * 2^23 rounds t to an
+    // integer and its bit pattern minus 0x4B400000 is that integer), then n =
+    // d0 * 2^14 + d1 * 2^7 + d2 with every digit in [-64, 64] by integer shifts.
+    float m = 0.f;
+    each_group([&](uint32_t, const float4 &v) {
+      m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    });
+    m = warp_max(m);
+    named_bar(1, NCT);  // scr[] reuse after the RMSNorm reduction
+    if (lane == 0) scr[cw] = m;
+    named_bar(1, NCT);
+    float mx = 0.f;
+#pragma unroll
+    for (int w = 0; w < kMvConsumers; ++w) mx = fmaxf(mx, scr[w]);
+    int e = 0;
+    const bool nz = block_exponent(__float_as_uint(mx), e);
+    const float inv = nz ? pow2f(-e) : 0.f;
     constexpr float kRnd = 12582912.0f;
     constexpr int kRndBits = 0x4B400000;
-    auto split = [&](float x, float inv, int &q0, int &q1, int &q2) {
+    auto split = [&](float x, int &q0, int &q1, int &q2) {
       const int n = __float_as_int(fmaf(x * inv, 16384.0f, kRnd)) - kRndBits;
       q0 = (n + 8192) >> 14;
       const int r = n - (q0 << 14);
@@ -525,22 +539,11 @@ __device__ __forceinline__ void mv_activation(uint32_t C, uint32_t cols_pad, con
       q2 = r - (q1 << 7);
     };
     auto digits = [&](uint32_t g, const float4 &v) {
-      // block of this lane: group block q = lane / 8; max over its 8 lanes
-      uint32_t mb = max(max(__float_as_uint(fabsf(v.x)), __float_as_uint(fabsf(v.y))),
-                        max(__float_as_uint(fabsf(v.z)), __float_as_uint(fabsf(v.w))));
-      mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, 1));
-      mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, 2));
-      mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, 4));
-      int e = 0;
-      const bool nz = block_exponent(mb, e);
-      int q[3][4] = {};
-      if (nz) {
-        const float inv = pow2f(-e);
-        split(v.x, inv, q[0][0], q[1][0], q[2][0]);
-        split(v.y, inv, q[0][1], q[1][1], q[2][1]);
-        split(v.z, inv, q[0][2], q[1][2], q[2][2]);
-        split(v.w, inv, q[0][3], q[1][3], q[2][3]);
-      }
+      int q[3][4];
+      split(v.x, q[0][0], q[1][0], q[2][0]);
+      split(v.y, q[0][1], q[1][1], q[2][1]);
+      split(v.z, q[0][2], q[1][2], q[2][2]);
+      split(v.w, q[0][3], q[1][3], q[2][3]);
       const uint32_t k0 = elem0(g), b = k0 >> 5;
       if (b * 32u < cols_pad) {
         const uint32_t o = b * 32u + bfrag_byte_q8(k0 & 31u);  // 4 consecutive bytes
@@ -550,13 +553,11 @@ __device__ __forceinline__ void mv_activation(uint32_t C, uint32_t cols_pad, con
                                          __byte_perm((uint32_t)q[d][2], (uint32_t)q[d][3], 0x0040u), 0x5410u);
           *reinterpret_cast<uint32_t *>(areg + d * plane + o) = w;
         }
-        if ((lane & 7u) == 0) sx[b] = nz ? pow2f(e) : 0.f;
       }
     };
     each_group(digits);
-    // each warp consumes only its own blocks when tiles have a multiple of 4 segments
-    if ((cols_pad / (kSegSteps * 32u)) % kStageSegs != 0) named_bar(1, NCT);
-    else __syncwarp();
+    if (cw == 0 && lane == 0) *sx = nz ? pow2f(e) : 0.f;
+    named_bar(1, NCT);
   } else {
     // whole-vector power-of-two scale, then fp16 hi + lo
     float m = 0.f;
@@ -629,9 +630,14 @@ __device__ __forceinline__ void mv_consume(const MvRing &R, RingPos &rp, uint32_
   // 0 and mask it). Lane (gq, tq) receives D rows gq and gq + 8, columns 2tq
   // and 2tq + 1.
   const uint32_t gq = lane >> 2, tq = lane & 3u;
+  // Q8: columns 3-7 of B may hold anything (their sums are dropped: column 3
+  // by c7 = 0 in lane tq = 1, columns 4-7 by lane_scale = 0), so every lane
+  // loads a digit plane unmasked; F16: columns 2-7 are zero (masked), since
+  // fp16 products of arbitrary bytes need not be finite
   const bool brow = Q8 ? (gq < 3) : (gq < 2);
-  const uint8_t *bplane = areg + (brow ? gq : 0u) * plane;
-  const uint32_t bmask = brow ? 0xFFFFFFFFu : 0u;
+  const uint8_t *bplane = areg + (Q8 ? gq % 3u : (brow ? gq : 0u)) * plane;
+  const uint32_t bmask = (Q8 || brow) ? 0xFFFFFFFFu : 0u;
+  const float c7 = tq == 0 ? 0.0078125f : 0.f;
   // Q8_0: the int32 accumulator of the MMA starts at the bit pattern of
   // 1.5 * 2^23, so the result read as a float is 1.5 * 2^23 + S exactly
   // (|S| <= 32 * 127 * 64 < 2^22) and one exact subtraction gives S. Lane tq=0
@@ -641,6 +647,7 @@ __device__ __forceinline__ void mv_consume(const MvRing &R, RingPos &rp, uint32_
   constexpr int kMagicBits = 0x4B400000;
   constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
   const float lane_scale = Q8 ? (tq == 0 ? 1.f : tq == 1 ? 6.103515625e-05f : 0.f) : (tq == 0 ? 1.f : 0.f);
+  const float xsc = Q8 ? *sx : *xscale;  // the activation's power of two
   float acc0 = 0.f, acc1 = 0.f;
   float acc0b = 0.f, acc1b = 0.f;  // Q8_0: second chain when two stages are processed together
   float cf[2][4] = {};  // F16: two accumulator chains
@@ -650,8 +657,8 @@ __device__ __forceinline__ void mv_consume(const MvRing &R, RingPos &rp, uint32_
   auto flush = [&](uint32_t rel) {
     float v0, v1;
     if constexpr (Q8) {
-      v0 = (acc0 + acc0b) * lane_scale;
-      v1 = (acc1 + acc1b) * lane_scale;
+      v0 = (acc0 + acc0b) * (lane_scale * xsc);
+      v1 = (acc1 + acc1b) * (lane_scale * xsc);
     } else {
       v0 = (cf[0][0] + cf[0][1] + cf[1][0] + cf[1][1]) * lane_scale;
       v1 = (cf[0][2] + cf[0][3] + cf[1][2] + cf[1][3]) * lane_scale;
@@ -662,8 +669,8 @@ __device__ __forceinline__ void mv_consume(const MvRing &R, RingPos &rp, uint32_
     v1 += __shfl_xor_sync(0xffffffffu, v1, 2);
     if (tq == 0) {
       if constexpr (!Q8) {
-        v0 *= *xscale;
-        v1 *= *xscale;
+        v0 *= xsc;
+        v1 *= xsc;
       }
       red[(rel * kMvConsumers + cw) * kTileRows + gq] = v0;
       red[(rel * kMvConsumers + cw) * kTileRows + gq + 8u] = v1;
@@ -704,14 +711,10 @@ __device__ __forceinline__ void mv_consume(const MvRing &R, RingPos &rp, uint32_
         b1[nb][q] = bw.y & bmask;
       }
     if constexpr (Q8) {
-      // the scales of rows gq and gq + 8 for the 4 K-steps, and the 4 blocks' 2^e
+      // the scales of rows gq and gq + 8 for the 4 K-steps
       uint4 wsv[NB];
-      float4 xsv[NB];
 #pragma unroll
-      for (int nb = 0; nb < NB; ++nb) {
-        wsv[nb] = *reinterpret_cast<const uint4 *>(sgs[nb] + kSegQsBytes + gq * 32u + sq * 4u);
-        xsv[nb] = *reinterpret_cast<const float4 *>(sx + kss[nb]);
-      }
+      for (int nb = 0; nb < NB; ++nb) wsv[nb] = *reinterpret_cast<const uint4 *>(sgs[nb] + kSegQsBytes + gq * 32u + sq * 4u);
       int r[NB][4][4];
 #pragma unroll
       for (int nb = 0; nb < NB; ++nb)
@@ -720,15 +723,14 @@ __device__ __forceinline__ void mv_consume(const MvRing &R, RingPos &rp, uint32_
 #pragma unroll
       for (int nb = 0; nb < NB; ++nb) {
         const uint32_t wsw[4] = {wsv[nb].x, wsv[nb].y, wsv[nb].z, wsv[nb].w};
-        const float xs[4] = {xsv[nb].x, xsv[nb].y, xsv[nb].z, xsv[nb].w};
         float &A0 = nb == 0 ? acc0 : acc0b, &A1 = nb == 0 ? acc1 : acc1b;
 #pragma unroll
         for (uint32_t q = 0; q < 4; ++q) {
           const float2 w = __half22float2(*reinterpret_cast<const __half2 *>(&wsw[q]));
-          const float v0 = fmaf(__int_as_float(r[nb][q][1]) - kMagic, 0.0078125f, __int_as_float(r[nb][q][0]) - kMagic);
-          const float v1 = fmaf(__int_as_float(r[nb][q][3]) - kMagic, 0.0078125f, __int_as_float(r[nb][q][2]) - kMagic);
-          A0 = fmaf(v0, w.x * xs[q], A0);
-          A1 = fmaf(v1, w.y * xs[q], A1);
+          const float v0 = fmaf(__int_as_float(r[nb][q][1]) - kMagic, c7, __int_as_float(r[nb][q][0]) - kMagic);
+          const float v1 = fmaf(__int_as_float(r[nb][q][3]) - kMagic, c7, __int_as_float(r[nb][q][2]) - kMagic);
+          A0 = fmaf(v0, w.x, A0);
+          A1 = fmaf(v1, w.y, A1);
         }
       }
     } else {
@@ -747,6 +749,37 @@ __device__ __forceinline__ void mv_consume(const MvRing &R, RingPos &rp, uint32_
       ++rel;
     }
   };
+  if (NSEG % (2u * kStageSegs) == 0) {
+    // Tiles of an even number of stages: every iteration takes two stages of
+    // one tile (this warp's segment cw / 2 of each), every tile ends on a pair.
+    const uint32_t ntl = n_items / NSEG, spt = NSEG / kStageSegs;
+    for (uint32_t t = 0; t < ntl && ok; ++t) {
+      for (uint32_t j = 0; j < spt; j += 2) {
+        RingPos nx = rp;
+        nx.next(R.nst);
+        if (!mbar_wait_bounded(&R.full[rp.slot], rp.phase, abort_flag) ||
+            !mbar_wait_bounded(&R.full[nx.slot], nx.phase, abort_flag)) {
+          set_error(err, kErrConsumerWait);
+          ok = false;
+          break;
+        }
+        const uint32_t ks0 = (j * kStageSegs + (cw >> 1)) * kSegSteps + sq;
+        const uint8_t *const sgs[2] = {R.ring + rp.slot * R.slot + (cw >> 1) * SEGB,
+                                       R.ring + nx.slot * R.slot + (cw >> 1) * SEGB};
+        const uint32_t kss[2] = {ks0, ks0 + kStageSegs * kSegSteps};
+        run(std::integral_constant<int, 2>{}, sgs, kss);
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive(&R.empty[rp.slot]);
+          mbar_arrive(&R.empty[nx.slot]);
+        }
+        rp = nx;
+        rp.next(R.nst);
+      }
+      if (ok) flush(t);
+    }
+    cur = 0xFFFFFFFFu;  // flushed
+  } else
   for (uint32_t s = 0; s < n_items && ok; s += kStageSegs) {
     const uint32_t slot0 = rp.slot;
     if (!mbar_wait_bounded(&R.full[slot0], rp.phase, abort_flag)) {

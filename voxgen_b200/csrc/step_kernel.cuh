@@ -84,7 +84,7 @@ __device__ __forceinline__ void step_activation(uint32_t C, uint32_t cols_pad, b
                                                 const float *stw, float eps, uint8_t *areg, uint32_t plane,
                                                 float *scr, uint32_t cw, uint32_t lane, float *xout) {
   constexpr uint32_t NCT = kMvConsumers * 32;
-  float *sx = reinterpret_cast<float *>(areg + 3u * plane);      // Q8: per-block 2^e
+  float *sx = reinterpret_cast<float *>(areg + 3u * plane);      // Q8: 2^e of the whole vector
   float *xscale = reinterpret_cast<float *>(areg + 2u * plane);  // F16: 2^e of the whole vector
   // warp cw takes the groups of 128 elements g * 8 + cw, 4 per lane (mv_activation)
   const uint32_t NGRP = (cols_pad / 32u + 3u) / 4u;
@@ -141,10 +141,26 @@ __device__ __forceinline__ void step_activation(uint32_t C, uint32_t cols_pad, b
     if (k0 + 3u < C) xout[k0 + 3u] = v.w;
   };
   if constexpr (Q8) {
-    // int8 digits and the per-block 2^e (mv_activation)
+    // int8 digits and the whole-vector 2^e (mv_activation)
+    float m = 0.f;
+#pragma unroll 1
+    for (uint32_t g = 0; g < JG; ++g) {
+      const float4 v = xval(elem0(g));
+      m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    }
+    m = warp_max(m);
+    named_bar(1, NCT);  // scr[] reuse after the RMSNorm reduction
+    if (lane == 0) scr[cw] = m;
+    named_bar(1, NCT);
+    float mx = 0.f;
+#pragma unroll
+    for (int w = 0; w < kMvConsumers; ++w) mx = fmaxf(mx, scr[w]);
+    int e = 0;
+    const bool nz = block_exponent(__float_as_uint(mx), e);
+    const float inv = nz ? pow2f(-e) : 0.f;
     constexpr float kRnd = 12582912.0f;
     constexpr int kRndBits = 0x4B400000;
-    auto split = [&](float x, float inv, int &q0, int &q1, int &q2) {
+    auto split = [&](float x, int &q0, int &q1, int &q2) {
       const int n = __float_as_int(fmaf(x * inv, 16384.0f, kRnd)) - kRndBits;
       q0 = (n + 8192) >> 14;
       const int r = n - (q0 << 14);
@@ -156,21 +172,11 @@ __device__ __forceinline__ void step_activation(uint32_t C, uint32_t cols_pad, b
       const uint32_t k0 = elem0(g), b = k0 >> 5;
       const float4 v = xval(k0);
       put_xout(k0, v);
-      uint32_t mb = max(max(__float_as_uint(fabsf(v.x)), __float_as_uint(fabsf(v.y))),
-                        max(__float_as_uint(fabsf(v.z)), __float_as_uint(fabsf(v.w))));
-      mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, 1));
-      mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, 2));
-      mb = max(mb, __shfl_xor_sync(0xffffffffu, mb, 4));
-      int e = 0;
-      const bool nz = block_exponent(mb, e);
-      int q[3][4] = {};
-      if (nz) {
-        const float inv = pow2f(-e);
-        split(v.x, inv, q[0][0], q[1][0], q[2][0]);
-        split(v.y, inv, q[0][1], q[1][1], q[2][1]);
-        split(v.z, inv, q[0][2], q[1][2], q[2][2]);
-        split(v.w, inv, q[0][3], q[1][3], q[2][3]);
-      }
+      int q[3][4];
+      split(v.x, q[0][0], q[1][0], q[2][0]);
+      split(v.y, q[0][1], q[1][1], q[2][1]);
+      split(v.z, q[0][2], q[1][2], q[2][2]);
+      split(v.w, q[0][3], q[1][3], q[2][3]);
       if (b * 32u < cols_pad) {
         const uint32_t o = b * 32u + bfrag_byte_q8(k0 & 31u);  // 4 consecutive bytes
 #pragma unroll
@@ -179,12 +185,10 @@ __device__ __forceinline__ void step_activation(uint32_t C, uint32_t cols_pad, b
                                          __byte_perm((uint32_t)q[d][2], (uint32_t)q[d][3], 0x0040u), 0x5410u);
           *reinterpret_cast<uint32_t *>(areg + d * plane + o) = w;
         }
-        if ((lane & 7u) == 0) sx[b] = nz ? pow2f(e) : 0.f;
       }
     }
-    // each warp consumes only its own blocks when tiles have a multiple of 4 segments
-    if ((cols_pad / (kSegSteps * 32u)) % kStageSegs != 0) named_bar(1, NCT);
-    else __syncwarp();
+    if (cw == 0 && lane == 0) *sx = nz ? pow2f(e) : 0.f;
+    named_bar(1, NCT);
   } else {
     // whole-vector power-of-two scale, then fp16 hi + lo (mv_activation)
     float m = 0.f;
