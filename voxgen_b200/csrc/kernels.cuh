@@ -614,13 +614,15 @@ __device__ __noinline__ void mv_epilogue_rt(Mode mode, const MvParams &p, uint32
 }
 
 // Consumer side of a matvec over n_items ring segments (tiles t0.. of this
-// CTA's run). epilogue(R, a, b) receives the finished rows R and R + 8.
-template <bool Q8, class Epilogue>
+// CTA's run). epilogue(R, a, b, pv) receives the finished rows R and R + 8
+// and pv = pre(R); for the first tile of each warp pre runs before the K
+// loop, so the loads it makes overlap the loop.
+template <bool Q8, class Pre, class Epilogue>
 __device__ __forceinline__ void mv_consume(const MvRing &R, RingPos &rp, uint32_t n_items, uint32_t NSEG,
                                            uint32_t SEGB, const uint8_t *areg, uint32_t plane, float *red,
                                            const MvParams &p, uint32_t t0, uint32_t cw, uint32_t lane,
                                            const uint32_t *abort_flag, uint32_t *err, bool &ok,
-                                           const float *defer_ss, Epilogue epilogue) {
+                                           const float *defer_ss, Pre pre, Epilogue epilogue) {
   constexpr uint32_t NCT = kMvConsumers * 32;
   const float *sx = reinterpret_cast<const float *>(areg + 3u * plane);
   const float *xscale = reinterpret_cast<const float *>(areg + 2u * plane);
@@ -695,6 +697,9 @@ __device__ __forceinline__ void mv_consume(const MvRing &R, RingPos &rp, uint32_
     ++rel;
   }
   uint32_t cur = 0xFFFFFFFFu;  // tile (relative) of the accumulated partial
+  const uint32_t ntiles = (n_items + NSEG - 1) / NSEG;
+  float2 pv0 = make_float2(0.f, 0.f);
+  if (lane < 8 && cw < ntiles) pv0 = pre((t0 + cw) * kTileRows + lane);
   // K-steps of NB stages (segment bases sgs, first K-steps kss): all
   // shared-memory loads first, then the NB * 4 independent MMAs, then the rescale
   auto run = [&](auto nbc, const uint8_t *const (&sgs)[2], const uint32_t (&kss)[2]) {
@@ -839,7 +844,6 @@ __device__ __forceinline__ void mv_consume(const MvRing &R, RingPos &rp, uint32_
   }
   // Tile reduction and epilogue: tile rel goes to warp rel % 8, lanes 0-7
   // take rows (l, l + 8), summing the 8 warps' partials in order.
-  const uint32_t ntiles = (n_items + NSEG - 1) / NSEG;
   for (uint32_t t = cw; t < ntiles; t += kMvConsumers) {
     if (lane < 8) {
       float a = 0.f, b = 0.f;
@@ -848,7 +852,8 @@ __device__ __forceinline__ void mv_consume(const MvRing &R, RingPos &rp, uint32_
         a += red[(t * kMvConsumers + w) * kTileRows + lane];
         b += red[(t * kMvConsumers + w) * kTileRows + lane + 8u];
       }
-      epilogue((t0 + t) * kTileRows + lane, a * row_scale, b * row_scale);
+      const uint32_t R0 = (t0 + t) * kTileRows + lane;
+      epilogue(R0, a * row_scale, b * row_scale, t == cw ? pv0 : pre(R0));
     }
   }
 }
@@ -907,7 +912,8 @@ __global__ void __launch_bounds__(kMvThreads, 1) matvec_kernel(const __grid_cons
   RingPos rp;
   mv_consume<Q8>(R, rp, n_items, NSEG, SEGB, smem + L.a, p.plane, red, p, t0, cw, lane, nullptr, err, ok,
                  P == Pro::RMSNORM ? scr + 8 : nullptr,
-                 [&](uint32_t R0, float a, float b) { mv_epilogue<M>(p, R0, a, b, pos); });
+                 [](uint32_t) { return make_float2(0.f, 0.f); },
+                 [&](uint32_t R0, float a, float b, float2) { mv_epilogue<M>(p, R0, a, b, pos); });
 }
 
 // ---------------------------------------------------------------------------

@@ -103,12 +103,20 @@ __device__ __forceinline__ void step_activation(uint32_t C, uint32_t cols_pad, b
   // when there is no xout (mv_activation)
   const bool defer = rms && xout == nullptr;
   float inv_rms = 1.0f;
+  // with the factor deferred, the sum of squares and the operand's largest
+  // magnitude come from one pass; the operand is then x * w
+  float mdef = 0.f;
   if (rms) {
     float ss = 0.f;
 #pragma unroll 1
     for (uint32_t g = 0; g < JG; ++g) {
       const float4 v = ld4(stg, elem0(g));
       ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+      if (defer) {
+        const float4 w = ld4(stw, elem0(g));
+        mdef = fmaxf(mdef, fmaxf(fmaxf(fabsf(__fmul_rn(v.x, w.x)), fabsf(__fmul_rn(v.y, w.y))),
+                                 fmaxf(fabsf(__fmul_rn(v.z, w.z)), fabsf(__fmul_rn(v.w, w.w)))));
+      }
     }
     ss = warp_sum(ss);
     if (defer) {
@@ -142,14 +150,16 @@ __device__ __forceinline__ void step_activation(uint32_t C, uint32_t cols_pad, b
   };
   if constexpr (Q8) {
     // int8 digits and the whole-vector 2^e (mv_activation)
-    float m = 0.f;
+    float m = mdef;
+    if (!defer) {
 #pragma unroll 1
-    for (uint32_t g = 0; g < JG; ++g) {
-      const float4 v = xval(elem0(g));
-      m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+      for (uint32_t g = 0; g < JG; ++g) {
+        const float4 v = xval(elem0(g));
+        m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+      }
     }
     m = warp_max(m);
-    named_bar(1, NCT);  // scr[] reuse after the RMSNorm reduction
+    if (rms && !defer) named_bar(1, NCT);  // scr[] reuse after the RMSNorm reduction
     if (lane == 0) scr[cw] = m;
     named_bar(1, NCT);
     float mx = 0.f;
@@ -191,14 +201,16 @@ __device__ __forceinline__ void step_activation(uint32_t C, uint32_t cols_pad, b
     named_bar(1, NCT);
   } else {
     // whole-vector power-of-two scale, then fp16 hi + lo (mv_activation)
-    float m = 0.f;
+    float m = mdef;
+    if (!defer) {
 #pragma unroll 1
-    for (uint32_t g = 0; g < JG; ++g) {
-      const float4 v = xval(elem0(g));
-      m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+      for (uint32_t g = 0; g < JG; ++g) {
+        const float4 v = xval(elem0(g));
+        m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+      }
     }
     m = warp_max(m);
-    named_bar(1, NCT);  // scr[] reuse after the RMSNorm reduction
+    if (rms && !defer) named_bar(1, NCT);  // scr[] reuse after the RMSNorm reduction
     if (lane == 0) scr[cw] = m;
     named_bar(1, NCT);
     float mx = 0.f;
@@ -434,10 +446,21 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_step_kernel(const __grid
     if (consume)
       mv_consume<WQ8>(R, rp, (t1 - t0) * NSEG, NSEG, SEGB, aux, p.plane, red, mp, t0, cw, lane, err, err, ok,
                       (rms && xout == nullptr) ? scr + 8 : nullptr,
-                      [&](uint32_t R0, float a, float b) {
+                      [&](uint32_t R0) {  // the residual, in flight during the K loop
+                        float2 v = make_float2(0.f, 0.f);
+                        if (mode == Mode::RESID) {
+                          if (R0 < mp.g.rows) v.x = __ldcg(mp.resid + R0);
+                          if (R0 + 8u < mp.g.rows) v.y = __ldcg(mp.resid + R0 + 8u);
+                        }
+                        return v;
+                      },
+                      [&](uint32_t R0, float a, float b, float2 pv) {
                         switch (mode) {
                           case Mode::PLAIN: mv_epilogue<Mode::PLAIN>(mp, R0, a, b, pos); break;
-                          case Mode::RESID: mv_epilogue<Mode::RESID>(mp, R0, a, b, pos); break;
+                          case Mode::RESID:  // residual_rmsnorm.comp:27
+                            if (R0 < mp.g.rows) mp.out[R0] = __fadd_rn(pv.x, __fmul_rn(a, mp.alpha));
+                            if (R0 + 8u < mp.g.rows) mp.out[R0 + 8u] = __fadd_rn(pv.y, __fmul_rn(b, mp.alpha));
+                            break;
                           case Mode::SWIGLU: mv_epilogue<Mode::SWIGLU>(mp, R0, a, b, pos); break;
                           case Mode::QKV: mv_epilogue<Mode::QKV>(mp, R0, a, b, pos); break;
                         }
