@@ -181,6 +181,44 @@ int vg_decode_embedding(vg_stream *stream, const float *host_embedding,
                         int want_logits);
 int vg_decode_embedding_device(vg_stream *stream, const float *device_embedding,
                                int want_logits);
+
+/* ---- ResidualLM + FSQ + fusion (acoustic GGUF) -----------------------------
+ * vg_residual_load_gguf replaces ResidualFsqEngine::new (src/acoustic.rs:
+ * 435-560) with AcousticConfig::from_gguf's checks (:59-187): the acoustic
+ * GGUF's residual_lm.blk.N.* layers, fsq.{in,out}_proj and
+ * projections.res_fusion_proj, F16 matrices, against the BaseLM model base
+ * (same heads, head_dim, FFN width and epsilon; no RoPE). The result is a
+ * vg_model with no token table and no LM head: vg_stream_create gives it a
+ * KV cache (max_context <= 8192), vg_stream_output its final normalised
+ * hidden state, vg_stream_reset / vg_stream_position work as for BaseLM.
+ *   vg_residual_step:      one position, step_record_submit / _gpu_only
+ *                          (:851-900): with fsq_applied the LM state is
+ *                          FSQ(base) (record_fsq :921-944), else the raw base
+ *                          hidden (text prefix); the layers take
+ *                          res_fusion_proj([LM state | embed]) + bias
+ *                          (record_fusion :946-966; embed NULL = zeros), then
+ *                          record_residual_lm (:968-1035). Device fp32[H]
+ *                          inputs, read in stream order.
+ *   vg_residual_step_host: the same with host inputs; returns once the step
+ *                          is enqueued and the inputs are copied.
+ *   vg_residual_state:     device fp32[H] buffers of the last step: the FSQ
+ *                          output, the fusion output (fusion_snapshot) and the
+ *                          LM state (current_lm). The buffers stay valid until
+ *                          the stream is destroyed. */
+enum {
+  VG_RESIDUAL_FSQ_OUTPUT = 0,
+  VG_RESIDUAL_FUSED_INPUT = 1,
+  VG_RESIDUAL_LM_STATE = 2
+};
+int vg_residual_load_gguf(vg_ctx *ctx, const char *acoustic_path, const vg_model *base,
+                          vg_model **out);
+int vg_residual_step(vg_stream *stream, const float *device_base_hidden,
+                     const float *device_embed, int fsq_applied);
+int vg_residual_step_host(vg_stream *stream, const float *base_hidden, const float *embed,
+                          int fsq_applied);
+int vg_residual_state(const vg_stream *stream, int which, const float **device_buffer);
+/* Host copy of n <= H floats of one of those buffers, after the stream's work. */
+int vg_residual_copy_state(vg_stream *stream, int which, float *host, size_t n);
 /* prefill_tokens (src/baselm.rs:823-839): n decode_token steps, logits on the
  * last one only when want_logits_last is set. */
 int vg_prefill_tokens(vg_stream *stream, const uint32_t *tokens, uint32_t n,

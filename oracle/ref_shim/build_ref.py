@@ -36,9 +36,12 @@ OUT_DIR = ORACLE / "_ref"
 LIB = OUT_DIR / "libvoxgen_ref.so"
 DEFAULT_REFERENCE = Path("/root/reference")
 
-# The normal (non-_xtx7900) shaders that BaseLM's decode step records (baselm.rs:892-1052).
+# The normal (non-_xtx7900) shaders that BaseLM's decode step records (baselm.rs:892-1052),
+# and the three ResidualLM adds around the same layers (acoustic.rs:921-966): FSQ's linear
+# layers with bias, its quantiser, and the fusion projection.
 SHADERS = ["embedding", "rmsnorm", "residual_rmsnorm", "qkv_matvec", "rope", "store_kv",
-           "attn_scores", "softmax", "attn_values", "matvec", "matvec_swiglu"]
+           "attn_scores", "softmax", "attn_values", "matvec", "matvec_swiglu",
+           "linear_bias", "fsq_quantize", "fusion_linear"]
 
 _BUF = re.compile(r"layout\s*\(([^)]*)\)\s*((?:(?:readonly|writeonly|coherent|restrict|volatile)\s+)*)"
                   r"buffer\s+(\w+)\s*\{\s*(\w+)\s+(\w+)\s*\[\s*\]\s*;\s*\}\s*(\w+)\s*;")

@@ -8,7 +8,7 @@
 // unpackHalf2x16 (low half in .x), packHalf2x16 (round to nearest even, the
 // conversion the oracle and the CUDA path use), inversesqrt as 1/sqrt.
 // Translation units that include this header must not include <cmath> or
-// <math.h>: the unqualified exp/pow/cos/sin/max/min calls of a shader have to
+// <math.h>: the unqualified exp/pow/cos/sin/tanh/round/max/min calls of a shader have to
 // resolve to the float overloads below.
 //
 // Workgroup model: every invocation of a workgroup is a fiber on one host
@@ -31,6 +31,8 @@ float powf(float, float);
 float cosf(float);
 float sinf(float);
 float sqrtf(float);
+float tanhf(float);
+float roundf(float);
 }
 
 inline float exp(float x) { return expf(x); }
@@ -38,6 +40,9 @@ inline float pow(float x, float y) { return powf(x, y); }
 inline float cos(float x) { return cosf(x); }
 inline float sin(float x) { return sinf(x); }
 inline float inversesqrt(float x) { return 1.0f / sqrtf(x); }
+inline float tanh(float x) { return tanhf(x); }
+// GLSL leaves the direction of halves to the implementation; roundf takes them away from zero.
+inline float round(float x) { return roundf(x); }
 inline float max(float a, float b) { return a < b ? b : a; }
 inline float min(float a, float b) { return b < a ? b : a; }
 inline uint max(uint a, uint b) { return a < b ? b : a; }
@@ -60,6 +65,13 @@ inline vec2 unpackHalf2x16(uint v) {
 inline uint packHalf2x16(vec2 v) { return vgref::float_to_half(v.x) | (vgref::float_to_half(v.y) << 16); }
 inline void barrier() { vgref::barrier(); }
 
+// The shaders declare only local_size_x, so y and z of the global id are the group's.
+inline uvec3 vgref_global_id(uint local_size_x) {
+  uvec3 g = vgref::group_id();
+  g.x = g.x * local_size_x + vgref::local_id().x;
+  return g;
+}
+#define gl_GlobalInvocationID (vgref_global_id(vgref_local_size))
 #define gl_LocalInvocationID (::vgref::local_id())
 #define gl_WorkGroupID (::vgref::group_id())
 #define gl_NumWorkGroups (::vgref::num_groups())

@@ -37,7 +37,12 @@ EXPORTS = [
     "vg_copy_output", "vg_copy_logits", "vg_stream_sync", "vg_step_result_get", "vg_benchmark",
     "vg_stream_profile_step", "vg_decode_batch", "vg_k_packed_bytes", "vg_k_repack", "vg_k_matvec", "vg_k_embedding",
     "vg_k_residual_rmsnorm", "vg_k_attention", "vg_k_attention_noalloc",
+    "vg_residual_load_gguf", "vg_residual_step", "vg_residual_step_host", "vg_residual_state",
+    "vg_residual_copy_state",
 ]
+
+# which buffer vg_residual_state / vg_residual_copy_state return
+RESIDUAL_STATE = {"fsq_output": 0, "fused_input": 1, "lm_state": 2}
 
 
 class VoxGenError(RuntimeError):
@@ -126,6 +131,11 @@ def lib() -> C.CDLL:
         "vg_k_residual_rmsnorm": ([P, P, P, U32, F, F, P, P], I),
         "vg_k_attention": ([P, P, P, U32, U32, U32, U32, U32, P, P], I),
         "vg_k_attention_noalloc": ([P, P, P, U32, U32, U32, U32, U32, P, P], I),
+        "vg_residual_load_gguf": ([P, C.c_char_p, P, PP], I),
+        "vg_residual_step": ([P, P, P, I], I),
+        "vg_residual_step_host": ([P, P, P, I], I),
+        "vg_residual_state": ([P, I, PP], I),
+        "vg_residual_copy_state": ([P, I, P, SZ], I),
     }
     for name, (args, res) in sig.items():
         f = getattr(L, name)
@@ -215,6 +225,22 @@ class Model:
         if getattr(self, "h", None):
             lib().vg_model_destroy(self.h)
             self.h = None
+
+
+class ResidualModel(Model):
+    """The ResidualLM + FSQ + fusion weights of an acoustic GGUF, following a BaseLM ``base``
+    (ResidualFsqEngine::new, src/acoustic.rs:435-560)."""
+
+    def __init__(self, ctx: Context, acoustic_path, base: Model):
+        self.ctx = ctx
+        h = C.c_void_p()
+        ctx.check(lib().vg_residual_load_gguf(ctx.h, str(acoustic_path).encode(), base.h, C.byref(h)))
+        self.h = h
+        info = ModelInfo()
+        ctx.check(lib().vg_model_info_get(h, C.byref(info)))
+        self.info = info.as_dict()
+        self.path = Path(acoustic_path)
+        self.base = base
 
 
 @dataclass
@@ -384,3 +410,36 @@ def decode_batch(engines: Sequence[BaseLmEngine], tokens: Sequence[int]) -> None
     rc = lib().vg_decode_batch(arr, len(engines), _ptr(t))
     if rc:
         engines[0]._check(rc)
+
+
+class ResidualEngine(BaseLmEngine):
+    """A ResidualLM session: KV cache and the FSQ / fusion / layer launches of one position.
+
+    ``step`` is step_record_submit_gpu_only (src/acoustic.rs:851-869): ``fsq_applied`` selects
+    FSQ(BaseLM hidden) as the LM state, else the raw BaseLM hidden (a text-prefix position);
+    ``embed`` is the current acoustic embedding (None = zeros). ``output`` is the final
+    normalised hidden state; ``state`` reads the FSQ output, the fusion output and the LM state.
+    """
+
+    def step(self, base_hidden, embed=None, fsq_applied: bool = True) -> None:
+        if isinstance(base_hidden, int):  # device pointers
+            self._check(lib().vg_residual_step(self.h, C.c_void_p(base_hidden),
+                                               C.c_void_p(embed) if embed is not None else None,
+                                               1 if fsq_applied else 0))
+            return
+        b = np.ascontiguousarray(base_hidden, np.float32)
+        e = np.ascontiguousarray(embed, np.float32) if embed is not None else None
+        if b.size != self.H or (e is not None and e.size != self.H):
+            raise ValueError(f"ResidualLM inputs must have {self.H} values")
+        self._check(lib().vg_residual_step_host(self.h, _ptr(b), _ptr(e) if e is not None else None,
+                                                1 if fsq_applied else 0))
+
+    def state(self, which: str) -> np.ndarray:
+        out = np.empty(self.H, np.float32)
+        self._check(lib().vg_residual_copy_state(self.h, RESIDUAL_STATE[which], _ptr(out), self.H))
+        return out
+
+    def state_buffer(self, which: str) -> int:
+        p = C.c_void_p()
+        self._check(lib().vg_residual_state(self.h, RESIDUAL_STATE[which], C.byref(p)))
+        return p.value

@@ -254,6 +254,12 @@ struct vg_model {
   bool rope_ok = true;
   vg_model_info info{};
   int streams = 0;
+  // ResidualLM + FSQ + fusion of an acoustic GGUF (vg_residual_load_gguf):
+  // the layers above, no token table or LM head, no RoPE
+  bool residual = false;
+  AcousticConfig acoustic;
+  DevMat fsq_in, fsq_out, fuse;  // [latent x H], [H x latent], [H x 2H]
+  float *fsq_in_b = nullptr, *fsq_out_b = nullptr, *fuse_b = nullptr;
 };
 
 struct vg_stream {
@@ -282,6 +288,12 @@ struct vg_stream {
   uint32_t step_smem = 0, step_grid = 0;
   bool step_head_apart = false;  // the LM head is stored in another format: own launch after the step
   MvPlan step_head{};
+  // ResidualLM streams: the BaseLM hidden state in, the FSQ latent, the FSQ
+  // output, the fusion input [left | right], its output (snapshot), the LM
+  // state (post-FSQ or raw BaseLM hidden), and the three matvec plans
+  float *res_base = nullptr, *res_embed = nullptr, *fsq_lat = nullptr, *fsq_res = nullptr, *fuse_in = nullptr,
+        *fused = nullptr, *cur_lm = nullptr;
+  MvPlan fsq_in_p{}, fsq_out_p{}, fuse_p{};
 };
 
 namespace {
@@ -334,7 +346,7 @@ void fill_info(vg_model *m) {
   uint64_t lw = 0;
   for (uint32_t l = 0; l < c.block_count; ++l)
     for (const char *s : {"attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up", "ffn_down"})
-      lw += m->summary.find(strf("blk.%u.%s.weight", l, s))->bytes;
+      lw += m->summary.find(strf(m->residual ? "residual_lm.blk.%u.%s.weight" : "blk.%u.%s.weight", l, s))->bytes;
   i.layer_weight_bytes = lw;
   i.norm_weight_bytes = (uint64_t)(2 * c.block_count + 1) * c.embedding_length * 4;
   i.device_weight_bytes = m->arena_bytes;
@@ -456,6 +468,139 @@ void load_model(vg_model *m, const std::string &path, uint32_t requested) {
     }
     CK(cudaMemcpy(m->inv_freq, inv.data(), inv.size() * 4, cudaMemcpyHostToDevice));
     CK(cudaMemcpy(m->ext, ext.data(), ext.size() * 4, cudaMemcpyHostToDevice));
+  } catch (...) {
+    munmap(map, S.file_bytes);
+    if (staging) cudaFree(staging);
+    if (st) cudaStreamDestroy(st);
+    throw;
+  }
+  munmap(map, S.file_bytes);
+  cudaFree(staging);
+  cudaStreamDestroy(st);
+  fill_info(m);
+}
+
+// The ResidualLM + FSQ + fusion part of an acoustic GGUF
+// (ResidualFsqEngine::new, src/acoustic.rs:435-560), following the BaseLM
+// model base: its layers are repacked exactly like the BaseLM's, the step
+// kernel runs them with RoPE off (inv_freq = 0 makes the rotation (1, 0)),
+// and FSQ and the fusion projection are matvecs with the bias as residual.
+void load_residual_model(vg_model *m, const std::string &path, const vg_model *base) {
+  m->summary = load_summary(path);
+  const GgufSummary &S = m->summary;
+  m->acoustic = acoustic_from_gguf(S, base->cfg);
+  m->residual = true;
+  BaseLmConfig c = base->cfg;
+  c.block_count = m->acoustic.residual_block_count;
+  c.vocab_size = 0;
+  c.context_length = 8192;  // VOXCPM2_MAX_GENERATION_CONTEXT, src/acoustic.rs:72-76
+  c.rope_scaling_type = "none";
+  c.format = GGML_F16;
+  c.tied_output = true;
+  c.output_tensor.clear();
+  m->cfg = c;
+  const uint32_t H = c.embedding_length, F = c.feed_forward_length, KV = c.kv_dim;
+  const uint32_t QR = c.head_count * c.head_dim, LAT = m->acoustic.fsq_latent_dim;
+  auto tensor = [&](const std::string &n) -> const TensorInfo & { return *S.find(n); };
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    size_t o = off;
+    off = round_up_sz(off + bytes, 256);
+    return o;
+  };
+  struct Pending {
+    DevMat *mat;
+    size_t off;
+  };
+  std::vector<Pending> mats;
+  std::vector<std::pair<float **, size_t>> vecs;
+  m->layers.resize(c.block_count);
+  for (uint32_t l = 0; l < c.block_count; ++l) {
+    Layer &L = m->layers[l];
+    L.qkv = make_mat(QR + 2 * KV, H, GGML_F16);
+    L.o = make_mat(H, QR, GGML_F16);
+    L.gateup = make_mat(2 * F, H, GGML_F16);
+    L.down = make_mat(H, F, GGML_F16);
+    for (DevMat *d : {&L.qkv, &L.o, &L.gateup, &L.down}) mats.push_back({d, take(d->g.bytes())});
+    vecs.push_back({&L.attn_norm, take((size_t)H * 4)});
+    vecs.push_back({&L.ffn_norm, take((size_t)H * 4)});
+  }
+  m->fsq_in = make_mat(LAT, H, GGML_F16);
+  m->fsq_out = make_mat(H, LAT, GGML_F16);
+  m->fuse = make_mat(H, 2 * H, GGML_F16);
+  for (DevMat *d : {&m->fsq_in, &m->fsq_out, &m->fuse}) mats.push_back({d, take(d->g.bytes())});
+  vecs.push_back({&m->fsq_in_b, take((size_t)LAT * 4)});
+  vecs.push_back({&m->fsq_out_b, take((size_t)H * 4)});
+  vecs.push_back({&m->fuse_b, take((size_t)H * 4)});
+  vecs.push_back({&m->out_norm, take((size_t)H * 4)});
+  vecs.push_back({&m->inv_freq, take((size_t)c.head_dim / 2 * 4)});
+  vecs.push_back({&m->ext, take((size_t)c.head_dim / 2 * 4)});
+  m->arena_bytes = off;
+  CK(cudaMalloc(&m->arena, m->arena_bytes));
+  for (auto &p : mats) p.mat->w = m->arena + p.off;
+  CK(cudaMemset(m->arena, 0, m->arena_bytes));  // tile padding stays zero
+  for (auto &v : vecs) *v.first = reinterpret_cast<float *>(m->arena + v.second);
+
+  int fd = ::open(path.c_str(), O_RDONLY);
+  if (fd < 0) fail(VG_EIO, "open " + path + " failed");
+  void *map = mmap(nullptr, S.file_bytes, PROT_READ, MAP_PRIVATE, fd, 0);
+  ::close(fd);
+  if (map == MAP_FAILED) fail(VG_EIO, "mmap " + path + " failed");
+  const uint8_t *data = static_cast<const uint8_t *>(map) + S.data_offset;
+  size_t max_raw = 0;
+  for (const auto &t : S.tensors) max_raw = std::max<size_t>(max_raw, t.bytes);
+  uint8_t *staging = nullptr;
+  cudaStream_t st = nullptr;
+  try {
+    CK(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+    CK(cudaMalloc(&staging, max_raw));
+    auto repack = [&](const std::string &name, const DevMat &dst, uint32_t row0, uint32_t perm, uint32_t group,
+                      uint32_t half) {
+      const TensorInfo &t = tensor(name);
+      CK(cudaMemcpyAsync(staging, data + t.offset, t.bytes, cudaMemcpyHostToDevice, st));
+      const uint32_t rows = (uint32_t)t.dims[1];
+      if (row0 % kTileRows) fail(VG_EUNSUPPORTED, "tensor " + name + " does not start on a tile boundary");
+      TileGeom sub = dst.g;
+      sub.rows = dst.g.rows - row0;
+      repack_kernel<<<std::min<uint32_t>(rows, 65535u), 256, 0, st>>>(
+          staging, rows, sub, dst.w + dst.g.seg_base(row0, 0), perm, group, half);
+      CK(cudaGetLastError());
+      CK(cudaStreamSynchronize(st));
+    };
+    // vectors as fp32 (the biases may be stored F16: load_scalar, linear_bias.comp)
+    auto upload_vec = [&](const std::string &name, float *dst) {
+      const TensorInfo &t = tensor(name);
+      std::vector<float> v(t.elements);
+      for (uint64_t i = 0; i < t.elements; ++i)
+        v[i] = t.type == GGML_F32 ? reinterpret_cast<const float *>(data + t.offset)[i]
+                                  : __half2float(reinterpret_cast<const __half *>(data + t.offset)[i]);
+      CK(cudaMemcpy(dst, v.data(), v.size() * 4, cudaMemcpyHostToDevice));
+    };
+    for (uint32_t l = 0; l < c.block_count; ++l) {
+      Layer &L = m->layers[l];
+      auto nm = [&](const char *x) { return strf("residual_lm.blk.%u.%s.weight", l, x); };
+      repack(nm("attn_q"), L.qkv, 0, kPermRope, c.head_dim, 0);
+      repack(nm("attn_k"), L.qkv, QR, kPermRope, c.head_dim, 0);
+      repack(nm("attn_v"), L.qkv, QR + KV, kPermIdentity, 0, 0);
+      repack(nm("attn_output"), L.o, 0, kPermIdentity, 0, 0);
+      repack(nm("ffn_gate"), L.gateup, 0, kPermHalves, 0, 0);
+      repack(nm("ffn_up"), L.gateup, 0, kPermHalves, 0, 1);
+      repack(nm("ffn_down"), L.down, 0, kPermIdentity, 0, 0);
+      upload_vec(nm("attn_norm"), L.attn_norm);
+      upload_vec(nm("ffn_norm"), L.ffn_norm);
+    }
+    repack("fsq.in_proj.weight", m->fsq_in, 0, kPermIdentity, 0, 0);
+    repack("fsq.out_proj.weight", m->fsq_out, 0, kPermIdentity, 0, 0);
+    repack("projections.res_fusion_proj.weight", m->fuse, 0, kPermIdentity, 0, 0);
+    upload_vec("fsq.in_proj.bias", m->fsq_in_b);
+    upload_vec("fsq.out_proj.bias", m->fsq_out_b);
+    upload_vec("projections.res_fusion_proj.bias", m->fuse_b);
+    upload_vec("residual_lm.output_norm.weight", m->out_norm);
+    // no RoPE (record_residual_lm, src/acoustic.rs:968-970): angle 0, factor 1
+    std::vector<float> inv(c.head_dim / 2, 0.0f), ext(c.head_dim / 2, 1.0f);
+    CK(cudaMemcpy(m->inv_freq, inv.data(), inv.size() * 4, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(m->ext, ext.data(), ext.size() * 4, cudaMemcpyHostToDevice));
+    m->rope_ok = true;
   } catch (...) {
     munmap(map, S.file_bytes);
     if (staging) cudaFree(staging);
@@ -631,7 +776,7 @@ std::string plan_step(vg_stream *s) {
   }
   const uint32_t grid = (uint32_t)m->ctx->sms;
   uint32_t segb = 0, plane = 0, cpad = 0, rb = 1;
-  s->step_head_apart = m->out.type != type;
+  s->step_head_apart = m->out.g.rows > 0 && m->out.type != type;
   if (s->step_head_apart) s->step_head = plan_matvec<Mode::PLAIN, Pro::COPY>(m->out, dev, (uint32_t)m->ctx->sms);
   for (const TileGeom *g : {&p.g_qkv, &p.g_o, &p.g_gu, &p.g_down, &p.g_head}) {
     if (g == &p.g_head && s->step_head_apart) continue;
@@ -731,6 +876,7 @@ uint8_t *staging_slot(vg_stream *s) {
 cudaEvent_t staging_event(vg_stream *s) { return s->pin_ev[(s->pin_next + kStagingSlots - 1) % kStagingSlots]; }
 
 void launch_step(vg_stream *s, bool token_input, bool logits) {
+  if (logits && s->m->cfg.vocab_size == 0) fail(VG_EUNSUPPORTED, "this model has no LM head");
   cudaGraphExec_t g = s->step_graph ? get_graph(s, token_input, logits) : nullptr;
   if (g)
     CK(cudaGraphLaunch(g, s->st));
@@ -962,6 +1108,10 @@ int vg_stream_create(vg_model *m, uint32_t max_context, vg_stream **out) {
                  o_sp = take((size_t)c.head_count_kv * nch * G * D * 4),
                  o_sml = take((size_t)c.head_count_kv * nch * G * 8),
                  o_stk = take((size_t)c.head_count_kv * 4);
+    const uint32_t LAT = m->residual ? m->acoustic.fsq_latent_dim : 0u, HR = m->residual ? H : 0u;
+    const size_t o_rb = take((size_t)HR * 4), o_re = take((size_t)HR * 4), o_rl = take((size_t)LAT * 4),
+                 o_rf = take((size_t)HR * 4), o_ri = take((size_t)HR * 8), o_rs = take((size_t)HR * 4),
+                 o_rc = take((size_t)HR * 4);
     CK(cudaMalloc(&s->dev_block, off));
     CK(cudaMemset(s->dev_block, 0, off));
     uint8_t *b = static_cast<uint8_t *>(s->dev_block);
@@ -975,6 +1125,30 @@ int vg_stream_create(vg_model *m, uint32_t max_context, vg_stream **out) {
     s->logits = (float *)(b + o_lg);
     s->part = (float *)(b + o_part);
     s->tickets = (uint32_t *)(b + o_tk);
+    if (m->residual) {
+      s->res_base = (float *)(b + o_rb);
+      s->res_embed = (float *)(b + o_re);
+      s->fsq_lat = (float *)(b + o_rl);
+      s->fsq_res = (float *)(b + o_rf);
+      s->fuse_in = (float *)(b + o_ri);
+      s->fused = (float *)(b + o_rs);
+      s->cur_lm = (float *)(b + o_rc);
+      const int dev = m->ctx->device;
+      const uint32_t sms = (uint32_t)m->ctx->sms;
+      // linear_bias.comp / fusion_linear.comp: (W x + bias), the bias as the residual
+      auto plan = [&](const DevMat &w, const float *x, float *y, const float *bias) {
+        MvPlan pl = plan_matvec<Mode::RESID, Pro::COPY>(w, dev, sms);
+        pl.p.xsrc = x;
+        pl.p.out = y;
+        pl.p.resid = bias;
+        pl.p.alpha = 1.0f;
+        pl.p.ctrl = s->ctrl;
+        return pl;
+      };
+      s->fsq_in_p = plan(m->fsq_in, s->res_base, s->fsq_lat, m->fsq_in_b);
+      s->fsq_out_p = plan(m->fsq_out, s->fsq_lat, s->fsq_res, m->fsq_out_b);
+      s->fuse_p = plan(m->fuse, s->fuse_in, s->fused, m->fuse_b);
+    }
     if (s->use_step) {
       StepParams &p = s->sp;
       std::vector<StepLayer> tab(c.block_count);
@@ -1171,6 +1345,116 @@ int vg_decode_embedding_device(vg_stream *s, const float *dev, int want_logits) 
     CK(cudaSetDevice(s->m->ctx->device));
     CK(cudaMemcpyAsync(s->hid_a, dev, (size_t)s->m->cfg.embedding_length * 4, cudaMemcpyDeviceToDevice, s->st));
     launch_step(s, false, want_logits != 0);
+    return VG_OK;
+  });
+}
+
+// ---- ResidualLM + FSQ + fusion (acoustic GGUF) -------------------------------
+
+int vg_residual_load_gguf(vg_ctx *ctx, const char *path, const vg_model *base, vg_model **out) {
+  if (!live(ctx) || !live(base)) return VG_ESTATE;
+  if (!path || !out) return VG_EINVAL;
+  *out = nullptr;
+  if (base->residual || base->ctx != ctx) return VG_EINVAL;
+  vg_model *m = new vg_model();
+  m->ctx = ctx;
+  int rc = guard(ctx, [&] {
+    CK(cudaSetDevice(ctx->device));
+    load_residual_model(m, path, base);
+    return VG_OK;
+  });
+  if (rc) {
+    if (m->arena) cudaFree(m->arena);
+    delete m;
+    return rc;
+  }
+  live_add(m);
+  *out = m;
+  return VG_OK;
+}
+
+namespace {
+// One ResidualLM position (step_record_submit, src/acoustic.rs:851-900): with
+// fsq_applied, FSQ(BaseLM hidden) (record_fsq :921-944) becomes the LM state,
+// else the raw BaseLM hidden does (a text-prefix position); the fusion
+// projection of [LM state | current acoustic embedding] (record_fusion
+// :946-966) is the input of the ResidualLM layers (record_residual_lm
+// :968-1035). res_base and res_embed hold the step's inputs.
+void residual_enqueue(vg_stream *s, bool embed_given, bool fsq_applied) {
+  vg_model *m = s->m;
+  const uint32_t H = m->cfg.embedding_length, LAT = m->acoustic.fsq_latent_dim;
+  const float *left = s->res_base;
+  if (fsq_applied) {
+    CK(run_matvec(s->fsq_in_p, s->st, false));
+    fsq_quantize_kernel<<<(LAT + 255) / 256, 256, 0, s->st>>>(s->fsq_lat, LAT, m->acoustic.fsq_scale);
+    CK(cudaGetLastError());
+    CK(run_matvec(s->fsq_out_p, s->st, false));
+    left = s->fsq_res;
+  }
+  CK(cudaMemcpyAsync(s->cur_lm, left, (size_t)H * 4, cudaMemcpyDeviceToDevice, s->st));
+  CK(cudaMemcpyAsync(s->fuse_in, left, (size_t)H * 4, cudaMemcpyDeviceToDevice, s->st));
+  if (embed_given)
+    CK(cudaMemcpyAsync(s->fuse_in + H, s->res_embed, (size_t)H * 4, cudaMemcpyDeviceToDevice, s->st));
+  else
+    CK(cudaMemsetAsync(s->fuse_in + H, 0, (size_t)H * 4, s->st));  // zero_embed
+  CK(run_matvec(s->fuse_p, s->st, false));
+  CK(cudaMemcpyAsync(s->hid_a, s->fused, (size_t)H * 4, cudaMemcpyDeviceToDevice, s->st));
+  launch_step(s, false, false);
+}
+}  // namespace
+
+int vg_residual_step(vg_stream *s, const float *dev_base_hidden, const float *dev_embed, int fsq_applied) {
+  if (!live(s)) return VG_ESTATE;
+  if (!dev_base_hidden) return VG_EINVAL;
+  if (!s->m->residual) return VG_EINVAL;
+  return guard(s->m->ctx, [&] {
+    check_step(s);
+    CK(cudaSetDevice(s->m->ctx->device));
+    const size_t bytes = (size_t)s->m->cfg.embedding_length * 4;
+    CK(cudaMemcpyAsync(s->res_base, dev_base_hidden, bytes, cudaMemcpyDeviceToDevice, s->st));
+    if (dev_embed) CK(cudaMemcpyAsync(s->res_embed, dev_embed, bytes, cudaMemcpyDeviceToDevice, s->st));
+    residual_enqueue(s, dev_embed != nullptr, fsq_applied != 0);
+    return VG_OK;
+  });
+}
+
+int vg_residual_step_host(vg_stream *s, const float *base_hidden, const float *embed, int fsq_applied) {
+  if (!live(s)) return VG_ESTATE;
+  if (!base_hidden) return VG_EINVAL;
+  if (!s->m->residual) return VG_EINVAL;
+  return guard(s->m->ctx, [&] {
+    check_step(s);
+    CK(cudaSetDevice(s->m->ctx->device));
+    const size_t bytes = (size_t)s->m->cfg.embedding_length * 4;
+    CK(cudaMemcpyAsync(s->res_base, base_hidden, bytes, cudaMemcpyHostToDevice, s->st));
+    if (embed) CK(cudaMemcpyAsync(s->res_embed, embed, bytes, cudaMemcpyHostToDevice, s->st));
+    residual_enqueue(s, embed != nullptr, fsq_applied != 0);
+    CK(cudaStreamSynchronize(s->st));  // the host buffers may be reused on return
+    return VG_OK;
+  });
+}
+
+int vg_residual_state(const vg_stream *s, int which, const float **dev) {
+  if (!live(s)) return VG_ESTATE;
+  if (!dev || !s->m->residual) return VG_EINVAL;
+  switch (which) {
+    case VG_RESIDUAL_FSQ_OUTPUT: *dev = s->fsq_res; return VG_OK;
+    case VG_RESIDUAL_FUSED_INPUT: *dev = s->fused; return VG_OK;
+    case VG_RESIDUAL_LM_STATE: *dev = s->cur_lm; return VG_OK;
+  }
+  return VG_EINVAL;
+}
+
+int vg_residual_copy_state(vg_stream *s, int which, float *host, size_t n) {
+  if (!live(s)) return VG_ESTATE;
+  if (!host || !s->m->residual || n > s->m->cfg.embedding_length) return VG_EINVAL;
+  const float *dev = nullptr;
+  int rc = vg_residual_state(s, which, &dev);
+  if (rc) return rc;
+  return guard(s->m->ctx, [&] {
+    CK(cudaSetDevice(s->m->ctx->device));
+    CK(cudaStreamSynchronize(s->st));
+    CK(cudaMemcpy(host, dev, n * 4, cudaMemcpyDeviceToHost));
     return VG_OK;
   });
 }

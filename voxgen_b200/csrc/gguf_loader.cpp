@@ -25,6 +25,15 @@ static std::string fmt(const char *f, ...) {
 }
 
 [[noreturn]] static void fail(int code, const std::string &msg) { throw Error{code, msg}; }
+static std::string strf(const char *f, ...) __attribute__((format(printf, 1, 2)));
+static std::string strf(const char *f, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, f);
+  vsnprintf(buf, sizeof buf, f, ap);
+  va_end(ap);
+  return buf;
+}
 
 const TensorInfo *GgufSummary::find(const std::string &name) const {
   for (const auto &t : tensors)
@@ -426,6 +435,71 @@ void check_kernel_support(const GgufSummary &s, const BaseLmConfig &c) {
   }
   const TensorInfo &tok = *s.find("token_embd.weight");
   if (!cols_ok(tok.type, tok.dims[0])) fail(VG_EUNSUPPORTED, "token_embd.weight row width not supported");
+}
+
+AcousticConfig acoustic_from_gguf(const GgufSummary &s, const BaseLmConfig &base) {
+  AcousticConfig a;
+  const MetaValue *arch = meta(s, {"general.architecture"});
+  a.architecture = arch && arch->kind == MetaValue::TEXT ? arch->text : std::string();
+  if (a.architecture != "voxcpm-acoustic")  // src/acoustic.rs:64-67
+    fail(VG_EINVAL, "expected general.architecture=voxcpm-acoustic for the acoustic GGUF, got \"" + a.architecture + "\"");
+  if (!meta_f32(s, {"voxcpm.model_version"}, a.model_version) || std::fabs(a.model_version - 2.0f) > 0.01f)
+    fail(VG_EUNSUPPORTED, "the acoustic GGUF must be VoxCPM2 acoustic v2.0 (voxcpm.model_version)");
+  const MetaValue *nr = meta(s, {"voxcpm.residual_lm.no_rope"});
+  if (!meta_u32(s, {"voxcpm.residual_lm.n_layer"}, a.residual_block_count) ||
+      !meta_u32(s, {"voxcpm.residual_lm.n_embd"}, a.embedding_length) ||
+      !meta_u32(s, {"voxcpm.fsq.latent_dim"}, a.fsq_latent_dim) || !meta_f32(s, {"voxcpm.fsq.scale"}, a.fsq_scale) ||
+      !nr || nr->kind != MetaValue::NUMBER)
+    fail(VG_EINVAL, "acoustic GGUF metadata is missing voxcpm.residual_lm.* or voxcpm.fsq.* keys");
+  a.no_rope = nr->number != 0;
+  if (!a.no_rope) fail(VG_EUNSUPPORTED, "VoxCPM2 ResidualLM must run with no_rope=true");  // src/acoustic.rs:969
+  if (a.residual_block_count == 0 || a.fsq_latent_dim == 0)
+    fail(VG_EINVAL, "acoustic GGUF declares an empty ResidualLM or FSQ latent");
+  if (a.embedding_length != base.embedding_length)  // src/acoustic.rs:92-99
+    fail(VG_EINVAL, strf("BaseLM geometry is incompatible with ResidualLM: n_embd %u vs BaseLM %u",
+                         a.embedding_length, base.embedding_length));
+  if (!std::isfinite(a.fsq_scale) || a.fsq_scale <= 0.0f) fail(VG_EINVAL, strf("invalid FSQ scale %g", a.fsq_scale));
+  for (const auto &t : s.tensors)  // validate_acoustic_f16, src/gguf.rs:150-160
+    if (t.type != GGML_F32 && t.type != GGML_F16)
+      fail(VG_EUNSUPPORTED, "unsupported acoustic tensor type in " + t.name + "; the F16 acoustic GGUF is required");
+  const uint32_t H = a.embedding_length, L = a.fsq_latent_dim, KV = base.kv_dim, F = base.feed_forward_length;
+  auto need = [&](const std::string &name) -> const TensorInfo & {
+    const TensorInfo *t = s.find(name);
+    if (!t) fail(VG_EINVAL, "acoustic GGUF is missing tensor " + name);
+    return *t;
+  };
+  auto matrix = [&](const std::string &name, uint32_t cols, uint32_t rows) {  // require_matrix, :189-205
+    const TensorInfo &t = need(name);
+    if (t.dims.size() != 2 || t.dims[0] != cols || t.dims[1] != rows)
+      fail(VG_EINVAL, strf("tensor %s does not have dimensions [%u, %u]", name.c_str(), cols, rows));
+    if (t.type != GGML_F16) fail(VG_EUNSUPPORTED, "tensor " + name + " must be F16");
+  };
+  auto vector = [&](const std::string &name, uint32_t n, bool f32_only, bool allow_f32) {  // require_vector, :207-216
+    const TensorInfo &t = need(name);
+    if (t.dims.size() != 1 || t.dims[0] != n) fail(VG_EINVAL, strf("tensor %s does not have dimensions [%u]", name.c_str(), n));
+    if (f32_only ? t.type != GGML_F32 : !(t.type == GGML_F16 || (allow_f32 && t.type == GGML_F32)))
+      fail(VG_EUNSUPPORTED, "tensor " + name + " has an unsupported type");
+  };
+  matrix("fsq.in_proj.weight", H, L);
+  vector("fsq.in_proj.bias", L, false, false);
+  matrix("fsq.out_proj.weight", L, H);
+  vector("fsq.out_proj.bias", H, false, false);
+  matrix("projections.res_fusion_proj.weight", 2 * H, H);
+  vector("projections.res_fusion_proj.bias", H, false, false);
+  vector("residual_lm.output_norm.weight", H, true, true);
+  for (uint32_t l = 0; l < a.residual_block_count; ++l) {
+    auto p = [&](const char *sfx) { return strf("residual_lm.blk.%u.%s", l, sfx); };
+    vector(p("attn_norm.weight"), H, true, true);
+    vector(p("ffn_norm.weight"), H, true, true);
+    matrix(p("attn_q.weight"), H, base.head_count * base.head_dim);
+    matrix(p("attn_k.weight"), H, KV);
+    matrix(p("attn_v.weight"), H, KV);
+    matrix(p("attn_output.weight"), base.head_count * base.head_dim, H);
+    matrix(p("ffn_gate.weight"), H, F);
+    matrix(p("ffn_up.weight"), H, F);
+    matrix(p("ffn_down.weight"), F, H);
+  }
+  return a;
 }
 
 }  // namespace vg

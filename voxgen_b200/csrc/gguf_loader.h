@@ -56,6 +56,18 @@ struct BaseLmConfig {
   bool rope_long() const { return context_length > rope_original_context_length; }
 };
 
+// The ResidualLM + FSQ + fusion part of an acoustic GGUF (AcousticConfig,
+// src/acoustic.rs:59-187), checked against the BaseLM it follows. The
+// reference accepts only 8 layers, 2048 wide, a 512-wide FSQ latent; this
+// loader takes any geometry the kernels support and the same tensor table.
+struct AcousticConfig {
+  std::string architecture;
+  float model_version = 0;
+  uint32_t residual_block_count = 0, embedding_length = 0, fsq_latent_dim = 0;
+  bool no_rope = false;
+  float fsq_scale = 0;
+};
+
 // Thrown (inside the library only) with a VG_* status and message.
 struct Error {
   int code;
@@ -69,5 +81,8 @@ uint32_t primary_base_format(const GgufSummary &s);         // throws Error
 BaseLmConfig config_from_gguf(const GgufSummary &s, uint32_t requested_format);
 // Geometry limits of the CUDA kernels (head_dim, alignment of row widths, ...).
 void check_kernel_support(const GgufSummary &s, const BaseLmConfig &c);
+// Parses and validates the acoustic GGUF's ResidualLM/FSQ/fusion tensors
+// against the BaseLM geometry (heads, head_dim, FFN width, epsilon).
+AcousticConfig acoustic_from_gguf(const GgufSummary &s, const BaseLmConfig &base);
 
 }  // namespace vg

@@ -226,6 +226,15 @@ __device__ __forceinline__ void rope_pair(float &a, float &b, uint32_t pos, uint
   b = b2;
 }
 
+// FSQ quantisation in place (fsq_quantize.comp:8-11): x = round(tanh(x) * scale)
+// / scale. GLSL leaves the rounding of halves to the implementation; roundf
+// rounds them away from zero.
+__global__ void fsq_quantize_kernel(float *x, uint32_t n, float scale) {
+  const uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  x[i] = __fdiv_rn(roundf(__fmul_rn(tanhf(x[i]), scale)), scale);
+}
+
 // Power-of-two scale 2^e for a block whose largest magnitude has fp32 bits
 // `mbits`, chosen so that max|x| * 2^-e lies in [32, 64). Returns false for a
 // block that is zero or below 2^-117 in magnitude (treated as zero).

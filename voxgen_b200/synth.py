@@ -234,3 +234,97 @@ def hidden_inputs(spec: ModelSpec, n: int, seed_index: int = 2000) -> np.ndarray
 def token_ids(spec: ModelSpec, n: int, seed_index: int = 3000) -> np.ndarray:
     """Uniform random token ids in [0, vocab)."""
     return _rng(spec.seed, seed_index).integers(0, spec.vocab, size=n, dtype=np.uint32)
+
+
+# ---- acoustic GGUF: ResidualLM + FSQ + fusion ----------------------------------------------
+
+@dataclass(frozen=True)
+class AcousticSpec:
+    """A synthetic acoustic GGUF (general.architecture = voxcpm-acoustic) whose ResidualLM
+    follows the BaseLM ``base``: F16 matrices and biases ~N(0, 0.02), fp32 norms 1 + N(0, 0.01)
+    (the tensor table AcousticConfig::validate_tensors checks, src/acoustic.rs:128-187)."""
+    name: str
+    base: ModelSpec
+    layers: int = 2
+    latent: int = 64
+    fsq_scale: float = 9.0
+    seed: int = 40
+    alignment: int = 32
+
+
+ACOUSTIC_PRESETS: Dict[str, AcousticSpec] = {
+    # head_dim 32 (GQA 4) like "tiny"; F16 layers as the acoustic GGUF requires
+    "res_tiny": AcousticSpec("res_tiny", PRESETS["tiny_f16"], layers=2, latent=64, seed=41),
+    # the VoxCPM2 shape: 8 layers, 2048 wide, FSQ latent 512, over cfg2's BaseLM geometry
+    "res_cfg2": AcousticSpec("res_cfg2", PRESETS["cfg2"], layers=8, latent=512, seed=42),
+}
+
+
+def _f16_vector(spec: AcousticSpec, n: int, index: int) -> Callable[[], np.ndarray]:
+    return lambda: (_rng(spec.seed, index).standard_normal(n, dtype=np.float32) * 0.02).astype(np.float16)
+
+
+def _f16_mat(spec: AcousticSpec, rows: int, cols: int, index: int) -> Callable[[], np.ndarray]:
+    return lambda: f16_matrix(_rng(spec.seed, index), rows, cols)
+
+
+def build_acoustic_gguf(spec: AcousticSpec) -> Tuple[GgufFile, List[Tuple[str, Tuple[int, ...], int, Callable]]]:
+    b = spec.base
+    H, F, KV, QR, L = b.hidden, b.ffn, b.kv_dim, b.heads * b.head_dim, spec.latent
+    meta = {
+        "general.architecture": "voxcpm-acoustic",
+        "general.name": f"voxgen-b200-synthetic-{spec.name}",
+        "voxcpm.model_version": F32(2.0),
+        "voxcpm.residual_lm.n_layer": U32(spec.layers),
+        "voxcpm.residual_lm.n_embd": U32(H),
+        "voxcpm.residual_lm.no_rope": True,
+        "voxcpm.fsq.latent_dim": U32(L),
+        "voxcpm.fsq.scale": F32(spec.fsq_scale),
+    }
+    g = GgufFile(metadata=meta, alignment=spec.alignment)
+    plan: List[Tuple[str, Tuple[int, ...], int, Callable]] = []
+
+    def add(name, dims, ty, gen):
+        plan.append((name, tuple(dims), ty, gen))
+
+    add("fsq.in_proj.weight", (H, L), GGML_F16, _f16_mat(spec, L, H, 1))
+    add("fsq.in_proj.bias", (L,), GGML_F16, _f16_vector(spec, L, 2))
+    add("fsq.out_proj.weight", (L, H), GGML_F16, _f16_mat(spec, H, L, 3))
+    add("fsq.out_proj.bias", (H,), GGML_F16, _f16_vector(spec, H, 4))
+    add("projections.res_fusion_proj.weight", (2 * H, H), GGML_F16, _f16_mat(spec, H, 2 * H, 5))
+    add("projections.res_fusion_proj.bias", (H,), GGML_F16, _f16_vector(spec, H, 6))
+    add("residual_lm.output_norm.weight", (H,), GGML_F32, lambda: norm_vector(_rng(spec.seed, 7), H))
+    for layer in range(spec.layers):
+        base = 16 + 16 * layer
+        p = f"residual_lm.blk.{layer}."
+        add(p + "attn_norm.weight", (H,), GGML_F32, (lambda i: lambda: norm_vector(_rng(spec.seed, i), H))(base))
+        add(p + "attn_q.weight", (H, QR), GGML_F16, _f16_mat(spec, QR, H, base + 1))
+        add(p + "attn_k.weight", (H, KV), GGML_F16, _f16_mat(spec, KV, H, base + 2))
+        add(p + "attn_v.weight", (H, KV), GGML_F16, _f16_mat(spec, KV, H, base + 3))
+        add(p + "attn_output.weight", (QR, H), GGML_F16, _f16_mat(spec, H, QR, base + 4))
+        add(p + "ffn_norm.weight", (H,), GGML_F32, (lambda i: lambda: norm_vector(_rng(spec.seed, i), H))(base + 5))
+        add(p + "ffn_gate.weight", (H, F), GGML_F16, _f16_mat(spec, F, H, base + 6))
+        add(p + "ffn_up.weight", (H, F), GGML_F16, _f16_mat(spec, F, H, base + 7))
+        add(p + "ffn_down.weight", (F, H), GGML_F16, _f16_mat(spec, H, F, base + 8))
+    return g, plan
+
+
+def acoustic_model_path(spec: AcousticSpec, cache_dir: Optional[Path] = None) -> Path:
+    """Generates (once) and returns the acoustic GGUF path of ``spec``."""
+    from .gguf import Tensor
+    d = Path(cache_dir or os.environ.get("VOXGEN_MODEL_CACHE", "/tmp/voxgen_b200_models"))
+    d.mkdir(parents=True, exist_ok=True)
+    p = d / f"{spec.name}-{spec_digest(spec)}.gguf"
+    if not p.exists():
+        g, plan = build_acoustic_gguf(spec)
+        for name, dims, ty, gen in plan:
+            g.tensors.append(Tensor(name, dims, ty, _Deferred(storage_bytes(ty, int(np.prod(dims))), gen)))
+        tmp = Path(str(p) + f".tmp{os.getpid()}")
+        write_gguf(tmp, g)
+        tmp.replace(p)
+    return p
+
+
+def acoustic_preset(name: str, **overrides) -> AcousticSpec:
+    spec = ACOUSTIC_PRESETS[name]
+    return replace(spec, **overrides) if overrides else spec
