@@ -7,6 +7,7 @@ Workloads (seeded synthetic models):
   cfg3            cfg2 with F16 projections
   cfg1            24 layers at H=1024 (config[0]'s layer), F16 token table, 128-token prefill
   cfg0            config[0]: one layer at H=1024, 512 prior positions
+  residual        ResidualLM + FSQ + fusion at VoxCPM2's shape (8 layers, H=2048, F16), positions/s
 
 A step is one decode token of one stream. `value` is the whole-job aggregate tok/s over all
 GPUs (independent replicas, weights replicated, no collectives on the data path), device-timed
@@ -40,6 +41,9 @@ WORKLOADS = {
     "cfg3": dict(preset="cfg3", prefill=1023, ctx=4096, desc="BaseLM 28L H2048 16x128 GQA 2 KV F6144 F16"),
     "cfg1": dict(preset="cfg1", prefill=128, ctx=512, desc="BaseLM 24L H1024 16x64 GQA 2 KV F4096 Q8_0"),
     "cfg0": dict(preset="cfg0", prefill=512, ctx=1024, desc="one BaseLM layer H1024 16x64 GQA 2 KV F4096 Q8_0"),
+    # ResidualLM + FSQ + fusion after BaseLM (src/acoustic.rs:851-1035), VoxCPM2's shape
+    "residual": dict(acoustic="res_cfg2", prefill=0, ctx=4096,
+                     desc="ResidualLM 8L H2048 16x128 GQA 2 KV F6144 F16 + FSQ 512 + fusion"),
 }
 
 
@@ -203,9 +207,128 @@ def cpu_baseline_sample(args, spec, path, wl):
                       f"({el:.1f} s, C restatement of the reference shaders, OpenMP)"}
 
 
+def run_residual(args, rank, world, local):
+    """ResidualLM positions per second: one step is FSQ(BaseLM hidden) + fusion + the ResidualLM
+    layers (an audio position), device-timed over K steps with device-resident inputs; e2e
+    copies the step's BaseLM hidden and acoustic embedding from host memory and reads the output
+    back. The CPU baseline is the oracle restatement (oracle/residual.py)."""
+    import torch
+
+    from voxgen_b200 import api, replicas, synth
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = replicas.init("nccl", world, timeout_s=600, device=dev)
+    wl = WORKLOADS[args.workload]
+    aspec = synth.acoustic_preset(wl["acoustic"])
+    if rank == 0:
+        synth.model_path(aspec.base, model_cache())
+        synth.acoustic_model_path(aspec, model_cache())
+    replicas.barrier(pg)
+    bpath = synth.model_path(aspec.base, model_cache())
+    apath = synth.acoustic_model_path(aspec, model_cache())
+    K, W = args.steps, args.warmup
+    ctx = api.Context(local)
+    base = api.Model(ctx, bpath)
+    res = api.ResidualModel(ctx, apath, base)
+    info = res.info
+    H = info["embedding_length"]
+    eng = api.ResidualEngine(res, max(wl["ctx"], W + K + 8))
+    hs = torch.from_numpy(synth.hidden_inputs(aspec.base, 8, seed_index=2000 + rank)).to(dev)
+    em = torch.from_numpy(synth.hidden_inputs(aspec.base, 8, seed_index=2100 + rank) * 0.5).to(dev)
+    torch.cuda.synchronize()
+    stream = torch.cuda.ExternalStream(eng.cuda_stream, device=dev)
+    for i in range(W):
+        eng.step(hs[i % 8].data_ptr(), em[i % 8].data_ptr(), fsq_applied=True)
+    eng.sync()
+    p0 = eng.position
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    replicas.barrier(pg)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local)
+    start.record(stream)
+    for i in range(K):
+        eng.step(hs[i % 8].data_ptr(), em[i % 8].data_ptr(), fsq_applied=True)
+    end.record(stream)
+    eng.sync(timeout_s=600)
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms_max = replicas.max_over_ranks(start.elapsed_time(end), pg, dev)
+    # e2e: host inputs in, the output hidden state out, every step
+    KE = args.e2e_steps or min(K, 300)
+    eng.reset()
+    hh = synth.hidden_inputs(aspec.base, 8, seed_index=2000 + rank)
+    he = synth.hidden_inputs(aspec.base, 8, seed_index=2100 + rank) * 0.5
+    out = np.empty(H, np.float32)
+    torch.cuda.synchronize()
+    e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e_start.record(stream)
+    for i in range(KE):
+        eng.step(hh[i % 8], he[i % 8], fsq_applied=True)
+        out[:] = eng.output()
+    e_end.record(stream)
+    torch.cuda.synchronize()
+    e_ms_max = replicas.max_over_ranks(e_start.elapsed_time(e_end), pg, dev)
+    # algorithmic bytes of a step: every matrix once (F16), norms, biases, KV rows read and written
+    L, F, KV, LAT = info["block_count"], info["feed_forward_length"], info["kv_dim"], aspec.latent
+    layer_w = L * 2 * (H * (H + 2 * KV) + H * H + 3 * H * F)
+    other_w = 2 * (2 * LAT * H + 2 * H * H) + 4 * (LAT + 2 * H) + 4 * (2 * L + 1) * H
+    kv_row = L * KV * 2 * 2
+    positions = range(p0, p0 + K)
+    avg_bytes = layer_w + other_w + sum(kv_row * (p + 2) for p in positions) / K
+    step_ms = ms_max / K
+    peak, peak_kind = measured_peaks()
+    ach = avg_bytes / (step_ms * 1e-3) / 1e9
+    line = {
+        "metric": "ResidualLM positions/s", "value": round(world * K / (ms_max / 1e3), 2), "unit": "positions/s",
+        "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": round(step_ms, 5), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"{args.workload}: {wl['desc']}", "weights": "F16",
+                   "positions": [p0, p0 + K - 1], "streams_per_gpu": 1,
+                   "parallelism": f"replicas x{world} (weights replicated, no collectives)",
+                   "l2": f"inputs larger than L2: {layer_w / 1e9:.2f} GB of layer weights per step",
+                   "input": "seeded BaseLM hidden states and acoustic embeddings, FSQ on"},
+        "roofline": {"kernel": "FSQ + fusion matvecs and the ResidualLM step kernel (whole position)",
+                     "bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
+                     "frac": round(ach / peak, 4), "traffic": None, "bytes_per_launch": int(avg_bytes),
+                     "peak_source": f"{peak_kind} hbm_gbs"},
+        "e2e": {"value": round(world * KE / (e_ms_max / 1e3), 2), "unit": "positions/s", "steps": KE,
+                "h2d_bytes_per_step": 2 * H * 4, "d2h_bytes_per_step": H * 4},
+        "gpu_launches": K * 5,
+        "clocks": clk,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import oracle as O
+        from oracle.residual import ResidualOracle
+        o = ResidualOracle(apath, bpath, KE + 8)
+        o.step(hh[0], he[0], True)
+        n, c0 = 0, time.perf_counter()
+        while n < 2 or (time.perf_counter() - c0 < args.cpu_seconds and n < KE):
+            o.step(hh[n % 8], he[n % 8], True)
+            n += 1
+        el = time.perf_counter() - c0
+        line["cpu_baseline"] = {"value": n / el, "unit": "positions/s", "cores": O.threads(), "kind": "port",
+                                "sample": f"{n} ResidualLM positions ({el:.1f} s, oracle restatement, OpenMP)"}
+    eng.close()
+    res.close()
+    base.close()
+    ctx.close()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    replicas.barrier(pg)
+    replicas.shutdown(pg)
+
+
 def main():
     args = parse()
     rank, world, local = dist_env()
+    if args.workload == "residual":
+        if args.impl == "reference":
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "unavailable":
+                                  "the ResidualLM workload has no reference CPU arm (the reference arm covers BaseLM)"}))
+            return
+        run_residual(args, rank, world, local)
+        return
     if args.impl == "reference":
         run_reference(args, rank, world)
         return
