@@ -417,18 +417,23 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_step_kernel(const __grid
       mbar_arrive_expect_tx(sbar + 1, C * 4u);
       bulk_g2s(stw, mp.normw, C * 4u, sbar + 1);
     }
-    wait_phase(ph);
-    if (src.x == nullptr) {
-      for (uint32_t k = tid; k < C; k += NCT) stg[k] = xsrc_elem<true>(src, k);  // token-table row
-      named_bar(1, NCT);
-    } else {
-      // one bulk copy of the input; the thread that acquired the other CTAs'
-      // writes at the grid barrier orders them before its async-proxy read
-      if (tid == 0) {
+    // One bulk copy of the input, issued by the thread that acquired the other
+    // CTAs' writes at the grid barrier as soon as it has them (it orders them
+    // before its async-proxy read). stg is free: the CTA barrier that ended the
+    // previous phase came after its last reader.
+    if (tid == 0) {
+      if (ph > 0 && !grid_wait(p.bar, base + (unsigned long long)ph * gridDim.x, err)) set_error(err, kErrGridWait);
+      if (src.x != nullptr) {
         fence_proxy_async_global();
         mbar_arrive_expect_tx(sbar, C * 4u);
         bulk_g2s(stg, src.x, C * 4u, sbar);
       }
+    }
+    named_bar(1, NCT);
+    if (src.x == nullptr) {
+      for (uint32_t k = tid; k < C; k += NCT) stg[k] = xsrc_elem<true>(src, k);  // token-table row
+      named_bar(1, NCT);
+    } else {
       if (!mbar_wait_bounded(sbar, spar & 1u, err)) {
         set_error(err, kErrConsumerWait);
         ok = false;
@@ -490,8 +495,17 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_step_kernel(const __grid
       const uint32_t SST = p.chunk + 4u;            // row stride of sS (padded)
       uint2 *sQB = reinterpret_cast<uint2 *>(aux);  // [HT][KS][2][32] q fragments
       float *sS = reinterpret_cast<float *>(aux + HT * KS * 2u * 32u * 8u);  // [G][SST]
+      static_assert(D / 2u <= NCT, "one word of the current K and V row per thread");
       for (uint32_t u = blockIdx.x; u < n_units; u += gridDim.x) {
         const AttnUnit a = attn_unit(p, u, nch, pos);
+        // the current position's K and V rows (stored by this step's QKV phase)
+        // are loaded here, so their L2 round trip overlaps the q loads below
+        const bool cur_row = a.staged < a.len && tid < D / 2u;
+        uint32_t kcur = 0, vcur = 0;
+        if (cur_row) {
+          kcur = __ldcg(reinterpret_cast<const unsigned int *>(Ly.kc + ((size_t)a.kvh * p.ctx + pos) * D) + tid);
+          vcur = __ldcg(reinterpret_cast<const unsigned int *>(Ly.vc + ((size_t)a.kvh * p.ctx + pos) * D) + tid);
+        }
         // q of the group as the B operand of the score MMAs (K = dims, N = 8
         // heads per tile), split into fp16 hi + lo: entry [ht][ks][h][lane] =
         // the lane's b0/b1 words (rows 2tq, 2tq+1 and 2tq+8, 2tq+9 of K-step
@@ -530,14 +544,9 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_step_kernel(const __grid
         __half *kS = reinterpret_cast<__half *>(R.ring + sK * R.slot);
         __half *vS = reinterpret_cast<__half *>(R.ring + sV * R.slot);
         const uint32_t len16 = (a.len + 15u) & ~15u;
-        if (a.staged < a.len) {
-          // the current position's row was stored by this step's QKV phase
-          const __half *kr = Ly.kc + ((size_t)a.kvh * p.ctx + pos) * D;
-          const __half *vr = Ly.vc + ((size_t)a.kvh * p.ctx + pos) * D;
-          for (uint32_t i = tid; i < D / 2u; i += NCT) {
-            reinterpret_cast<uint32_t *>(kS + a.staged * D)[i] = __ldcg(reinterpret_cast<const unsigned int *>(kr) + i);
-            reinterpret_cast<uint32_t *>(vS + a.staged * D)[i] = __ldcg(reinterpret_cast<const unsigned int *>(vr) + i);
-          }
+        if (cur_row) {
+          reinterpret_cast<uint32_t *>(kS + a.staged * D)[tid] = kcur;
+          reinterpret_cast<uint32_t *>(vS + a.staged * D)[tid] = vcur;
         }
         // V rows past the chunk's end meet zero weights; make them zero too (not
         // stale bytes, which may be NaN)
@@ -623,14 +632,15 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_step_kernel(const __grid
             if (gg < G) p.part[(((size_t)a.kvh * p.max_chunks + a.c) * G + gg) * D + dd] = c[j];
           }
         }
-        named_bar(1, NCT);  // every warp is done with the K and V stages
-        // release the K and V stages
+        // every warp is done with the K and V stages, and every partial of the
+        // unit is written (the barrier orders those writes before the ticket's
+        // release)
+        named_bar(1, NCT);
         if (lane == 0) {
           mbar_arrive(&R.empty[sK]);
           mbar_arrive(&R.empty[sV]);
         }
         // the last unit of this KV head to finish merges all of its chunks
-        named_bar(1, NCT);
         if (cw == 0 && lane == 0) sflags[0] = atomic_add_acq_rel(&p.tickets[a.kvh], 1u) == nch - 1u;
         named_bar(1, NCT);
         if (sflags[0]) {
