@@ -8,6 +8,8 @@ Workloads (seeded synthetic models):
   cfg1            24 layers at H=1024 (config[0]'s layer), F16 token table, 128-token prefill
   cfg0            config[0]: one layer at H=1024, 512 prior positions
   residual        ResidualLM + FSQ + fusion at VoxCPM2's shape (8 layers, H=2048, F16), positions/s
+  cfg4            16 streams per GPU at cfg2's shape with ragged KV lengths ~U[64, 4096]; a step
+                  advances every stream by one token (vg_decode_batch)
 
 A step is one decode token of one stream. `value` is the whole-job aggregate tok/s over all
 GPUs (independent replicas, weights replicated, no collectives on the data path), device-timed
@@ -44,6 +46,9 @@ WORKLOADS = {
     # ResidualLM + FSQ + fusion after BaseLM (src/acoustic.rs:851-1035), VoxCPM2's shape
     "residual": dict(acoustic="res_cfg2", prefill=0, ctx=4096,
                      desc="ResidualLM 8L H2048 16x128 GQA 2 KV F6144 F16 + FSQ 512 + fusion"),
+    # BASELINE cfg4: many streams per GPU, each with its own KV cache (runtime.rs's engines)
+    "cfg4": dict(preset="cfg2", streams=16, ctx=4096, slack=256, prefill=2080,
+                 desc="16 streams per GPU, BaseLM 28L H2048 Q8_0, ragged KV ~U[64,4096]"),
 }
 
 
@@ -287,13 +292,15 @@ def run_residual(args, rank, world, local):
                    "parallelism": f"replicas x{world} (weights replicated, no collectives)",
                    "l2": f"inputs larger than L2: {layer_w / 1e9:.2f} GB of layer weights per step",
                    "input": "seeded BaseLM hidden states and acoustic embeddings, FSQ on"},
-        "roofline": {"kernel": "FSQ + fusion matvecs and the ResidualLM step kernel (whole position)",
+        "roofline": {"kernel": "decode_step_kernel with the FSQ and fusion phases (one launch per position)"
+                               if eng.kernel_mode == 1 else
+                               "FSQ + fusion matvecs and the ResidualLM layers (whole position)",
                      "bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(ach / peak, 4), "traffic": None, "bytes_per_launch": int(avg_bytes),
                      "peak_source": f"{peak_kind} hbm_gbs"},
         "e2e": {"value": round(world * KE / (e_ms_max / 1e3), 2), "unit": "positions/s", "steps": KE,
                 "h2d_bytes_per_step": 2 * H * 4, "d2h_bytes_per_step": H * 4},
-        "gpu_launches": K * 5,
+        "gpu_launches": K * (1 if eng.kernel_mode == 1 else 4 + 5 * L + 1),
         "clocks": clk,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -318,9 +325,133 @@ def run_residual(args, rank, world, local):
     replicas.shutdown(pg)
 
 
+def run_batch(args, rank, world, local):
+    """cfg4: S streams per GPU over one model, each with its own KV cache prefilled to a seeded
+    ragged length ~U[64, 4096]. A step advances every stream by one token through
+    vg_decode_batch (each stream's step on its own CUDA stream; the weights are read once per
+    stream). value = tokens of all streams on all ranks / device time (events on every engine
+    stream, max over streams and ranks). e2e copies the S token ids from host memory and reads
+    the S output hidden states back every step."""
+    import torch
+
+    from voxgen_b200 import api, replicas, synth
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = replicas.init("nccl", world, timeout_s=600, device=dev)
+
+    def barrier():
+        replicas.barrier(pg)
+
+    wl = WORKLOADS[args.workload]
+    spec = synth.preset(wl["preset"])
+    path = ensure_model(spec, rank, world, barrier)
+    K, W, S = args.steps, args.warmup, wl["streams"]
+    KE = args.e2e_steps or min(K, 20)
+    lens = np.random.default_rng([4, rank]).integers(64, wl["ctx"] + 1, size=S)
+    max_ctx = int(max(wl["ctx"] + wl["slack"], lens.max() + W + K + KE + 1))
+    ctx = api.Context(local)
+    model = api.Model(ctx, path)
+    info = model.info
+    engs = [api.BaseLmEngine(model, max_ctx) for _ in range(S)]
+    kpre, vpre = synth.kv_prefill(spec, int(lens.max()))
+
+    def prefill():
+        for e, n in zip(engs, lens):
+            e.write_kv(kpre[:, :n], vpre[:, :n])
+
+    toks = synth.token_ids(spec, (W + K + KE) * S, seed_index=4000 + rank).reshape(W + K + KE, S)
+    streams = [torch.cuda.ExternalStream(e.cuda_stream, device=dev) for e in engs]
+
+    def timed(rows, read_back):
+        start = torch.cuda.Event(enable_timing=True)
+        ends = [torch.cuda.Event(enable_timing=True) for _ in engs]
+        barrier()
+        torch.cuda.synchronize()
+        start.record(torch.cuda.current_stream())
+        for st in streams:
+            st.wait_event(start)
+        for row in rows:
+            api.decode_batch(engs, [int(t) for t in row])   # S token ids from host memory
+            if read_back:
+                for e in engs:
+                    e.output()                                # D2H of each stream's hidden state
+        for st, ev in zip(streams, ends):
+            ev.record(st)
+        for e in engs:
+            e.sync(timeout_s=600)
+        torch.cuda.synchronize()
+        barrier()
+        return max(start.elapsed_time(ev) for ev in ends)
+
+    prefill()
+    for row in toks[:W]:
+        api.decode_batch(engs, [int(t) for t in row])
+    for e in engs:
+        e.sync()
+    p0 = [e.position for e in engs]
+    clocks = ClockSampler(local)
+    ms = timed(toks[W:W + K], False)
+    clk = clocks.stop()
+    ms_max = replicas.max_over_ranks(ms, pg, dev)
+    prefill()
+    e_ms_max = replicas.max_over_ranks(timed(toks[W + K:W + K + KE], True), pg, dev)
+
+    peak, peak_kind = measured_peaks()
+    kv = info["block_count"] * info["kv_dim"] * 2 * 2
+    wbytes = info["layer_weight_bytes"] + info["norm_weight_bytes"]
+    kv_step = sum(kv * (p + j + 1) + kv for p in p0 for j in range(K)) / K   # all streams, per step
+    step_ms = ms_max / K
+    # per launch of the step kernel (one stream's token): its weights and that stream's KV
+    launch_bytes = wbytes + kv_step / S
+    launch_ach = launch_bytes * S / (step_ms * 1e-3) / 1e9
+    # per batched step, counting the weights once (the roofline of a shared weight pass)
+    batch_bytes = wbytes + kv_step
+    batch_ach = batch_bytes / (step_ms * 1e-3) / 1e9
+    line = {
+        "metric": "decode tok/s", "value": round(replicas.aggregate_rate(K * S, world, ms_max), 2),
+        "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": round(step_ms, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {
+            "workload": f"{args.workload}: {wl['desc']}", "weights": "Q8_0", "streams_per_gpu": S,
+            "kv_lengths": [int(x) for x in lens], "step": f"one token for each of the {S} streams",
+            "parallelism": f"replicas x{world} (weights replicated, streams partitioned, no collectives)",
+            "l2": f"inputs larger than L2: {info['layer_weight_bytes'] / 1e9:.2f} GB of weights per stream token",
+            "input": "seeded token ids",
+        },
+        "roofline": {"kernel": "decode_step_kernel (one launch per stream token; the weight pass is not "
+                               "shared between streams)", "bound": "hbm", "achieved": round(launch_ach, 1),
+                     "peak": peak, "unit": "GB/s", "frac": round(launch_ach / peak, 4), "traffic": None,
+                     "bytes_per_launch": int(launch_bytes),
+                     "avg_launch_ms": round(step_ms / S, 5), "peak_source": f"{peak_kind} hbm_gbs"},
+        "batch_roofline": {"bytes_per_step": int(batch_bytes), "achieved": round(batch_ach, 1), "peak": peak,
+                           "unit": "GB/s", "frac": round(batch_ach / peak, 4),
+                           "note": "weights counted once per batched step"},
+        "e2e": {"value": round(replicas.aggregate_rate(KE * S, world, e_ms_max), 2), "unit": "tok/s",
+                "steps": KE, "h2d_bytes_per_step": 4 * S,
+                "d2h_bytes_per_step": S * info["embedding_length"] * 4},
+        "gpu_launches": K * S,
+        "clocks": clk,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        mean_len = int(np.mean(lens))
+        line["cpu_baseline"] = cpu_baseline_sample(args, spec, path, {"ctx": mean_len + 80, "prefill": mean_len})
+        line["cpu_baseline"]["sample"] += f"; the {S} streams would run one after another"
+    for e in engs:
+        e.close()
+    model.close()
+    ctx.close()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    replicas.barrier(pg)
+    replicas.shutdown(pg)
+
+
 def main():
     args = parse()
     rank, world, local = dist_env()
+    if args.workload == "cfg4" and args.impl == "ours":
+        run_batch(args, rank, world, local)
+        return
     if args.workload == "residual":
         if args.impl == "reference":
             if rank == 0:

@@ -288,11 +288,11 @@ struct vg_stream {
   uint32_t step_smem = 0, step_grid = 0;
   bool step_head_apart = false;  // the LM head is stored in another format: own launch after the step
   MvPlan step_head{};
-  // ResidualLM streams: the BaseLM hidden state in, the FSQ latent, the FSQ
-  // output, the fusion input [left | right], its output (snapshot), the LM
-  // state (post-FSQ or raw BaseLM hidden), and the three matvec plans
-  float *res_base = nullptr, *res_embed = nullptr, *fsq_lat = nullptr, *fsq_res = nullptr, *fuse_in = nullptr,
-        *fused = nullptr, *cur_lm = nullptr;
+  // ResidualLM streams: the BaseLM hidden state in (FSQ positions), the FSQ
+  // latent, the FSQ output, the fusion input [LM state | acoustic embedding]
+  // (the LM state is the FSQ output or the raw BaseLM hidden), the fusion
+  // output (snapshot), and the three matvec plans of the per-kernel path
+  float *res_base = nullptr, *fsq_lat = nullptr, *fsq_res = nullptr, *fuse_in = nullptr, *fused = nullptr;
   MvPlan fsq_in_p{}, fsq_out_p{}, fuse_p{};
 };
 
@@ -769,8 +769,24 @@ std::string plan_step(vg_stream *s) {
   p.g_head = m->out.g;
   p.n_layers = c.block_count;
   p.H = c.embedding_length;
+  if (m->residual) {
+    // FSQ and fusion run as the step's first three phases
+    for (const DevMat *d : {&m->fsq_in, &m->fsq_out, &m->fuse})
+      if (d->type != type) return "the FSQ and fusion projections do not share the layers' weight format";
+    p.pre = 3;
+    p.g_fin = m->fsq_in.g;
+    p.g_fout = m->fsq_out.g;
+    p.g_fuse = m->fuse.g;
+    p.w_fin = m->fsq_in.w;
+    p.w_fout = m->fsq_out.w;
+    p.w_fuse = m->fuse.w;
+    p.b_fin = m->fsq_in_b;
+    p.b_fout = m->fsq_out_b;
+    p.b_fuse = m->fuse_b;
+    p.fsq_scale = m->acoustic.fsq_scale;
+  }
   p.xcols = 0;
-  for (const TileGeom *g : {&p.g_qkv, &p.g_o, &p.g_gu, &p.g_down, &p.g_head}) {
+  for (const TileGeom *g : {&p.g_qkv, &p.g_o, &p.g_gu, &p.g_down, &p.g_head, &p.g_fin, &p.g_fout, &p.g_fuse}) {
     if (g->cols % 4u) return strf("a matvec input of %u columns is not a whole number of 16-byte copies", g->cols);
     p.xcols = std::max(p.xcols, g->cols);
   }
@@ -778,8 +794,9 @@ std::string plan_step(vg_stream *s) {
   uint32_t segb = 0, plane = 0, cpad = 0, rb = 1;
   s->step_head_apart = m->out.g.rows > 0 && m->out.type != type;
   if (s->step_head_apart) s->step_head = plan_matvec<Mode::PLAIN, Pro::COPY>(m->out, dev, (uint32_t)m->ctx->sms);
-  for (const TileGeom *g : {&p.g_qkv, &p.g_o, &p.g_gu, &p.g_down, &p.g_head}) {
+  for (const TileGeom *g : {&p.g_qkv, &p.g_o, &p.g_gu, &p.g_down, &p.g_head, &p.g_fin, &p.g_fout, &p.g_fuse}) {
     if (g == &p.g_head && s->step_head_apart) continue;
+    if (g->rows == 0) continue;  // no LM head, or not a ResidualLM
     segb = std::max(segb, g->seg_bytes());
     const uint32_t cp = g->nseg() * g->seg_cols();
     cpad = std::max(cpad, cp);
@@ -790,6 +807,7 @@ std::string plan_step(vg_stream *s) {
   // positions per attention unit: a whole number of 16-row MMA tiles of K (or V) rows in a stage slot
   p.chunk = std::min<uint32_t>(64u, p.slot / (2u * D)) & ~15u;
   if (p.chunk == 0) return strf("a stage slot of %u bytes holds no 16 rows of head_dim %u", p.slot, D);
+  if (c.head_count_kv > 64) return strf("%u KV heads (the step kernel keeps at most 64 merge counters)", c.head_count_kv);
   p.max_chunks = (s->max_ctx + p.chunk - 1) / p.chunk;
   p.plane = plane;
   p.a_bytes = std::max(round_up(3u * plane + cpad / 32u * 4u + 16u, 128u), step_attn_bytes(G, D, p.chunk, p.max_chunks));
@@ -809,9 +827,14 @@ std::string plan_step(vg_stream *s) {
   return "";
 }
 
+// token_input selects the token-table input of a BaseLM step; a ResidualLM
+// stream has no token table, and the same flag selects its FSQ phases.
 cudaError_t launch_step_kernel(vg_stream *s, bool token_input, bool logits) {
   StepParams p = s->sp;
-  p.token_input = token_input;
+  if (s->m->residual)
+    p.fsq_on = token_input;
+  else
+    p.token_input = token_input;
   p.want_logits = logits && !s->step_head_apart;
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(s->step_grid);
@@ -829,7 +852,7 @@ cudaError_t launch_step_kernel(vg_stream *s, bool token_input, bool logits) {
 }
 
 cudaGraphExec_t get_graph(vg_stream *s, bool token_input, bool logits) {
-  cudaGraphExec_t &g = s->graphs[token_input][logits];
+  cudaGraphExec_t &g = s->graphs[token_input][logits];  // ResidualLM: [fsq_on][0]
   if (g) return g;
   std::vector<Launch> prog;
   if (s->use_step) {
@@ -884,6 +907,17 @@ void launch_step(vg_stream *s, bool token_input, bool logits) {
     CK(launch_step_kernel(s, token_input, logits));
   s->pos += 1;
   s->logits_valid = logits;
+}
+
+// One ResidualLM position on the step kernel (FSQ phases on or off).
+void launch_residual_step(vg_stream *s, bool fsq) {
+  cudaGraphExec_t g = s->step_graph ? get_graph(s, fsq, false) : nullptr;
+  if (g)
+    CK(cudaGraphLaunch(g, s->st));
+  else
+    CK(launch_step_kernel(s, fsq, false));
+  s->pos += 1;
+  s->logits_valid = false;
 }
 
 int sync_stream(vg_stream *s, uint64_t timeout_ns, bool check_flag) {
@@ -1107,11 +1141,10 @@ int vg_stream_create(vg_model *m, uint32_t max_context, vg_stream **out) {
                  o_bar = take(8), o_sl = take((size_t)c.block_count * sizeof(StepLayer)),
                  o_sp = take((size_t)c.head_count_kv * nch * G * D * 4),
                  o_sml = take((size_t)c.head_count_kv * nch * G * 8),
-                 o_stk = take((size_t)c.head_count_kv * 4);
+                 o_stk = take((size_t)c.head_count_kv * 4), o_rdy = take((size_t)c.head_count_kv * 8);
     const uint32_t LAT = m->residual ? m->acoustic.fsq_latent_dim : 0u, HR = m->residual ? H : 0u;
-    const size_t o_rb = take((size_t)HR * 4), o_re = take((size_t)HR * 4), o_rl = take((size_t)LAT * 4),
-                 o_rf = take((size_t)HR * 4), o_ri = take((size_t)HR * 8), o_rs = take((size_t)HR * 4),
-                 o_rc = take((size_t)HR * 4);
+    const size_t o_rb = take((size_t)HR * 4), o_rl = take((size_t)LAT * 4), o_rf = take((size_t)HR * 4),
+                 o_ri = take((size_t)HR * 8), o_rs = take((size_t)HR * 4);
     CK(cudaMalloc(&s->dev_block, off));
     CK(cudaMemset(s->dev_block, 0, off));
     uint8_t *b = static_cast<uint8_t *>(s->dev_block);
@@ -1127,12 +1160,10 @@ int vg_stream_create(vg_model *m, uint32_t max_context, vg_stream **out) {
     s->tickets = (uint32_t *)(b + o_tk);
     if (m->residual) {
       s->res_base = (float *)(b + o_rb);
-      s->res_embed = (float *)(b + o_re);
       s->fsq_lat = (float *)(b + o_rl);
       s->fsq_res = (float *)(b + o_rf);
       s->fuse_in = (float *)(b + o_ri);
       s->fused = (float *)(b + o_rs);
-      s->cur_lm = (float *)(b + o_rc);
       const int dev = m->ctx->device;
       const uint32_t sms = (uint32_t)m->ctx->sms;
       // linear_bias.comp / fusion_linear.comp: (W x + bias), the bias as the residual
@@ -1180,6 +1211,14 @@ int vg_stream_create(vg_model *m, uint32_t max_context, vg_stream **out) {
       p.part = (float *)(b + o_sp);
       p.part_ml = (float2 *)(b + o_sml);
       p.tickets = (uint32_t *)(b + o_stk);
+      p.ready = (unsigned long long *)(b + o_rdy);
+      if (m->residual) {
+        p.res_base = s->res_base;
+        p.fsq_lat = s->fsq_lat;
+        p.fsq_res = s->fsq_res;
+        p.fuse_in = s->fuse_in;
+        p.fused = s->fused;
+      }
       p.inv_freq = m->inv_freq;
       p.ext = m->ext;
       p.rope_scaling = c.rope_scaling_factor();
@@ -1379,26 +1418,32 @@ namespace {
 // else the raw BaseLM hidden does (a text-prefix position); the fusion
 // projection of [LM state | current acoustic embedding] (record_fusion
 // :946-966) is the input of the ResidualLM layers (record_residual_lm
-// :968-1035). res_base and res_embed hold the step's inputs.
-void residual_enqueue(vg_stream *s, bool embed_given, bool fsq_applied) {
+// :968-1035). The inputs are copied in place first: the BaseLM hidden into
+// res_base (FSQ positions) or straight into the LM state, the embedding (or
+// zeros) after it. With the step kernel the whole position is one launch (FSQ
+// and fusion are its first phases); otherwise standalone kernels run them.
+void residual_enqueue(vg_stream *s, const float *base, const float *embed, bool fsq, cudaMemcpyKind kind) {
   vg_model *m = s->m;
   const uint32_t H = m->cfg.embedding_length, LAT = m->acoustic.fsq_latent_dim;
-  const float *left = s->res_base;
-  if (fsq_applied) {
+  const size_t bytes = (size_t)H * 4;
+  CK(cudaMemcpyAsync(fsq ? s->res_base : s->fuse_in, base, bytes, kind, s->st));
+  if (embed)
+    CK(cudaMemcpyAsync(s->fuse_in + H, embed, bytes, kind, s->st));
+  else
+    CK(cudaMemsetAsync(s->fuse_in + H, 0, bytes, s->st));  // zero_embed
+  if (s->use_step) {
+    launch_residual_step(s, fsq);
+    return;
+  }
+  if (fsq) {
     CK(run_matvec(s->fsq_in_p, s->st, false));
     fsq_quantize_kernel<<<(LAT + 255) / 256, 256, 0, s->st>>>(s->fsq_lat, LAT, m->acoustic.fsq_scale);
     CK(cudaGetLastError());
     CK(run_matvec(s->fsq_out_p, s->st, false));
-    left = s->fsq_res;
+    CK(cudaMemcpyAsync(s->fuse_in, s->fsq_res, bytes, cudaMemcpyDeviceToDevice, s->st));
   }
-  CK(cudaMemcpyAsync(s->cur_lm, left, (size_t)H * 4, cudaMemcpyDeviceToDevice, s->st));
-  CK(cudaMemcpyAsync(s->fuse_in, left, (size_t)H * 4, cudaMemcpyDeviceToDevice, s->st));
-  if (embed_given)
-    CK(cudaMemcpyAsync(s->fuse_in + H, s->res_embed, (size_t)H * 4, cudaMemcpyDeviceToDevice, s->st));
-  else
-    CK(cudaMemsetAsync(s->fuse_in + H, 0, (size_t)H * 4, s->st));  // zero_embed
   CK(run_matvec(s->fuse_p, s->st, false));
-  CK(cudaMemcpyAsync(s->hid_a, s->fused, (size_t)H * 4, cudaMemcpyDeviceToDevice, s->st));
+  CK(cudaMemcpyAsync(s->hid_a, s->fused, bytes, cudaMemcpyDeviceToDevice, s->st));
   launch_step(s, false, false);
 }
 }  // namespace
@@ -1410,10 +1455,7 @@ int vg_residual_step(vg_stream *s, const float *dev_base_hidden, const float *de
   return guard(s->m->ctx, [&] {
     check_step(s);
     CK(cudaSetDevice(s->m->ctx->device));
-    const size_t bytes = (size_t)s->m->cfg.embedding_length * 4;
-    CK(cudaMemcpyAsync(s->res_base, dev_base_hidden, bytes, cudaMemcpyDeviceToDevice, s->st));
-    if (dev_embed) CK(cudaMemcpyAsync(s->res_embed, dev_embed, bytes, cudaMemcpyDeviceToDevice, s->st));
-    residual_enqueue(s, dev_embed != nullptr, fsq_applied != 0);
+    residual_enqueue(s, dev_base_hidden, dev_embed, fsq_applied != 0, cudaMemcpyDeviceToDevice);
     return VG_OK;
   });
 }
@@ -1425,10 +1467,7 @@ int vg_residual_step_host(vg_stream *s, const float *base_hidden, const float *e
   return guard(s->m->ctx, [&] {
     check_step(s);
     CK(cudaSetDevice(s->m->ctx->device));
-    const size_t bytes = (size_t)s->m->cfg.embedding_length * 4;
-    CK(cudaMemcpyAsync(s->res_base, base_hidden, bytes, cudaMemcpyHostToDevice, s->st));
-    if (embed) CK(cudaMemcpyAsync(s->res_embed, embed, bytes, cudaMemcpyHostToDevice, s->st));
-    residual_enqueue(s, embed != nullptr, fsq_applied != 0);
+    residual_enqueue(s, base_hidden, embed, fsq_applied != 0, cudaMemcpyHostToDevice);
     CK(cudaStreamSynchronize(s->st));  // the host buffers may be reused on return
     return VG_OK;
   });
@@ -1440,7 +1479,7 @@ int vg_residual_state(const vg_stream *s, int which, const float **dev) {
   switch (which) {
     case VG_RESIDUAL_FSQ_OUTPUT: *dev = s->fsq_res; return VG_OK;
     case VG_RESIDUAL_FUSED_INPUT: *dev = s->fused; return VG_OK;
-    case VG_RESIDUAL_LM_STATE: *dev = s->cur_lm; return VG_OK;
+    case VG_RESIDUAL_LM_STATE: *dev = s->fuse_in; return VG_OK;
   }
   return VG_EINVAL;
 }

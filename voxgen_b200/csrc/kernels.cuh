@@ -31,7 +31,9 @@
 
 namespace vg {
 
-enum class Mode { PLAIN, RESID, SWIGLU, QKV };
+// FSQ (step kernel only): bias + round(tanh(y) * scale) / scale, the ResidualLM
+// quantiser (fsq_quantize.comp) on linear_bias.comp's output.
+enum class Mode { PLAIN, RESID, SWIGLU, QKV, FSQ };
 enum class Pro { COPY, RMSNORM };
 
 constexpr int kMvConsumers = 8;                       // consumer warps per matvec CTA
@@ -105,6 +107,7 @@ struct MvParams {
   const float *ext;       // [head_dim/2], LongRoPE factors
   float rope_scaling;
   uint32_t *ctrl;
+  float *out2;            // step kernel RESID: a second copy of the output (nullptr: none)
 };
 
 // Shared-memory plan of one matvec CTA (host and device agree on it).
@@ -607,21 +610,8 @@ __device__ __forceinline__ void mv_activation(uint32_t C, uint32_t cols_pad, con
 // Consumes the n_items segments of this CTA's tile run from ring stages j, j+1,
 // ... (tile t0 first), writes per-(tile, warp) partials into red (zeroed by the
 // caller for the run's tiles), and after a consumer barrier runs the tile
-// reductions and the epilogue. Returns the next stage index; ok turns false
-// when a wait gave up (the partials are then incomplete and the error flag is
-// set).
-// The epilogue with the mode chosen at run time, as one out-of-line copy: the
-// persistent step kernel runs every mode from a single call site.
-__device__ __noinline__ void mv_epilogue_rt(Mode mode, const MvParams &p, uint32_t R, float a, float b,
-                                            uint32_t pos) {
-  switch (mode) {
-    case Mode::PLAIN: mv_epilogue<Mode::PLAIN>(p, R, a, b, pos); break;
-    case Mode::RESID: mv_epilogue<Mode::RESID>(p, R, a, b, pos); break;
-    case Mode::SWIGLU: mv_epilogue<Mode::SWIGLU>(p, R, a, b, pos); break;
-    case Mode::QKV: mv_epilogue<Mode::QKV>(p, R, a, b, pos); break;
-  }
-}
-
+// reductions and the epilogue. ok turns false when a wait gave up (the
+// partials are then incomplete and the error flag is set).
 // Consumer side of a matvec over n_items ring segments (tiles t0.. of this
 // CTA's run). epilogue(R, a, b, pv) receives the finished rows R and R + 8
 // and pv = pre(R); for the first tile of each warp pre runs before the K

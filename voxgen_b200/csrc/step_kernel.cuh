@@ -41,6 +41,7 @@ struct StepParams {
   float *part;              // attention partial outputs [kv_heads][max_chunks][G][head_dim]
   float2 *part_ml;          // their running max and sum [kv_heads][max_chunks][G]
   uint32_t *tickets;        // [kv_heads], zero between steps
+  unsigned long long *ready;  // [kv_heads] merge releases: +1 per layer when a head's chunks are all written
   const float *inv_freq, *ext;
   float rope_scaling, eps, res_scale, emb_scale, logit_scale, attn_scale;
   uint32_t H, F, heads, kv_heads, head_dim, ctx;
@@ -48,6 +49,18 @@ struct StepParams {
   uint32_t token_input, want_logits;
   uint32_t *ctrl;
   unsigned long long *bar;  // grid barrier arrivals
+  // ResidualLM (pre = 3; else 0): three phases before the layers, FSQ in_proj
+  // + bias + quantiser into fsq_lat, FSQ out_proj + bias into fuse_in[0, H)
+  // (the LM state) and fsq_res, fusion [fuse_in] + bias into hid_a and fused.
+  // With fsq_on = 0 (a text-prefix position, fuse_in[0, H) given) the two FSQ
+  // phases only keep their grid barriers.
+  uint32_t pre, fsq_on;
+  TileGeom g_fin, g_fout, g_fuse;
+  const uint8_t *w_fin, *w_fout, *w_fuse;
+  const float *b_fin, *b_fout, *b_fuse;
+  float fsq_scale;
+  const float *res_base;    // FSQ input: the BaseLM hidden state
+  float *fsq_lat, *fsq_res, *fuse_in, *fused;
   // shared-memory plan (host and device agree through StepSmem)
   uint32_t nst, slot;       // ring stages and bytes per stage slot
   uint32_t a_bytes, plane;  // activation / attention scratch region and digit-plane stride
@@ -242,12 +255,19 @@ __device__ __forceinline__ void step_activation(uint32_t C, uint32_t cols_pad, b
   }
 }
 
-// Attention scratch inside the aux region: the q fragments of one KV group,
-// then the scores of a chunk (rows padded by 4 floats).
+// Attention scratch inside the aux region: for a unit, the q fragments of one
+// KV group, then the scores of a chunk (rows padded by 4 floats); for a merge
+// slice, the chunk weights and 1/sum (max_chunks + 4 floats), then the chunk
+// groups' partial rows (4 * consumer threads floats).
+__host__ __device__ inline uint32_t step_merge_w_bytes(uint32_t max_chunks) {
+  return ((max_chunks + 4u) * 4u + 15u) & ~15u;
+}
 __host__ __device__ inline uint32_t step_attn_bytes(uint32_t G, uint32_t head_dim, uint32_t chunk,
                                                     uint32_t max_chunks) {
   const uint32_t q_frag = (G + 7u) / 8u * (head_dim / 16u) * 2u * 32u * 8u;
-  return q_frag + G * ((chunk > max_chunks ? chunk : max_chunks) + 4u) * 4u;
+  const uint32_t unit = q_frag + G * ((chunk > max_chunks ? chunk : max_chunks) + 4u) * 4u;
+  const uint32_t merge = step_merge_w_bytes(max_chunks) + 4u * kMvConsumers * 32u * 4u;
+  return unit > merge ? unit : merge;
 }
 
 enum : uint32_t { kPhQkv = 0, kPhAttn = 1, kPhO = 2, kPhGu = 3, kPhDown = 4, kPhasesPerLayer = 5 };
@@ -296,11 +316,12 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_step_kernel(const __grid
   float *stw = reinterpret_cast<float *>(smem + L.stw);
   float *scr = reinterpret_cast<float *>(smem + L.scr);                                 // 64 floats
   unsigned long long *sbase = reinterpret_cast<unsigned long long *>(smem + L.scr + 256u);
-  uint32_t *sflags = reinterpret_cast<uint32_t *>(smem + L.scr + 264u);                // 8 words
+  // merge-release counts of the KV heads at the step's start (kv_heads <= 64)
+  unsigned long long *srdy = reinterpret_cast<unsigned long long *>(smem + L.scr + 512u);
 
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
   uint32_t *err = p.ctrl + kCtrlErr;
-  const uint32_t nb = p.n_layers * kPhasesPerLayer;  // barriers per step = arrivals per CTA
+  const uint32_t nb = p.pre + p.n_layers * kPhasesPerLayer;  // barriers per step = arrivals per CTA
   const uint32_t G = p.heads / p.kv_heads;
 
   if (threadIdx.x == 0) {
@@ -320,6 +341,9 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_step_kernel(const __grid
   }
   for (uint32_t i = threadIdx.x; i < p.n_layers * (uint32_t)sizeof(StepLayer) / 8u; i += blockDim.x)
     reinterpret_cast<unsigned long long *>(layers)[i] = reinterpret_cast<const unsigned long long *>(p.layers)[i];
+  // Read before this CTA's first grid-barrier arrival: the first release of
+  // this step comes after the first barrier, which waits for every CTA.
+  for (uint32_t i = threadIdx.x; i < p.kv_heads; i += blockDim.x) srdy[i] = ld_acquire_u64(p.ready + i);
   __syncthreads();
   const unsigned long long base = *sbase;
 
@@ -352,7 +376,12 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_step_kernel(const __grid
       };
       // the phases in order, each through one call site
       for (uint32_t ph = 0; ph <= nb && live; ++ph) {
-        const uint32_t l = ph / kPhasesPerLayer, kind = ph - l * kPhasesPerLayer;
+        if (ph < p.pre) {
+          if (ph == 2u) stream(p.w_fuse, p.g_fuse);
+          else if (p.fsq_on) stream(ph == 0u ? p.w_fin : p.w_fout, ph == 0u ? p.g_fin : p.g_fout);
+          continue;
+        }
+        const uint32_t l = (ph - p.pre) / kPhasesPerLayer, kind = ph - p.pre - l * kPhasesPerLayer;
         const StepLayer &Ly = layers[l < p.n_layers ? l : 0u];
         if (ph < nb && kind == kPhAttn) {
           for (uint32_t u = blockIdx.x; u < n_units; u += gridDim.x) {
@@ -453,7 +482,7 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_step_kernel(const __grid
                       (rms && xout == nullptr) ? scr + 8 : nullptr,
                       [&](uint32_t R0) {  // the residual, in flight during the K loop
                         float2 v = make_float2(0.f, 0.f);
-                        if (mode == Mode::RESID) {
+                        if (mode == Mode::RESID || mode == Mode::FSQ) {
                           if (R0 < mp.g.rows) v.x = __ldcg(mp.resid + R0);
                           if (R0 + 8u < mp.g.rows) v.y = __ldcg(mp.resid + R0 + 8u);
                         }
@@ -462,10 +491,25 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_step_kernel(const __grid
                       [&](uint32_t R0, float a, float b, float2 pv) {
                         switch (mode) {
                           case Mode::PLAIN: mv_epilogue<Mode::PLAIN>(mp, R0, a, b, pos); break;
-                          case Mode::RESID:  // residual_rmsnorm.comp:27
-                            if (R0 < mp.g.rows) mp.out[R0] = __fadd_rn(pv.x, __fmul_rn(a, mp.alpha));
-                            if (R0 + 8u < mp.g.rows) mp.out[R0 + 8u] = __fadd_rn(pv.y, __fmul_rn(b, mp.alpha));
+                          case Mode::RESID: {  // residual_rmsnorm.comp:27 (linear_bias.comp:75 with alpha 1)
+                            const float y0 = __fadd_rn(pv.x, __fmul_rn(a, mp.alpha));
+                            const float y1 = __fadd_rn(pv.y, __fmul_rn(b, mp.alpha));
+                            if (R0 < mp.g.rows) mp.out[R0] = y0;
+                            if (R0 + 8u < mp.g.rows) mp.out[R0 + 8u] = y1;
+                            if (mp.out2) {
+                              if (R0 < mp.g.rows) mp.out2[R0] = y0;
+                              if (R0 + 8u < mp.g.rows) mp.out2[R0 + 8u] = y1;
+                            }
                             break;
+                          }
+                          case Mode::FSQ: {  // linear_bias.comp:75, then fsq_quantize.comp:8-11
+                            const float s = p.fsq_scale;
+                            if (R0 < mp.g.rows)
+                              mp.out[R0] = __fdiv_rn(roundf(__fmul_rn(tanhf(__fadd_rn(pv.x, a)), s)), s);
+                            if (R0 + 8u < mp.g.rows)
+                              mp.out[R0 + 8u] = __fdiv_rn(roundf(__fmul_rn(tanhf(__fadd_rn(pv.y, b)), s)), s);
+                            break;
+                          }
                           case Mode::SWIGLU: mv_epilogue<Mode::SWIGLU>(mp, R0, a, b, pos); break;
                           case Mode::QKV: mv_epilogue<Mode::QKV>(mp, R0, a, b, pos); break;
                         }
@@ -483,12 +527,13 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_step_kernel(const __grid
 
   // Phases nb * layer + kind, then phase nb: the final RMSNorm and the optional LM head.
   for (uint32_t ph = 0; ph <= nb; ++ph) {
-    const uint32_t l = ph / kPhasesPerLayer;
-    const uint32_t kind = ph - l * kPhasesPerLayer;
+    const uint32_t lp = ph < p.pre ? 0u : ph - p.pre;  // phase within the layers
+    const uint32_t l = lp / kPhasesPerLayer;
+    const uint32_t kind = lp - l * kPhasesPerLayer;
     const StepLayer &Ly = layers[l < p.n_layers ? l : 0u];
 
-    // ---- attention: split-K units, the last unit of a KV head merges ----
-    if (ph < nb && kind == kPhAttn) {
+    // ---- attention: split-K units, then one merge slice per query head ----
+    if (ph >= p.pre && ph < nb && kind == kPhAttn) {
       wait_phase(ph);
       constexpr uint32_t KS = D / 16u;              // K-steps of a head row
       const uint32_t HT = (G + 7u) / 8u;            // tiles of 8 heads
@@ -640,78 +685,98 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_step_kernel(const __grid
           mbar_arrive(&R.empty[sK]);
           mbar_arrive(&R.empty[sV]);
         }
-        // the last unit of this KV head to finish merges all of its chunks
-        if (cw == 0 && lane == 0) sflags[0] = atomic_add_acq_rel(&p.tickets[a.kvh], 1u) == nch - 1u;
-        named_bar(1, NCT);
-        if (sflags[0]) {
-          // warp per query head: lanes hold the chunks' (max, sum) pairs, the
-          // weights go through shuffles, MB chunks' partial rows are loaded at
-          // once; the first MB rows and the first 64 pairs are loaded together
-          // (the rows do not depend on the max), then the chunks are summed in order
-          for (uint32_t g0 = cw; g0 < G; g0 += kMvConsumers) {
-            const size_t hb = (size_t)a.kvh * p.max_chunks * G + g0;  // slot of chunk 0
-            const float *ob = p.part + hb * D + lane * DPL;
-            constexpr uint32_t MB = DPL >= 8 ? 8u : 16u;  // chunks in flight (register budget)
-            float vs[MB][DPL];
-            auto load_rows = [&](uint32_t cb) {
-#pragma unroll
-              for (uint32_t k = 0; k < MB; ++k) {
-                const float *oc = ob + (size_t)(cb + k) * G * D;
-                if (cb + k < nch) {
-                  if constexpr (DPL % 4 == 0) {
-#pragma unroll
-                    for (int d = 0; d < DPL; d += 4) {
-                      const float4 v = __ldcg(reinterpret_cast<const float4 *>(oc + d));
-                      vs[k][d] = v.x;
-                      vs[k][d + 1] = v.y;
-                      vs[k][d + 2] = v.z;
-                      vs[k][d + 3] = v.w;
-                    }
-                  } else {
-#pragma unroll
-                    for (int d = 0; d < DPL; ++d) vs[k][d] = __ldcg(oc + d);
-                  }
-                }
-              }
-            };
-            auto ml_of = [&](uint32_t c) { return __ldcg(&p.part_ml[hb + (size_t)c * G]); };
-            load_rows(0);
-            const float2 mla = lane < nch ? ml_of(lane) : make_float2(-INFINITY, 0.f);
-            const float2 mlb = lane + 32u < nch ? ml_of(lane + 32u) : make_float2(-INFINITY, 0.f);
-            float M = fmaxf(mla.x, mlb.x);
-            for (uint32_t c = lane + 64u; c < nch; c += 32) M = fmaxf(M, ml_of(c).x);
-            M = warp_max(M);
-            float o[DPL];
-#pragma unroll
-            for (int d = 0; d < DPL; ++d) o[d] = 0.f;
-            float Lp = 0.f;
-            for (uint32_t c0 = 0; c0 < nch; c0 += 32) {
-              float wl = 0.f;
-              if (c0 + lane < nch) {
-                const float2 ml = c0 == 0 ? mla : c0 == 32 ? mlb : ml_of(c0 + lane);
-                wl = ml.x == -INFINITY ? 0.f : expf(ml.x - M);
-                Lp = fmaf(wl, ml.y, Lp);
-              }
-              const uint32_t nc = min(32u, nch - c0);
-              for (uint32_t cb = 0; cb < nc; cb += MB) {
-                if (c0 + cb != 0) load_rows(c0 + cb);
-#pragma unroll
-                for (uint32_t k = 0; k < MB; ++k) {
-                  const float wc = __shfl_sync(0xffffffffu, wl, (cb + k) & 31u);
-                  if (cb + k < nc) {
-#pragma unroll
-                    for (int d = 0; d < DPL; ++d) o[d] = fmaf(wc, vs[k][d], o[d]);
-                  }
-                }
-              }
-            }
-            const float inv = 1.0f / warp_sum(Lp);
-#pragma unroll
-            for (int d = 0; d < DPL; ++d) p.attn[((size_t)a.kvh * G + g0) * D + lane * DPL + d] = o[d] * inv;
-          }
-          if (cw == 0 && lane == 0) p.tickets[a.kvh] = 0;
+        // the last unit of this KV head to finish (its ticket acquired the
+        // other units' partials) releases the head to its merge slices
+        if (cw == 0 && lane == 0 && atomic_add_acq_rel(&p.tickets[a.kvh], 1u) == nch - 1u) {
+          p.tickets[a.kvh] = 0;
+          grid_arrive(p.ready + a.kvh);
         }
-        named_bar(1, NCT);  // sQB / sS / sflags reuse by the next unit
+        named_bar(1, NCT);  // sQB / sS reuse by the next unit
+      }
+      // Merge slices, one query head each, on the CTAs from the end of the
+      // grid (free of units while n_units <= gridDim.x - heads): wait for the
+      // head's release, then o = sum_c exp(m_c - M) o_c / sum_c exp(m_c - M) l_c
+      // over its chunks. Thread (grp, col) sums float4 column col of the chunks
+      // grp, grp + NGR, ...; the groups' rows are then added in order.
+      for (uint32_t j = gridDim.x - 1u - blockIdx.x; j < p.heads; j += gridDim.x) {
+        const uint32_t kvh = j / G, g0 = j - kvh * G;
+        if (cw == 0 && lane == 0 && !grid_wait(p.ready + kvh, srdy[kvh] + l + 1u, err)) set_error(err, kErrGridWait);
+        named_bar(1, NCT);
+        constexpr uint32_t NCOL = D / 4u, NGR = NCT / NCOL, MR = 8u;  // columns, chunk groups, rows in flight
+        static_assert(NCT % NCOL == 0, "whole chunk groups");
+        float *sW = reinterpret_cast<float *>(aux);  // [max_chunks] weights, then 1/sum
+        float4 *sO = reinterpret_cast<float4 *>(aux + step_merge_w_bytes(p.max_chunks));
+        const uint32_t col = tid % NCOL, grp = tid / NCOL;
+        const size_t hb = (size_t)kvh * p.max_chunks * G + g0;  // slot of chunk 0
+        const float4 *ob = reinterpret_cast<const float4 *>(p.part + hb * D) + col;
+        auto row = [&](uint32_t c) { return __ldcg(ob + (size_t)c * G * NCOL); };
+        // the first MR rows of this thread's chunks load with the weights
+        float4 v[MR];
+#pragma unroll
+        for (uint32_t i = 0; i < MR; ++i) {
+          const uint32_t c = grp + i * NGR;
+          v[i] = c < nch ? row(c) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+        if (cw == 0) {
+          constexpr uint32_t MLR = 4u;  // (max, sum) pairs per lane held in registers
+          float2 ml[MLR];
+          float M = -INFINITY;
+#pragma unroll
+          for (uint32_t i = 0; i < MLR; ++i) {
+            const uint32_t c = lane + 32u * i;
+            ml[i] = c < nch ? __ldcg(&p.part_ml[hb + (size_t)c * G]) : make_float2(-INFINITY, 0.f);
+            M = fmaxf(M, ml[i].x);
+          }
+          for (uint32_t c = lane + 32u * MLR; c < nch; c += 32u) M = fmaxf(M, __ldcg(&p.part_ml[hb + (size_t)c * G]).x);
+          M = warp_max(M);
+          float Ls = 0.f;
+#pragma unroll
+          for (uint32_t i = 0; i < MLR; ++i) {
+            const uint32_t c = lane + 32u * i;
+            if (c < nch) {
+              const float w = ml[i].x == -INFINITY ? 0.f : expf(ml[i].x - M);
+              sW[c] = w;
+              Ls = fmaf(w, ml[i].y, Ls);
+            }
+          }
+          for (uint32_t c = lane + 32u * MLR; c < nch; c += 32u) {
+            const float2 m2 = __ldcg(&p.part_ml[hb + (size_t)c * G]);
+            const float w = m2.x == -INFINITY ? 0.f : expf(m2.x - M);
+            sW[c] = w;
+            Ls = fmaf(w, m2.y, Ls);
+          }
+          Ls = warp_sum(Ls);
+          if (lane == 0) sW[p.max_chunks] = 1.0f / Ls;
+        }
+        named_bar(1, NCT);
+        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+        auto acc = [&](uint32_t c, const float4 &r) {
+          const float w = sW[c];
+          o.x = fmaf(w, r.x, o.x);
+          o.y = fmaf(w, r.y, o.y);
+          o.z = fmaf(w, r.z, o.z);
+          o.w = fmaf(w, r.w, o.w);
+        };
+#pragma unroll
+        for (uint32_t i = 0; i < MR; ++i)
+          if (grp + i * NGR < nch) acc(grp + i * NGR, v[i]);
+        for (uint32_t c = grp + MR * NGR; c < nch; c += NGR) acc(c, row(c));
+        sO[grp * NCOL + col] = o;
+        named_bar(1, NCT);
+        if (tid < NCOL) {
+          float4 t = sO[tid];
+          for (uint32_t gi = 1; gi < NGR; ++gi) {
+            const float4 u = sO[gi * NCOL + tid];
+            t.x += u.x;
+            t.y += u.y;
+            t.z += u.z;
+            t.w += u.w;
+          }
+          const float inv = sW[p.max_chunks];
+          reinterpret_cast<float4 *>(p.attn + ((size_t)kvh * G + g0) * D)[tid] =
+              make_float4(t.x * inv, t.y * inv, t.z * inv, t.w * inv);
+        }
+        named_bar(1, NCT);  // sW / sO reuse
       }
       arrive();
       continue;
@@ -724,7 +789,36 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_step_kernel(const __grid
     Mode mode = Mode::PLAIN;
     bool rms = false, consume = true;
     float *xout = nullptr;
-    if (ph == nb) {
+    if (ph < p.pre) {
+      // ResidualLM: linear_bias.comp (+ fsq_quantize.comp) and fusion_linear.comp
+      if (ph < 2u && !p.fsq_on) {
+        wait_phase(ph);
+        arrive();
+        continue;
+      }
+      mp.alpha = 1.0f;
+      if (ph == 0u) {
+        mp.g = p.g_fin;
+        mp.out = p.fsq_lat;
+        mp.resid = p.b_fin;
+        src.x = p.res_base;
+        mode = Mode::FSQ;
+      } else if (ph == 1u) {
+        mp.g = p.g_fout;
+        mp.out = p.fuse_in;
+        mp.out2 = p.fsq_res;
+        mp.resid = p.b_fout;
+        src.x = p.fsq_lat;
+        mode = Mode::RESID;
+      } else {
+        mp.g = p.g_fuse;
+        mp.out = p.hid_a;
+        mp.out2 = p.fused;
+        mp.resid = p.b_fuse;
+        src.x = p.fuse_in;
+        mode = Mode::RESID;
+      }
+    } else if (ph == nb) {
       // final RMSNorm into out (CTA 0), and the LM head on it when logits are wanted
       if (!p.want_logits && blockIdx.x != 0) break;
       mp.g = p.want_logits ? p.g_head : p.g_qkv;
