@@ -152,10 +152,15 @@ __device__ __forceinline__ float warp_sum(float v) {
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   return v;
 }
+// Largest value over the warp in one redux.sync: fp32 bit patterns mapped to
+// u32 keys in the same order (negative values: every bit flipped; others: the
+// sign bit set), the largest key taken, and mapped back. Exact, like fmaxf over
+// the lanes (NaN inputs excepted).
 __device__ __forceinline__ float warp_max(float v) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-  return v;
+  const uint32_t b = __float_as_uint(v);
+  const uint32_t k = b ^ ((uint32_t)((int32_t)b >> 31) | 0x80000000u);
+  const uint32_t r = __reduce_max_sync(0xffffffffu, k);
+  return __uint_as_float(r ^ ((r & 0x80000000u) ? 0x80000000u : 0xFFFFFFFFu));
 }
 
 // Sums 8 per-lane values over the warp with 9 shuffles (instead of 8 x 5): on

@@ -118,9 +118,8 @@ __device__ __forceinline__ void step_activation(uint32_t C, uint32_t cols_pad, b
   float inv_rms = 1.0f;
   // with the factor deferred, the sum of squares and the operand's largest
   // magnitude come from one pass; the operand is then x * w
-  float mdef = 0.f;
+  float mdef = 0.f, ss = 0.f;
   if (rms) {
-    float ss = 0.f;
 #pragma unroll 1
     for (uint32_t g = 0; g < JG; ++g) {
       const float4 v = ld4(stg, elem0(g));
@@ -131,10 +130,10 @@ __device__ __forceinline__ void step_activation(uint32_t C, uint32_t cols_pad, b
                                  fmaxf(fabsf(__fmul_rn(v.z, w.z)), fabsf(__fmul_rn(v.w, w.w)))));
       }
     }
-    ss = warp_sum(ss);
-    if (defer) {
-      if (lane == 0) scr[8 + cw] = ss;
-    } else {
+    // deferred: the warp's sum of squares is reduced after the digits (only
+    // the epilogue reads it)
+    if (!defer) {
+      ss = warp_sum(ss);
       if (lane == 0) scr[cw] = ss;
       named_bar(1, NCT);
       float tot = 0.f;
@@ -211,6 +210,10 @@ __device__ __forceinline__ void step_activation(uint32_t C, uint32_t cols_pad, b
       }
     }
     if (cw == 0 && lane == 0) *sx = nz ? pow2f(e) : 0.f;
+    if (defer) {
+      ss = warp_sum(ss);
+      if (lane == 0) scr[8 + cw] = ss;
+    }
     named_bar(1, NCT);
   } else {
     // whole-vector power-of-two scale, then fp16 hi + lo (mv_activation)
@@ -251,6 +254,10 @@ __device__ __forceinline__ void step_activation(uint32_t C, uint32_t cols_pad, b
       }
     }
     if (cw == 0 && lane == 0) *xscale = pow2f(e);
+    if (defer) {
+      ss = warp_sum(ss);
+      if (lane == 0) scr[8 + cw] = ss;
+    }
     named_bar(1, NCT);
   }
 }
