@@ -221,6 +221,24 @@ def test_backbone_long_context(ctx, model_dir, name):
     p.close()
 
 
+@pytest.mark.parametrize("name", ["tiny", "tiny_f16", "pin"])
+def test_attention_merge_long_context(ctx, model_dir, name):
+    """Contexts long enough that the attention units outnumber the CTAs left free for the merge
+    slices (tiny: 188 units on 148 CTAs, so some CTAs run two units and the last eight run a
+    unit and then a slice), and that a slice loads its chunks' rows in more than one batch
+    (pin: 94 chunks of one KV head at head_dim 128, 64 rows per batch)."""
+    spec = synth.preset(name)
+    n = 6000
+    p = Pair(ctx, spec_path(model_dir, name), n + 8)
+    k, v = synth.kv_prefill(spec, n)
+    p.write_kv(k, v)
+    hs = synth.hidden_inputs(spec, 3)
+    for i in range(3):
+        p.step_embedding(hs[i])
+        p.compare(f"{name} pos {n + i}")
+    p.close()
+
+
 def test_decode_batch_matches_single_streams(ctx, model_dir):
     """vg_decode_batch: every stream advances as if decoded alone (ragged positions)."""
     spec = synth.preset("tiny")
