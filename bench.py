@@ -85,6 +85,15 @@ def ensure_model(spec, rank, world, pg_barrier):
     return p
 
 
+def launch_traffic(workload):
+    """DRAM bytes of one step-kernel launch of this workload from an ncu capture
+    (profiles/traffic.json), or None."""
+    tr = ROOT / "profiles" / "traffic.json"
+    if not tr.exists():
+        return None
+    return json.loads(tr.read_text()).get(workload, {}).get("decode_step_kernel")
+
+
 def measured_peaks():
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -296,8 +305,9 @@ def run_residual(args, rank, world, local):
                                if eng.kernel_mode == 1 else
                                "FSQ + fusion matvecs and the ResidualLM layers (whole position)",
                      "bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
-                     "frac": round(ach / peak, 4), "traffic": None, "bytes_per_launch": int(avg_bytes),
-                     "peak_source": f"{peak_kind} hbm_gbs"},
+                     "frac": round(ach / peak, 4),
+                     "traffic": launch_traffic(args.workload) if eng.kernel_mode == 1 else None,
+                     "bytes_per_launch": int(avg_bytes), "peak_source": f"{peak_kind} hbm_gbs"},
         "e2e": {"value": round(world * KE / (e_ms_max / 1e3), 2), "unit": "positions/s", "steps": KE,
                 "h2d_bytes_per_step": 2 * H * 4, "d2h_bytes_per_step": H * 4},
         "gpu_launches": K * (1 if eng.kernel_mode == 1 else 4 + 5 * L + 1),
@@ -420,7 +430,8 @@ def run_batch(args, rank, world, local):
         },
         "roofline": {"kernel": "decode_step_kernel (one launch per stream token; the weight pass is not "
                                "shared between streams)", "bound": "hbm", "achieved": round(launch_ach, 1),
-                     "peak": peak, "unit": "GB/s", "frac": round(launch_ach / peak, 4), "traffic": None,
+                     "peak": peak, "unit": "GB/s", "frac": round(launch_ach / peak, 4),
+                     "traffic": launch_traffic(args.workload),
                      "bytes_per_launch": int(launch_bytes),
                      "avg_launch_ms": round(step_ms / S, 5), "peak_source": f"{peak_kind} hbm_gbs"},
         "batch_roofline": {"bytes_per_step": int(batch_bytes), "achieved": round(batch_ach, 1), "peak": peak,
