@@ -1141,7 +1141,7 @@ int vg_stream_create(vg_model *m, uint32_t max_context, vg_stream **out) {
                  o_bar = take(8), o_sl = take((size_t)c.block_count * sizeof(StepLayer)),
                  o_sp = take((size_t)c.head_count_kv * nch * G * D * 4),
                  o_sml = take((size_t)c.head_count_kv * nch * G * 8),
-                 o_stk = take((size_t)c.head_count_kv * 4), o_rdy = take((size_t)c.head_count_kv * 8);
+                 o_rdy = take((size_t)c.head_count_kv * 8);
     const uint32_t LAT = m->residual ? m->acoustic.fsq_latent_dim : 0u, HR = m->residual ? H : 0u;
     const size_t o_rb = take((size_t)HR * 4), o_rl = take((size_t)LAT * 4), o_rf = take((size_t)HR * 4),
                  o_ri = take((size_t)HR * 8), o_rs = take((size_t)HR * 4);
@@ -1210,7 +1210,6 @@ int vg_stream_create(vg_model *m, uint32_t max_context, vg_stream **out) {
       }
       p.part = (float *)(b + o_sp);
       p.part_ml = (float2 *)(b + o_sml);
-      p.tickets = (uint32_t *)(b + o_stk);
       p.ready = (unsigned long long *)(b + o_rdy);
       if (m->residual) {
         p.res_base = s->res_base;

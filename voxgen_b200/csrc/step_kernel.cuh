@@ -40,8 +40,10 @@ struct StepParams {
   float *q, *attn, *gate, *logits, *out;
   float *part;              // attention partial outputs [kv_heads][max_chunks][G][head_dim]
   float2 *part_ml;          // their running max and sum [kv_heads][max_chunks][G]
-  uint32_t *tickets;        // [kv_heads], zero between steps
-  unsigned long long *ready;  // [kv_heads] merge releases: +1 per layer when a head's chunks are all written
+  // [kv_heads] attention-unit arrivals, monotonic: each unit adds 1 with
+  // release semantics once its partials are written, so a KV head's chunks are
+  // all written when its count has grown by the chunk count in this layer
+  unsigned long long *ready;
   const float *inv_freq, *ext;
   float rope_scaling, eps, res_scale, emb_scale, logit_scale, attn_scale;
   uint32_t H, F, heads, kv_heads, head_dim, ctx;
@@ -323,7 +325,7 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_step_kernel(const __grid
   float *stw = reinterpret_cast<float *>(smem + L.stw);
   float *scr = reinterpret_cast<float *>(smem + L.scr);                                 // 64 floats
   unsigned long long *sbase = reinterpret_cast<unsigned long long *>(smem + L.scr + 256u);
-  // merge-release counts of the KV heads at the step's start (kv_heads <= 64)
+  // unit-arrival counts of the KV heads at the step's start (kv_heads <= 64)
   unsigned long long *srdy = reinterpret_cast<unsigned long long *>(smem + L.scr + 512u);
 
   const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
@@ -608,7 +610,7 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_step_kernel(const __grid
         // cores, a warp per (16 positions, 8 heads) tile
         for (uint32_t it = cw; it < (len16 / 16u) * HT; it += kMvConsumers) {
           const uint32_t pt = it / HT, ht = it % HT;
-          float c[4] = {0.f, 0.f, 0.f, 0.f};
+          float c[4] = {0.f, 0.f, 0.f, 0.f}, cl[4] = {0.f, 0.f, 0.f, 0.f};  // hi and lo chains
           const __half *kb = kS + (pt * 16u + (lane & 15u)) * D + (lane >> 4) * 8u;
 #pragma unroll 4
           for (uint32_t ks = 0; ks < KS; ++ks) {
@@ -617,13 +619,13 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_step_kernel(const __grid
             const uint2 bh = sQB[((ht * KS + ks) * 2u + 0u) * 32u + lane];
             const uint2 bl = sQB[((ht * KS + ks) * 2u + 1u) * 32u + lane];
             mma_f16(c, af, bh.x, bh.y);
-            mma_f16(c, af, bl.x, bl.y);
+            mma_f16(cl, af, bl.x, bl.y);
           }
           const uint32_t t = pt * 16u + (lane >> 2), g = ht * 8u + (lane & 3u) * 2u;
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const uint32_t tt = t + (j >> 1) * 8u, gg = g + (j & 1);
-            if (tt < a.len && gg < G) sS[gg * SST + tt] = __fmul_rn(c[j], p.attn_scale);
+            if (tt < a.len && gg < G) sS[gg * SST + tt] = __fmul_rn(__fadd_rn(c[j], cl[j]), p.attn_scale);
           }
         }
         named_bar(1, NCT);
@@ -651,7 +653,7 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_step_kernel(const __grid
         // A = V^T from the V rows by transposing loads, B = P^T in fp16 hi + lo
         for (uint32_t it = cw; it < KS * HT; it += kMvConsumers) {
           const uint32_t dt = it / HT, ht = it % HT;
-          float c[4] = {0.f, 0.f, 0.f, 0.f};
+          float c[4] = {0.f, 0.f, 0.f, 0.f}, cl[4] = {0.f, 0.f, 0.f, 0.f};  // hi and lo chains
           const uint32_t gb = ht * 8u + (lane >> 2);  // head of this lane's B column
           const float *pg = sS + (gb < G ? gb : 0u) * SST;
           const __half *vb = vS + (((lane >> 4) & 1u) * 8u + (lane & 7u)) * D + dt * 16u + ((lane >> 3) & 1u) * 8u;
@@ -674,40 +676,38 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_step_kernel(const __grid
                                  __float2half_rn(w[2 * j + 1] - __half2float(h1)));
             }
             mma_f16(c, af, bh[0], bh[1]);
-            mma_f16(c, af, bl[0], bl[1]);
+            mma_f16(cl, af, bl[0], bl[1]);
           }
           // c: dims dt * 16 + gq (+ 8), heads ht * 8 + 2tq (+ 1)
           const uint32_t d = dt * 16u + (lane >> 2), g = ht * 8u + (lane & 3u) * 2u;
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const uint32_t dd = d + (j >> 1) * 8u, gg = g + (j & 1);
-            if (gg < G) p.part[(((size_t)a.kvh * p.max_chunks + a.c) * G + gg) * D + dd] = c[j];
+            if (gg < G) p.part[(((size_t)a.kvh * p.max_chunks + a.c) * G + gg) * D + dd] = __fadd_rn(c[j], cl[j]);
           }
         }
         // every warp is done with the K and V stages, and every partial of the
-        // unit is written (the barrier orders those writes before the ticket's
+        // unit is written (the barrier orders those writes before the unit's
         // release)
         named_bar(1, NCT);
         if (lane == 0) {
           mbar_arrive(&R.empty[sK]);
           mbar_arrive(&R.empty[sV]);
         }
-        // the last unit of this KV head to finish (its ticket acquired the
-        // other units' partials) releases the head to its merge slices
-        if (cw == 0 && lane == 0 && atomic_add_acq_rel(&p.tickets[a.kvh], 1u) == nch - 1u) {
-          p.tickets[a.kvh] = 0;
-          grid_arrive(p.ready + a.kvh);
-        }
+        // this unit's partials are written: one arrival at its KV head
+        if (cw == 0 && lane == 0) grid_arrive(p.ready + a.kvh);
         named_bar(1, NCT);  // sQB / sS reuse by the next unit
       }
       // Merge slices, one query head each, on the CTAs from the end of the
-      // grid (free of units while n_units <= gridDim.x - heads): wait for the
-      // head's release, then o = sum_c exp(m_c - M) o_c / sum_c exp(m_c - M) l_c
+      // grid (free of units while n_units <= gridDim.x - heads): wait for all
+      // nch arrivals of the head's units in this layer (the acquire that reads
+      // the last one synchronises with every unit's release), then
+      // o = sum_c exp(m_c - M) o_c / sum_c exp(m_c - M) l_c
       // over its chunks. Thread (grp, col) sums float4 column col of the chunks
       // grp, grp + NGR, ...; the groups' rows are then added in order.
       for (uint32_t j = gridDim.x - 1u - blockIdx.x; j < p.heads; j += gridDim.x) {
         const uint32_t kvh = j / G, g0 = j - kvh * G;
-        if (cw == 0 && lane == 0 && !grid_wait(p.ready + kvh, srdy[kvh] + l + 1u, err)) set_error(err, kErrGridWait);
+        if (cw == 0 && lane == 0 && !grid_wait(p.ready + kvh, srdy[kvh] + (unsigned long long)(l + 1u) * nch, err)) set_error(err, kErrGridWait);
         named_bar(1, NCT);
         constexpr uint32_t NCOL = D / 4u, NGR = NCT / NCOL, MR = 8u;  // columns, chunk groups, rows in flight
         static_assert(NCT % NCOL == 0, "whole chunk groups");
