@@ -52,6 +52,26 @@ WORKLOADS = {
 }
 
 
+# The JSON line goes to the process's original stdout; everything else that
+# writes to file descriptor 1 (NCCL prints its version line there at
+# communicator set-up) is sent to stderr, so stdout holds the one line.
+_JSON_OUT = None
+
+
+def quiet_stdout():
+    global _JSON_OUT
+    if _JSON_OUT is None:
+        sys.stdout.flush()
+        _JSON_OUT = os.fdopen(os.dup(1), "w")
+        os.dup2(2, 1)
+
+
+def emit(line):
+    out = _JSON_OUT or sys.stdout
+    out.write(json.dumps(line) + "\n")
+    out.flush()
+
+
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -197,7 +217,7 @@ def run_reference(args, rank, world):
                          "sample": f"{n} decode steps from position {wl['prefill']} ({what}, {cores} threads)"},
         "e2e": {"value": val, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(line)
 
 
 def cpu_baseline_sample(args, spec, path, wl):
@@ -330,7 +350,7 @@ def run_residual(args, rank, world, local):
     base.close()
     ctx.close()
     if rank == 0:
-        print(json.dumps(line), flush=True)
+        emit(line)
     replicas.barrier(pg)
     replicas.shutdown(pg)
 
@@ -452,13 +472,14 @@ def run_batch(args, rank, world, local):
     model.close()
     ctx.close()
     if rank == 0:
-        print(json.dumps(line), flush=True)
+        emit(line)
     replicas.barrier(pg)
     replicas.shutdown(pg)
 
 
 def main():
     args = parse()
+    quiet_stdout()
     rank, world, local = dist_env()
     if args.workload == "cfg4" and args.impl == "ours":
         run_batch(args, rank, world, local)
@@ -466,8 +487,8 @@ def main():
     if args.workload == "residual":
         if args.impl == "reference":
             if rank == 0:
-                print(json.dumps({"impl": "reference", "unavailable":
-                                  "the ResidualLM workload has no reference CPU arm (the reference arm covers BaseLM)"}))
+                emit({"impl": "reference", "unavailable":
+                      "the ResidualLM workload has no reference CPU arm (the reference arm covers BaseLM)"})
             return
         run_residual(args, rank, world, local)
         return
@@ -625,7 +646,7 @@ def main():
     model.close()
     ctx.close()
     if rank == 0:
-        print(json.dumps(line), flush=True)
+        emit(line)
     replicas.barrier(pg)
     replicas.shutdown(pg)
 
