@@ -39,10 +39,15 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
 WORKLOADS = {
-    "cfg2": dict(preset="cfg2", prefill=1023, ctx=4096, desc="BaseLM 28L H2048 16x128 GQA 2 KV F6144 Q8_0"),
-    "cfg3": dict(preset="cfg3", prefill=1023, ctx=4096, desc="BaseLM 28L H2048 16x128 GQA 2 KV F6144 F16"),
-    "cfg1": dict(preset="cfg1", prefill=128, ctx=512, desc="BaseLM 24L H1024 16x64 GQA 2 KV F4096 Q8_0"),
-    "cfg0": dict(preset="cfg0", prefill=512, ctx=1024, desc="one BaseLM layer H1024 16x64 GQA 2 KV F4096 Q8_0"),
+    # span: the decode positions the config covers; the timed steps are spread over it
+    "cfg2": dict(preset="cfg2", prefill=1023, ctx=4096, span=(1024, 4095),
+                 desc="BaseLM 28L H2048 16x128 GQA 2 KV F6144 Q8_0"),
+    "cfg3": dict(preset="cfg3", prefill=1023, ctx=4096, span=(1024, 4095),
+                 desc="BaseLM 28L H2048 16x128 GQA 2 KV F6144 F16"),
+    "cfg1": dict(preset="cfg1", prefill=128, ctx=512, span=(128, 383),
+                 desc="BaseLM 24L H1024 16x64 GQA 2 KV F4096 Q8_0"),
+    "cfg0": dict(preset="cfg0", prefill=512, ctx=1024, span=(512, 1023),
+                 desc="one BaseLM layer H1024 16x64 GQA 2 KV F4096 Q8_0"),
     # ResidualLM + FSQ + fusion after BaseLM (src/acoustic.rs:851-1035), VoxCPM2's shape
     "residual": dict(acoustic="res_cfg2", prefill=0, ctx=4096,
                      desc="ResidualLM 8L H2048 16x128 GQA 2 KV F6144 F16 + FSQ 512 + fusion"),
@@ -122,41 +127,107 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
-class ClockSampler:
-    """nvidia-smi clock / throttle sampling during the timed region."""
+# NVML clock-event reason bits (nvmlClocksEventReason*): reported by name when active.
+_REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+            0x80: "hw_power_brake_slowdown"}
 
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+class ClockSampler:
+    """SM clock and clock-event reasons sampled during the timed region: NVML in a thread every
+    10 ms (plus one sample at start and one at stop, so a region of a few milliseconds still has
+    samples), else nvidia-smi. Reads only; nothing is set."""
 
     def __init__(self, device_index: int):
+        import threading
+        self.rows = []
         self.proc = None
-        self.dev = device_index
+        self.nv = None
+        self.stop_ev = threading.Event()
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={device_index}", f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "100"],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except (FileNotFoundError, OSError):
-            self.proc = None
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = None
+            try:
+                import torch
+                uuid = str(torch.cuda.get_device_properties(device_index).uuid)
+                self.h = pynvml.nvmlDeviceGetHandleByUUID(("GPU-" + uuid) if not uuid.startswith("GPU-") else uuid)
+            except Exception:
+                self.h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self._sample()
+            self.thread = threading.Thread(target=self._loop, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.nv = None
+            try:
+                self.proc = subprocess.Popen(
+                    ["nvidia-smi", f"--id={device_index}", "--query-gpu=clocks.sm,clocks.max.sm,"
+                     "clocks_event_reasons.active", "--format=csv,noheader,nounits", "-lms", "20"],
+                    stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            except (FileNotFoundError, OSError):
+                self.proc = None
+
+    def _sample(self):
+        nv = self.nv
+        sm = nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)
+        try:
+            bits = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+        except AttributeError:
+            bits = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self.h)
+        self.rows.append((float(sm), float(self.max_mhz), int(bits)))
+
+    def _loop(self):
+        while not self.stop_ev.wait(0.01):
+            try:
+                self._sample()
+            except Exception:
+                return
 
     def stop(self):
-        if not self.proc:
+        if self.nv is not None:
+            self.stop_ev.set()
+            self.thread.join(timeout=1)
+            try:
+                self._sample()
+            except Exception:
+                pass
+            rows = self.rows
+        elif self.proc:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            rows = []
+            for r in out.strip().splitlines():
+                f = [x.strip() for x in r.split(",")]
+                try:
+                    rows.append((float(f[0]), float(f[1]), int(f[2], 16)))
+                except (ValueError, IndexError):
+                    pass
+        else:
             return None
-        self.proc.terminate()
-        try:
-            out, _ = self.proc.communicate(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-            out, _ = self.proc.communicate()
-        rows = [r.split(",") for r in out.strip().splitlines() if r.count(",") >= 8]
         if not rows:
             return None
-        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.strip() == "Active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows)}
+        reasons = sorted({n for _, _, b in rows for bit, n in _REASONS.items() if b & bit})
+        return {"sm_mhz": statistics.median(r[0] for r in rows), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(rows), "source": "nvml" if self.nv else "nvidia-smi"}
+
+
+def spread_blocks(k, lo, hi, max_blocks=16):
+    """k decode steps as blocks (start position, steps) whose starts are spread evenly over the
+    positions [lo, hi], every block inside the range: at most max_blocks blocks, more only when
+    one block would not fit in the range."""
+    span = hi - lo + 1
+    nb = max(1, min(max_blocks, k), -(-k // span))
+    sizes = [k // nb + (1 if b < k % nb else 0) for b in range(nb)]
+    out = []
+    for b, n in enumerate(sizes):
+        last = hi - n + 1                          # latest start that keeps the block in range
+        out.append((lo + (round(b * (last - lo) / (nb - 1)) if nb > 1 else 0), n))
+    return [(p, n) for p, n in out if n > 0]
 
 
 def algorithmic_bytes(info, positions):
@@ -511,30 +582,38 @@ def main():
     spec = synth.preset(wl["preset"])
     path = ensure_model(spec, rank, world, barrier)
     K, W = args.steps, args.warmup
-    need = wl["prefill"] + W + K
-    max_ctx = max(wl["ctx"], need)
+    lo, hi = wl["span"]
+    max_ctx = max(wl["ctx"], hi + 1)
 
     ctx = api.Context(local)
     model = api.Model(ctx, path)
     info = model.info
     eng = api.BaseLmEngine(model, max_ctx)
-    kpre, vpre = synth.kv_prefill(spec, wl["prefill"])
-    toks = synth.token_ids(spec, W + K, seed_index=3000 + rank)
+    kpre, vpre = synth.kv_prefill(spec, hi)
+    toks = synth.token_ids(spec, W + max(K, args.e2e_steps or 0), seed_index=3000 + rank)
     stream = torch.cuda.ExternalStream(eng.cuda_stream, device=torch.device("cuda", local))
 
-    # ---- device-timed decode: W warm-up + K timed steps from the prefilled position ----
+    # ---- device-timed decode: W warm-up steps, then K timed steps spread over the span ----
+    # The cache holds seeded rows up to the end of the span, and the K steps run in blocks
+    # that start at evenly spaced positions (vg_stream_seek between blocks, inside the timed
+    # region), so the rate represents the whole context range the config decodes over.
     eng.write_kv(kpre, vpre)
+    eng.seek(lo)
     for t in toks[:W]:
         eng.decode_token_gpu_only(int(t))
     eng.sync()
-    p0 = eng.position
+    blocks = spread_blocks(K, lo, hi)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     torch.cuda.synchronize()
     clocks = ClockSampler(local)
     start.record(stream)
-    for t in toks[W:W + K]:
-        eng.decode_token_gpu_only(int(t))
+    i = W
+    for b0, n in blocks:
+        eng.seek(b0)
+        for t in toks[i:i + n]:
+            eng.decode_token_gpu_only(int(t))
+        i += n
     end.record(stream)
     eng.sync(timeout_s=600)
     torch.cuda.synchronize()
@@ -542,12 +621,13 @@ def main():
     clk = clocks.stop()
     ms = start.elapsed_time(end)
     ms_max = replicas.max_over_ranks(ms, pg, dev)
-    positions = list(range(p0, p0 + K))
+    positions = [b0 + j for b0, n in blocks for j in range(n)]
 
-    # ---- e2e through the C ABI with host buffers ----
+    # ---- e2e through the C ABI with host buffers, over the same spread of positions ----
     KE = args.e2e_steps or min(K, 500)
-    eng.write_kv(kpre, vpre)
+    e_blocks = spread_blocks(KE, lo, hi)
     host_out = np.empty(info["embedding_length"], np.float32)
+    eng.seek(lo)
     for t in toks[:min(W, 5)]:
         eng.decode_token_gpu_only(int(t))
         eng.output()
@@ -555,9 +635,13 @@ def main():
     torch.cuda.synchronize()
     e_start, e_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e_start.record(stream)
-    for t in toks[W:W + KE]:
-        eng.decode_token_gpu_only(int(t))          # token id copied from pinned host memory
-        host_out[:] = eng.output()                  # D2H of the final hidden state + sync
+    i = W
+    for b0, n in e_blocks:
+        eng.seek(b0)
+        for t in toks[i:i + n]:
+            eng.decode_token_gpu_only(int(t))          # token id copied from pinned host memory
+            host_out[:] = eng.output()                  # D2H of the final hidden state + sync
+        i += n
     e_end.record(stream)
     torch.cuda.synchronize()
     barrier()
@@ -586,10 +670,10 @@ def main():
                 "traffic": traffic.get("decode_step_kernel"), "bytes_per_launch": byt,
                 "avg_launch_ms": round(avg_ms, 5), "peak_source": peak_src}
     elif not args.no_profile:
-        eng.write_kv(kpre, vpre)
+        eng.seek(lo)
         for t in toks[:3]:
             eng.profile_step(int(t))       # warm
-        eng.write_kv(kpre, vpre)
+        eng.seek(lo)
         prof = [eng.profile_step(int(t)) for t in toks[3:8]]
         rows = [r for step in prof for r in step if r["name"] == "gate_up"]
         avg_ms = sum(r["ms"] for r in rows) / len(rows)
@@ -613,8 +697,15 @@ def main():
         "config": {
             "workload": f"{args.workload}: {wl['desc']}",
             "weights": "Q8_0" if info["format"] == 8 else "F16",
-            "compute": "int8/fp16 weights dequantised in registers, fp32 accumulation",
-            "streams_per_gpu": 1, "positions": [positions[0], positions[-1]],
+            "compute": ("Q8_0: activation as three int8 digits with one shared power of two per vector, "
+                        "exact s8 MMA (mma.sync), fp32 rescale by the fp16 block scales"
+                        if info["format"] == 8 else
+                        "F16: activation as fp16 hi + lo with one shared power of two per vector, "
+                        "f16 MMA (mma.sync) with fp32 accumulation"),
+            "streams_per_gpu": 1, "positions": [[b0, b0 + n - 1] for b0, n in blocks],
+            "position_sampling": (f"{K} timed steps in {len(blocks)} blocks whose starts are spread evenly over "
+                                  f"positions {lo}-{hi} (vg_stream_seek between blocks, inside the timed region; "
+                                  f"the cache holds seeded rows below every position)"),
             "parallelism": f"replicas x{world} (weights replicated, no collectives)",
             "l2": f"inputs larger than L2: {info['layer_weight_bytes'] / 1e9:.2f} GB of weights per step",
             "input": "seeded token ids",

@@ -144,6 +144,20 @@ int vg_stream_destroy(vg_stream *stream);
  * src/baselm.rs:616-620). */
 int vg_stream_reset(vg_stream *stream);
 int vg_stream_position(const vg_stream *stream, uint32_t *position);
+/* Moves the decode position to `position` (<= max_context) without touching
+ * the cache: the next step attends over rows [0, position] and writes row
+ * `position`, whatever rows [0, position) hold. vg_stream_reset is
+ * vg_stream_seek(stream, 0) (BaseLmEngine::reset, src/baselm.rs:616-620);
+ * other positions serve callers that restore a session whose cache they kept,
+ * and benchmarks that time steps at chosen context lengths. */
+int vg_stream_seek(vg_stream *stream, uint32_t position);
+/* Wall-clock limit of every bounded wait inside this stream's kernels (grid
+ * barriers, bulk-copy barriers, attention merge counters), in nanoseconds; 0
+ * restores the default of 2 s. A wait that runs out sets a bit in the stream's
+ * device error flag and the kernel leaves; the next vg_stream_sync or output
+ * copy returns VG_EDEVICE. Enqueued on the stream: it applies to later steps.
+ * The reference's fence wait has no limit (src/vulkan.rs:653). */
+int vg_stream_set_wait_limit(vg_stream *stream, uint64_t limit_ns);
 /* How this stream runs a decode step: 1 = one persistent cooperative kernel
  * per token (all layers, grid barriers between phases), 0 = one kernel per
  * projection / attention / norm (the program the reference records,
@@ -319,7 +333,10 @@ int vg_k_attention(const float *q, const uint16_t *k_cache,
  * or more than 1024 heads, returns VG_ERANGE before anything is enqueued.
  * The first call on a device looks the buffer's address up with
  * cudaGetSymbolAddress, which may load the library's device code: make that
- * first call outside any stream capture. There is one buffer per device, so
+ * first call outside any stream capture. The address is kept for the life of
+ * the library; cudaDeviceReset on that device unloads the device code and with
+ * it the buffer, so a caller that resets a device must unload and reload this
+ * library before calling this entry point on that device again. There is one buffer per device, so
  * calls on one device must not overlap: calls on different streams or host
  * threads that can run at the same time race on the scratch and give wrong
  * results. Order them on one stream or synchronise between them. */
@@ -329,6 +346,22 @@ int vg_k_attention_noalloc(const float *q, const uint16_t *k_cache,
                            const uint16_t *v_cache, uint32_t heads,
                            uint32_t kv_heads, uint32_t head_dim, uint32_t ctx,
                            uint32_t position, float *out, void *cuda_stream);
+
+/* ---- failure-detection test hooks (no reference counterpart) -------------- */
+/* One token step (like vg_decode_token without logits) in which every grid-
+ * barrier target is one arrival beyond what the grid provides, so the first
+ * barrier wait runs out after the stream's wait limit (vg_stream_set_wait_limit)
+ * and the kernel leaves with kErrGridWait (0x20) in its device error flag: the
+ * next vg_stream_sync returns VG_EDEVICE. The position advances, the row it
+ * writes holds garbage, and the stream stays usable (the barrier counter is
+ * left aligned). Nothing traps, faults or hangs. Persistent step kernel only. */
+int vg_test_stalled_step(vg_stream *stream, uint32_t token);
+/* Host-side fake of a failing driver call: while `status` is nonzero, every
+ * bounded host wait of the library (vg_stream_sync, output copies, staging
+ * waits) sees cudaEventQuery return `status` (e.g. 702, cudaErrorLaunchTimeout:
+ * "kernel timed out") and fails with VG_ECUDA; 0 restores real queries. The
+ * GPU work itself is not affected. Process-wide. */
+int vg_test_fake_event_status(int status);
 
 #ifdef __cplusplus
 }

@@ -34,7 +34,9 @@ HERE = Path(__file__).resolve().parent
 ORACLE = HERE.parent
 OUT_DIR = ORACLE / "_ref"
 LIB = OUT_DIR / "libvoxgen_ref.so"
-DEFAULT_REFERENCE = Path("/root/reference")
+# The VoxGen checkout: $VOXGEN_REFERENCE, else a directory named "reference" beside this
+# repository's root (the layout the build machine uses).
+DEFAULT_REFERENCE = ORACLE.parent.parent / "reference"
 
 # The normal (non-_xtx7900) shaders that BaseLM's decode step records (baselm.rs:892-1052),
 # and the three ResidualLM adds around the same layers (acoustic.rs:921-966): FSQ's linear

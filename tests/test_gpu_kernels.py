@@ -54,6 +54,34 @@ def test_matvec(dtype, rows, cols):
     assert_close(y.cpu().numpy(), want, what=f"matvec {dtype} {rows}x{cols}")
 
 
+@pytest.mark.parametrize("dtype,rows,cols", [(Q8, 2048, 6144), (Q8, 12288, 2048), (Q8, 1281, 2048),
+                                              (F16, 2048, 6144), (F16, 300, 1024)])
+@pytest.mark.parametrize("zero_column", [False, True])
+def test_matvec_outlier(dtype, rows, cols, zero_column):
+    """x with one element 1000x the rms of the others. The Q8_0 operand shares one power of two
+    over the whole vector, so the outlier sets the digits' resolution for every element. With
+    zero_column the outlier's weight column is zero: the products are then all small and the
+    quantisation error of the small elements is measured against small outputs."""
+    rng = np.random.default_rng(rows * 11 + cols + zero_column)
+    raw = make_matrix(rng, dtype, rows, cols)
+    x = rng.standard_normal(cols).astype(np.float32)
+    k = int(rng.integers(cols))
+    x[k] = 1000.0
+    if zero_column:
+        if dtype == Q8:
+            blocks = raw.view(np.uint8).reshape(rows, cols // 32, 34)
+            blocks[:, k // 32, 2 + k % 32] = 0
+        else:
+            raw.view(np.float16).reshape(rows, cols)[:, k] = 0
+    want = O.matvec(dtype, raw.view(np.uint8), rows, cols, x, 1.0)
+    packed = packed_matrix(dtype, raw, rows, cols)
+    xd = dev(x)
+    y = torch.full((rows,), float("nan"), dtype=torch.float32, device="cuda")
+    check(api.lib().vg_k_matvec(dtype, packed.data_ptr(), rows, cols, xd.data_ptr(), y.data_ptr(), 1.0, None))
+    torch.cuda.synchronize()
+    assert_close(y.cpu().numpy(), want, what=f"matvec {dtype} {rows}x{cols} outlier (zero column {zero_column})")
+
+
 def tile_offsets(rows, cols, q8):
     """Byte offsets of the segmented 16-row tile layout (mirror of TileGeom in kernels.cuh): a
     K-step of 16 rows x 32 bytes is four 8x16-byte matrices [rows 0-7 | rows 8-15] x [bytes 0-15 |

@@ -1,12 +1,10 @@
 """Full decode-step parity of the CUDA engine against the oracle, through the C ABI, on the
 BASELINE configurations (seeded synthetic models) and small edge-case models."""
-from dataclasses import replace
-
 import numpy as np
 import pytest
 
 from conftest import assert_close, spec_path
-from oracle import oracle as O
+from gpu_pair import Pair
 from voxgen_b200 import api, synth
 
 pytestmark = pytest.mark.gpu
@@ -17,57 +15,6 @@ def ctx():
     c = api.Context(0)
     yield c
     c.close()
-
-
-def _ordinal(bits):
-    """fp16 bit patterns mapped to integers that are monotonic in the value."""
-    b = bits.astype(np.int32)
-    return np.where(b & 0x8000, -(b & 0x7FFF), b)
-
-
-class Pair:
-    """The same session on the CUDA engine and on the oracle."""
-
-    def __init__(self, ctx, path, max_context):
-        self.model = api.Model(ctx, path)
-        self.eng = api.BaseLmEngine(self.model, max_context)
-        self.om = O.OracleModel(path)
-        self.ost = O.OracleState(self.om, max_context)
-
-    def write_kv(self, k, v):
-        self.eng.write_kv(k, v)
-        self.ost.write_kv(k, v)
-
-    def step_embedding(self, h, logits=False):
-        self.eng.decode_embedding_gpu_only(h, want_logits=logits)
-        self.ost.decode_embedding(h, want_logits=logits)
-
-    def step_token(self, t, logits=False):
-        self.eng.decode_token_gpu_only(int(t), want_logits=logits)
-        self.ost.decode_token(int(t), want_logits=logits)
-
-    def compare(self, what):
-        assert self.eng.position == self.ost.position
-        assert_close(self.eng.output(), self.ost.output(), what=what)
-
-    def compare_kv(self, n, what):
-        ke, ve = self.eng.read_kv(n)
-        ko, vo = self.ost.read_kv(n)
-        for a, b, name in ((ke, ko, "K"), (ve, vo, "V")):
-            fa = a.view(np.float16).astype(np.float32)
-            fb = b.view(np.float16).astype(np.float32)
-            assert_close(fa, fb, what=f"{what} {name} cache")
-            # Layer 0 projects bit-identical inputs (the embedding lookup is exact), so its
-            # fp16 stores of ordinary-magnitude values are at most one unit in the last place
-            # apart; deeper layers carry accumulated fp32 differences and are held to the
-            # value tolerance above.
-            big = np.abs(fb[0]) >= 1e-2
-            diff = np.abs(_ordinal(a[0]) - _ordinal(b[0]))[big]
-            assert diff.max(initial=0) <= 1, f"{what} {name} layer 0: fp16 values {diff.max()} ulp apart"
-
-    def close(self):
-        self.eng.close()
-        self.model.close()
 
 
 @pytest.mark.parametrize("name", ["tiny", "tiny_f16"])
@@ -184,17 +131,18 @@ def test_cfg0(ctx, model_dir):
 
 
 def test_cfg1_prefill_and_decode(ctx, model_dir):
-    """config[1]: 24 layers, F16 embedding table, token prefill then decode steps."""
+    """config[1]: 24 layers, F16 embedding table, a 128-token prefill then the config's 256
+    decode steps with seeded token ids, every step's final hidden state checked."""
     spec = synth.preset("cfg1")
     p = Pair(ctx, spec_path(model_dir, "cfg1"), 512)
-    toks = synth.token_ids(spec, 128 + 8)
+    toks = synth.token_ids(spec, 128 + 256)
     for t in toks[:128]:
         p.step_token(t)
     p.compare("cfg1 after 128-token prefill")
-    for t in toks[128:]:
+    for i, t in enumerate(toks[128:]):
         p.step_token(t)
-        p.compare("cfg1 decode")
-    p.compare_kv(136, "cfg1")
+        p.compare(f"cfg1 decode step {i}")
+    p.compare_kv(384, "cfg1")
     p.close()
 
 
@@ -218,6 +166,31 @@ def test_backbone_long_context(ctx, model_dir, name):
     with pytest.raises(api.VoxGenError) as e:
         p.eng.decode_embedding_gpu_only(hs[3])
     assert e.value.code == -6
+    p.close()
+
+
+def outlier_hidden(spec, n, seed_index=2500):
+    """N(0,1) hidden states with four "massive activation" channels at +-300 and +-3000 times
+    the rms of the rest, as real MiniCPM-class residual streams carry."""
+    hs = synth.hidden_inputs(spec, n, seed_index=seed_index)
+    ch = np.random.default_rng([spec.seed, seed_index]).choice(spec.hidden, 4, replace=False)
+    hs[:, ch] = np.array([300.0, -300.0, 3000.0, -3000.0], np.float32)
+    return hs
+
+
+@pytest.mark.parametrize("name", ["cfg2", "cfg3"])
+def test_backbone_outlier_channels(ctx, model_dir, name):
+    """config[2]/[3] steps whose input hidden state has outlier channels 300x and 3000x the rms
+    of the others. They stay in the residual stream through every layer, so every RMSNorm
+    operand h*w carries them, and they set the activation's power of two in every matvec
+    prologue while the other elements are 3-4 orders of magnitude smaller."""
+    spec = synth.preset(name)
+    p = Pair(ctx, spec_path(model_dir, name), 2048)
+    k, v = synth.kv_prefill(spec, 1023)
+    p.write_kv(k, v)
+    for i, h in enumerate(outlier_hidden(spec, 3)):
+        p.step_embedding(h)
+        p.compare(f"{name} outlier step {i}")
     p.close()
 
 

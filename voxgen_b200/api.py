@@ -38,7 +38,8 @@ EXPORTS = [
     "vg_stream_profile_step", "vg_decode_batch", "vg_k_packed_bytes", "vg_k_repack", "vg_k_matvec", "vg_k_embedding",
     "vg_k_residual_rmsnorm", "vg_k_attention", "vg_k_attention_noalloc",
     "vg_residual_load_gguf", "vg_residual_step", "vg_residual_step_host", "vg_residual_state",
-    "vg_residual_copy_state",
+    "vg_residual_copy_state", "vg_stream_seek", "vg_stream_set_wait_limit", "vg_test_stalled_step",
+    "vg_test_fake_event_status",
 ]
 
 # which buffer vg_residual_state / vg_residual_copy_state return
@@ -136,6 +137,10 @@ def lib() -> C.CDLL:
         "vg_residual_step_host": ([P, P, P, I], I),
         "vg_residual_state": ([P, I, PP], I),
         "vg_residual_copy_state": ([P, I, P, SZ], I),
+        "vg_stream_seek": ([P, U32], I),
+        "vg_stream_set_wait_limit": ([P, U64], I),
+        "vg_test_stalled_step": ([P, U32], I),
+        "vg_test_fake_event_status": ([I], I),
     }
     for name, (args, res) in sig.items():
         f = getattr(L, name)
@@ -295,6 +300,14 @@ class BaseLmEngine:
 
     def reset(self) -> None:
         self._check(lib().vg_stream_reset(self.h))
+
+    def seek(self, position: int) -> None:
+        """Moves the decode position without touching the KV cache (vg_stream_seek)."""
+        self._check(lib().vg_stream_seek(self.h, int(position)))
+
+    def set_wait_limit(self, seconds: float) -> None:
+        """Limit of every bounded device-side wait of this stream (0: the 2 s default)."""
+        self._check(lib().vg_stream_set_wait_limit(self.h, int(round(seconds * 1e9))))
 
     @property
     def kernel_mode(self) -> int:

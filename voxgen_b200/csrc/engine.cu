@@ -1,17 +1,22 @@
 // C ABI of the B200 BaseLM decode step (include/voxgen_cuda.h).
 //
 // Host side of the hot path: replaces BaseLmEngine (src/baselm.rs:429-1232)
-// and the Vulkan dispatch it records into (src/vulkan.rs). One decode step is
-// one CUDA graph of 5 kernels per layer plus the final norm, all launched with
-// programmatic dependent launch so each kernel's weight stream starts while
-// its predecessor finishes. Position and token live in device memory, so one
-// instantiated graph replays every step.
+// and the Vulkan dispatch it records into (src/vulkan.rs). A decode step is
+// one cooperative launch of the persistent step kernel (step_kernel.cuh: every
+// layer's phases in one launch, grid barriers between them), captured in a
+// CUDA graph per step variant. Position, token and error flags live in a
+// device control block, so one instantiated graph replays every step. Streams
+// whose model the persistent kernel does not take (projections in two weight
+// formats, no cooperative launch, or VOXGEN_STEP_KERNEL=0) run the step as a
+// program of one launch per projection / attention / norm (build_program),
+// chained with programmatic dependent launch and captured the same way.
 #include <cuda_runtime.h>
 #include <sys/mman.h>
 #include <fcntl.h>
 #include <unistd.h>
 
 #include <algorithm>
+#include <atomic>
 #include <chrono>
 #include <cmath>
 #include <cstdarg>
@@ -116,11 +121,17 @@ uint64_t packed_bytes(uint32_t type, uint32_t rows, uint32_t cols) {
   return TileGeom{rows, cols, type == GGML_Q8_0 ? 1u : 0u}.bytes();
 }
 
+// Test hook (vg_test_fake_event_status): when nonzero, host_wait treats every
+// event query as having returned this status, as a driver would report a
+// kernel that timed out (cudaErrorLaunchTimeout); the GPU work is untouched.
+std::atomic<int> g_fake_event_status{0};
+
 // Bounded host wait on an event: spin briefly, then poll with short sleeps.
 int host_wait(cudaEvent_t ev, uint64_t timeout_ns) {
   const auto t0 = std::chrono::steady_clock::now();
   for (uint64_t it = 0;; ++it) {
-    cudaError_t e = cudaEventQuery(ev);
+    const int fake = g_fake_event_status.load(std::memory_order_relaxed);
+    cudaError_t e = fake ? (cudaError_t)fake : cudaEventQuery(ev);
     if (e == cudaSuccess) return VG_OK;
     if (e != cudaErrorNotReady) fail(VG_ECUDA, strf("cudaEventQuery failed: %s", cudaGetErrorString(e)));
     const uint64_t el = (uint64_t)std::chrono::duration_cast<std::chrono::nanoseconds>(
@@ -1284,6 +1295,62 @@ int vg_stream_position(const vg_stream *s, uint32_t *position) {
   if (!live(s)) return VG_ESTATE;
   if (!position) return VG_EINVAL;
   *position = s->pos;
+  return VG_OK;
+}
+
+int vg_stream_seek(vg_stream *s, uint32_t position) {
+  if (!live(s)) return VG_ESTATE;
+  return guard(s->m->ctx, [&] {
+    if (position > s->max_ctx) fail(VG_EINVAL, strf("position %u is beyond the KV cache of %u", position, s->max_ctx));
+    CK(cudaSetDevice(s->m->ctx->device));
+    uint8_t *slot = staging_slot(s);
+    std::memcpy(slot, &position, 4);
+    CK(cudaMemcpyAsync(s->ctrl + kCtrlPos, slot, 4, cudaMemcpyHostToDevice, s->st));
+    CK(cudaEventRecord(staging_event(s), s->st));
+    s->pos = position;
+    return VG_OK;
+  });
+}
+
+int vg_stream_set_wait_limit(vg_stream *s, uint64_t limit_ns) {
+  if (!live(s)) return VG_ESTATE;
+  if (limit_ns > 0xFFFFFFFFull) {
+    set_err(s->m->ctx, "device wait limit above 4294967295 ns");
+    return VG_EINVAL;
+  }
+  return guard(s->m->ctx, [&] {
+    CK(cudaSetDevice(s->m->ctx->device));
+    const uint32_t v = (uint32_t)limit_ns;
+    uint8_t *slot = staging_slot(s);
+    std::memcpy(slot, &v, 4);
+    CK(cudaMemcpyAsync(s->ctrl + kCtrlWaitNs, slot, 4, cudaMemcpyHostToDevice, s->st));
+    CK(cudaEventRecord(staging_event(s), s->st));
+    return VG_OK;
+  });
+}
+
+int vg_test_stalled_step(vg_stream *s, uint32_t token) {
+  if (!live(s)) return VG_ESTATE;
+  return guard(s->m->ctx, [&] {
+    if (!s->use_step) fail(VG_EUNSUPPORTED, "the stalled-barrier test needs the persistent step kernel");
+    if (token >= s->m->cfg.vocab_size)
+      fail(VG_ERANGE, strf("token id %u is outside vocabulary 0..%u", token, s->m->cfg.vocab_size));
+    check_step(s);
+    CK(cudaSetDevice(s->m->ctx->device));
+    uint8_t *slot = staging_slot(s);
+    const uint32_t words[3] = {token, 1u, 0u};  // token, one missing barrier arrival, then its reset
+    std::memcpy(slot, words, sizeof words);
+    CK(cudaMemcpyAsync(s->ctrl + kCtrlToken, slot, 4, cudaMemcpyHostToDevice, s->st));
+    CK(cudaMemcpyAsync(s->ctrl + kCtrlBarExtra, slot + 4, 4, cudaMemcpyHostToDevice, s->st));
+    launch_step(s, true, false);
+    CK(cudaMemcpyAsync(s->ctrl + kCtrlBarExtra, slot + 8, 4, cudaMemcpyHostToDevice, s->st));
+    CK(cudaEventRecord(staging_event(s), s->st));
+    return VG_OK;
+  });
+}
+
+int vg_test_fake_event_status(int status) {
+  g_fake_event_status.store(status, std::memory_order_relaxed);
   return VG_OK;
 }
 

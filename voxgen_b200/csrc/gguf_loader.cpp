@@ -25,15 +25,6 @@ static std::string fmt(const char *f, ...) {
 }
 
 [[noreturn]] static void fail(int code, const std::string &msg) { throw Error{code, msg}; }
-static std::string strf(const char *f, ...) __attribute__((format(printf, 1, 2)));
-static std::string strf(const char *f, ...) {
-  char buf[512];
-  va_list ap;
-  va_start(ap, f);
-  vsnprintf(buf, sizeof buf, f, ap);
-  va_end(ap);
-  return buf;
-}
 
 const TensorInfo *GgufSummary::find(const std::string &name) const {
   for (const auto &t : tensors)
@@ -456,9 +447,9 @@ AcousticConfig acoustic_from_gguf(const GgufSummary &s, const BaseLmConfig &base
   if (a.residual_block_count == 0 || a.fsq_latent_dim == 0)
     fail(VG_EINVAL, "acoustic GGUF declares an empty ResidualLM or FSQ latent");
   if (a.embedding_length != base.embedding_length)  // src/acoustic.rs:92-99
-    fail(VG_EINVAL, strf("BaseLM geometry is incompatible with ResidualLM: n_embd %u vs BaseLM %u",
+    fail(VG_EINVAL, fmt("BaseLM geometry is incompatible with ResidualLM: n_embd %u vs BaseLM %u",
                          a.embedding_length, base.embedding_length));
-  if (!std::isfinite(a.fsq_scale) || a.fsq_scale <= 0.0f) fail(VG_EINVAL, strf("invalid FSQ scale %g", a.fsq_scale));
+  if (!std::isfinite(a.fsq_scale) || a.fsq_scale <= 0.0f) fail(VG_EINVAL, fmt("invalid FSQ scale %g", a.fsq_scale));
   for (const auto &t : s.tensors)  // validate_acoustic_f16, src/gguf.rs:150-160
     if (t.type != GGML_F32 && t.type != GGML_F16)
       fail(VG_EUNSUPPORTED, "unsupported acoustic tensor type in " + t.name + "; the F16 acoustic GGUF is required");
@@ -471,12 +462,12 @@ AcousticConfig acoustic_from_gguf(const GgufSummary &s, const BaseLmConfig &base
   auto matrix = [&](const std::string &name, uint32_t cols, uint32_t rows) {  // require_matrix, :189-205
     const TensorInfo &t = need(name);
     if (t.dims.size() != 2 || t.dims[0] != cols || t.dims[1] != rows)
-      fail(VG_EINVAL, strf("tensor %s does not have dimensions [%u, %u]", name.c_str(), cols, rows));
+      fail(VG_EINVAL, fmt("tensor %s does not have dimensions [%u, %u]", name.c_str(), cols, rows));
     if (t.type != GGML_F16) fail(VG_EUNSUPPORTED, "tensor " + name + " must be F16");
   };
   auto vector = [&](const std::string &name, uint32_t n, bool f32_only, bool allow_f32) {  // require_vector, :207-216
     const TensorInfo &t = need(name);
-    if (t.dims.size() != 1 || t.dims[0] != n) fail(VG_EINVAL, strf("tensor %s does not have dimensions [%u]", name.c_str(), n));
+    if (t.dims.size() != 1 || t.dims[0] != n) fail(VG_EINVAL, fmt("tensor %s does not have dimensions [%u]", name.c_str(), n));
     if (f32_only ? t.type != GGML_F32 : !(t.type == GGML_F16 || (allow_f32 && t.type == GGML_F32)))
       fail(VG_EUNSUPPORTED, "tensor " + name + " has an unsupported type");
   };
@@ -488,7 +479,7 @@ AcousticConfig acoustic_from_gguf(const GgufSummary &s, const BaseLmConfig &base
   vector("projections.res_fusion_proj.bias", H, false, false);
   vector("residual_lm.output_norm.weight", H, true, true);
   for (uint32_t l = 0; l < a.residual_block_count; ++l) {
-    auto p = [&](const char *sfx) { return strf("residual_lm.blk.%u.%s", l, sfx); };
+    auto p = [&](const char *sfx) { return fmt("residual_lm.blk.%u.%s", l, sfx); };
     vector(p("attn_norm.weight"), H, true, true);
     vector(p("ffn_norm.weight"), H, true, true);
     matrix(p("attn_q.weight"), H, base.head_count * base.head_dim);

@@ -1,26 +1,28 @@
-// CUDA kernels of the BaseLM decode step (sm_100a).
+// CUDA kernels of the BaseLM decode step (sm_100a): the shared matvec parts
+// (producer, activation prologue, tensor-core consumer, epilogues) used by the
+// persistent step kernel (step_kernel.cuh) and by the standalone kernels of
+// the vg_k_* entry points and the per-kernel step program.
 //
-// Weight layout in HBM ("segmented 8-row tiles", built by repack_kernel).
-// Every matrix is cut into tiles of 8 rows, and each tile into K-segments of
-// 16 K-steps; a K-step is 32 int8 quants (Q8_0: exactly one block) or 16 fp16
-// values, i.e. 8 rows x 32 bytes. A K-step is stored as two 128-byte 8x16-byte
-// matrices (bytes 0-15 and 16-31 of the 8 rows), which is the order ldmatrix
-// reads, so the tensor-core B operand loads are bank-conflict free. A Q8_0
-// segment ends with the 16 x 8 fp16 block scales. One segment (4352 B Q8_0,
-// 4096 B F16) is the unit the TMA engine streams into a shared-memory ring
-// slot with one cp.async.bulk.
+// Weight layout in HBM ("segmented 16-row tiles", built by repack_kernel; see
+// TileGeom). A tile is 16 output rows, the M of one mma.sync with the weights
+// as the A operand. A K-step is 32 Q8_0 quants (one block) or 16 fp16 values
+// of the 16 rows, 512 bytes stored as the four 8x16-byte matrices that
+// ldmatrix.x4 delivers as the A fragment. A segment is 8 K-steps followed
+// (Q8_0) by their fp16 block scales; a tile is its segments back to back and
+// tiles follow each other, so a CTA's run of tiles is one contiguous range
+// that the TMA engine streams into a shared-memory ring with cp.async.bulk.
 //
 // Row orders are permuted at load time so that fused epilogues find both
-// operands in one lane: rows 2j and 2j+1 of a tile are (i, i + head_dim/2) for
-// the Q and K projections (RoPE pairs) and (gate r, up r) for the FFN.
+// operands of a pair in one lane: rows l and l + 8 of a tile hold RoPE
+// elements (i, i + head_dim/2) of Q and K, and (gate r, up r) of the FFN.
 //
-// Activations enter the tensor cores exactly: for Q8_0, x is split per
-// 32-element block into three int8 digits with a power-of-two block scale,
-//   x = 2^e (d0 + d1 2^-7 + d2 2^-14),  |d_i| <= 64,
-// so each K-step is an exact int32 mma (m16n8k32, digits as the A rows, the 8
-// weight rows as B) that is then scaled by the fp16 block scale and 2^e in
-// fp32. For F16 weights x is scaled by a power of two and split into fp16
-// hi + lo, accumulated in fp32 by m16n8k16.
+// Activations enter the tensor cores exactly. Q8_0: the input vector is
+// scaled by one power of two 2^e for the whole vector (max|x| 2^-e in
+// [32, 64)) and written as three int8 digits, x = 2^e (d0 + d1 2^-7 + d2
+// 2^-14), the B columns of an exact s8 MMA (m16n8k32) whose int32 sums are
+// rescaled in fp32 by the fp16 block scale of each K-step. F16: x 2^-e is
+// split into fp16 hi + lo, two B columns of an f16 MMA (m16n8k16) with fp32
+// accumulation.
 #pragma once
 #include <type_traits>
 #include <cuda_fp16.h>
@@ -51,7 +53,12 @@ static_assert(kChunkSteps == 4 && kSegSteps % kChunkSteps == 0,
 constexpr uint32_t kCtrlPos = 0;    // decode position of the step being run
 constexpr uint32_t kCtrlToken = 1;  // token id of a token step
 constexpr uint32_t kCtrlErr = 2;    // error flag bits (ptx.cuh)
+constexpr uint32_t kCtrlWaitNs = 3; // limit of every bounded device wait in ns (0: kWaitLimitNs); read
+                                    // through the error word by wait_limit (ptx.cuh), so it follows it
+constexpr uint32_t kCtrlBarExtra = 4;  // arrivals added to every grid-barrier target of the next step
+                                       // (0 in service; a test sets 1 to make a barrier wait run out)
 constexpr uint32_t kCtrlWords = 16;
+static_assert(kCtrlWaitNs == kCtrlErr + 1, "wait_limit reads the limit from the word after the error word");
 
 // Segmented 16-row tiles. A K-step is 32 columns of Q8_0 quants or 16 columns
 // of fp16 values of the tile's 16 rows: 512 bytes stored as four 8x16-byte

@@ -4,6 +4,11 @@
 // Every wait here is bounded: it gives up after a wall-clock limit read from
 // %globaltimer (and an iteration cap as a backstop) and returns false, so a
 // kernel can record an error in its device flag and leave instead of hanging.
+//
+// A wait may be given the error word of a control block as its abort flag: it
+// then gives up as soon as that word is nonzero, and the word after it holds
+// the wall-clock limit in nanoseconds (0 = kWaitLimitNs), so a host can
+// shorten every wait of a stream at run time.
 #pragma once
 #include <cstdint>
 
@@ -69,16 +74,24 @@ __device__ __forceinline__ uint32_t ld_volatile_u32(const uint32_t *p) {
   return v;
 }
 
+// Wall-clock limit of a wait whose abort flag is a control block's error word
+// (the limit is the next word; 0 or no flag: kWaitLimitNs). Read once, when a
+// wait first fails its fast check.
+__device__ __forceinline__ uint64_t wait_limit(const uint32_t *abort_flag) {
+  const uint32_t ns = abort_flag ? ld_volatile_u32(abort_flag + 1) : 0u;
+  return ns ? (uint64_t)ns : kWaitLimitNs;
+}
+
 // Waits for the phase with the given parity to complete; false on timeout, or
 // as soon as *abort_flag (when given) is nonzero.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity,
                                                   const uint32_t *abort_flag = nullptr) {
   if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer();
+  const uint64_t t0 = globaltimer(), lim = wait_limit(abort_flag);
   for (uint32_t it = 0; it < kWaitMaxIters; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 255u) == 255u) {
-      if (globaltimer() - t0 > kWaitLimitNs) return false;
+      if (globaltimer() - t0 > lim) return false;
       if (abort_flag && ld_volatile_u32(abort_flag)) return false;
     }
   }
@@ -91,12 +104,12 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
 __device__ __forceinline__ bool mbar_wait_backoff(uint64_t *bar, uint32_t parity,
                                                   const uint32_t *abort_flag = nullptr) {
   if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer();
+  const uint64_t t0 = globaltimer(), lim = wait_limit(abort_flag);
   for (uint32_t it = 0; it < kWaitMaxIters; ++it) {
     __nanosleep(128);
     if (mbar_try_wait(bar, parity)) return true;
     if ((it & 15u) == 15u) {
-      if (globaltimer() - t0 > kWaitLimitNs) return false;
+      if (globaltimer() - t0 > lim) return false;
       if (abort_flag && ld_volatile_u32(abort_flag)) return false;
     }
   }
@@ -119,11 +132,11 @@ __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long
 __device__ __forceinline__ bool grid_wait(const unsigned long long *ctr, unsigned long long target,
                                           const uint32_t *abort_flag) {
   if (ld_acquire_u64(ctr) >= target) return true;
-  const uint64_t t0 = globaltimer();
+  const uint64_t t0 = globaltimer(), lim = wait_limit(abort_flag);
   for (uint32_t it = 0; it < kWaitMaxIters; ++it) {
     if (ld_acquire_u64(ctr) >= target) return true;
     if ((it & 63u) == 63u) {
-      if (globaltimer() - t0 > kWaitLimitNs) return false;
+      if (globaltimer() - t0 > lim) return false;
       if (abort_flag && ld_volatile_u32(abort_flag)) return false;
     }
   }

@@ -344,9 +344,12 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_step_kernel(const __grid
     // Every CTA arrives exactly nb times per step, so at a step's start the
     // counter is base + (arrivals of this step so far) with base a multiple of
     // nb * gridDim.x and fewer than nb * gridDim.x arrivals counted.
+    // A nonzero kCtrlBarExtra raises every barrier target of this step beyond
+    // what the grid provides, so the first wait runs out (the failure test);
+    // every CTA still arrives nb times, which keeps the counter aligned.
     const unsigned long long c = ld_acquire_u64(p.bar);
     const unsigned long long unit = (unsigned long long)nb * gridDim.x;
-    *sbase = c - c % unit;
+    *sbase = c - c % unit + p.ctrl[kCtrlBarExtra];
   }
   for (uint32_t i = threadIdx.x; i < p.n_layers * (uint32_t)sizeof(StepLayer) / 8u; i += blockDim.x)
     reinterpret_cast<unsigned long long *>(layers)[i] = reinterpret_cast<const unsigned long long *>(p.layers)[i];

@@ -51,6 +51,12 @@ class ModelSpec:
     tied_output: bool = True
     rope_scaling: str = "longrope"
     alignment: int = 32
+    # per-matrix formats that differ from `fmt`: pairs (tensor suffix, format), for example
+    # (("ffn_down", GGML_F16),) for a model whose projections do not share one format
+    fmt_overrides: Tuple[Tuple[str, int], ...] = ()
+
+    def fmt_of(self, suffix: str) -> int:
+        return dict(self.fmt_overrides).get(suffix, self.fmt)
 
     @property
     def kv_dim(self) -> int:
@@ -73,6 +79,11 @@ PRESETS: Dict[str, ModelSpec] = {
     "pin": ModelSpec("pin", 2, 256, 2, 1, 128, 512, 96, GGML_Q8_0, seed=31),
     "pin_f16": ModelSpec("pin_f16", 2, 256, 2, 1, 128, 512, 96, GGML_F16, seed=32, tied_output=False,
                          embedding_scale=12.0, residual_scale=0.25, logit_scale=0.125),
+    # projections in two formats (a Q8_0 model whose down projections are F16, which
+    # validate_baselm accepts, src/gguf.rs:135-148): a model the persistent step kernel does not
+    # take, so it runs the per-kernel program
+    "tiny_mixed": ModelSpec("tiny_mixed", 2, 256, 8, 2, 32, 608, 512, GGML_Q8_0, embd_fmt=GGML_Q8_0,
+                            seed=13, fmt_overrides=(("ffn_down", GGML_F16),)),
 }
 
 # Runtime inputs per config (BASELINE.json configs and the survey's measurement plan).
@@ -162,14 +173,15 @@ def build_gguf(spec: ModelSpec) -> Tuple[GgufFile, List[Tuple[str, Tuple[int, ..
         base = 16 + 16 * layer
         p = f"blk.{layer}."
         add(p + "attn_norm.weight", (H,), GGML_F32, vec(H, base + 0))
-        add(p + "attn_q.weight", (H, H), spec.fmt, _matrix(spec, spec.fmt, H, H, base + 1))
-        add(p + "attn_k.weight", (H, KV), spec.fmt, _matrix(spec, spec.fmt, KV, H, base + 2))
-        add(p + "attn_v.weight", (H, KV), spec.fmt, _matrix(spec, spec.fmt, KV, H, base + 3))
-        add(p + "attn_output.weight", (H, H), spec.fmt, _matrix(spec, spec.fmt, H, H, base + 4))
+        fq, fo, fg, fd = (spec.fmt_of(n) for n in ("attn_qkv", "attn_output", "ffn_gate_up", "ffn_down"))
+        add(p + "attn_q.weight", (H, H), fq, _matrix(spec, fq, H, H, base + 1))
+        add(p + "attn_k.weight", (H, KV), fq, _matrix(spec, fq, KV, H, base + 2))
+        add(p + "attn_v.weight", (H, KV), fq, _matrix(spec, fq, KV, H, base + 3))
+        add(p + "attn_output.weight", (H, H), fo, _matrix(spec, fo, H, H, base + 4))
         add(p + "ffn_norm.weight", (H,), GGML_F32, vec(H, base + 5))
-        add(p + "ffn_gate.weight", (H, F), spec.fmt, _matrix(spec, spec.fmt, F, H, base + 6))
-        add(p + "ffn_up.weight", (H, F), spec.fmt, _matrix(spec, spec.fmt, F, H, base + 7))
-        add(p + "ffn_down.weight", (F, H), spec.fmt, _matrix(spec, spec.fmt, H, F, base + 8))
+        add(p + "ffn_gate.weight", (H, F), fg, _matrix(spec, fg, F, H, base + 6))
+        add(p + "ffn_up.weight", (H, F), fg, _matrix(spec, fg, F, H, base + 7))
+        add(p + "ffn_down.weight", (F, H), fd, _matrix(spec, fd, H, F, base + 8))
     return g, plan
 
 
