@@ -110,13 +110,13 @@ def ensure_model(spec, rank, world, pg_barrier):
     return p
 
 
-def launch_traffic(workload):
-    """DRAM bytes of one step-kernel launch of this workload from an ncu capture
+def launch_traffic(workload, kernel="decode_step_kernel"):
+    """DRAM bytes of one launch of `kernel` on this workload from an ncu capture
     (profiles/traffic.json), or None."""
     tr = ROOT / "profiles" / "traffic.json"
     if not tr.exists():
         return None
-    return json.loads(tr.read_text()).get(workload, {}).get("decode_step_kernel")
+    return json.loads(tr.read_text()).get(workload, {}).get(kernel)
 
 
 def measured_peaks():
@@ -453,6 +453,7 @@ def run_batch(args, rank, world, local):
     ctx = api.Context(local)
     model = api.Model(ctx, path)
     info = model.info
+    batched = model.batch_columns >= S
     engs = [api.BaseLmEngine(model, max_ctx) for _ in range(S)]
     kpre, vpre = synth.kv_prefill(spec, int(lens.max()))
 
@@ -500,14 +501,23 @@ def run_batch(args, rank, world, local):
     peak, peak_kind = measured_peaks()
     kv = info["block_count"] * info["kv_dim"] * 2 * 2
     wbytes = info["layer_weight_bytes"] + info["norm_weight_bytes"]
+    emb = S * info["embedding_length"] * 2                                   # the S token-table rows
     kv_step = sum(kv * (p + j + 1) + kv for p in p0 for j in range(K)) / K   # all streams, per step
     step_ms = ms_max / K
-    # per launch of the step kernel (one stream's token): its weights and that stream's KV
-    launch_bytes = wbytes + kv_step / S
-    launch_ach = launch_bytes * S / (step_ms * 1e-3) / 1e9
     # per batched step, counting the weights once (the roofline of a shared weight pass)
-    batch_bytes = wbytes + kv_step
+    batch_bytes = wbytes + kv_step + emb
     batch_ach = batch_bytes / (step_ms * 1e-3) / 1e9
+    if batched:
+        # one launch per step reads the weights once and every stream's KV
+        launch_bytes, launch_ach, launches = batch_bytes, batch_ach, K
+        kname = (f"decode_batch_kernel (one launch per step for all {S} streams, every weight byte read once; "
+                 f"split-K over CTAs, fp16 hi+lo operand, f16 mma.sync)")
+    else:
+        # per launch of the step kernel (one stream's token): its weights and that stream's KV
+        launch_bytes = wbytes + kv_step / S
+        launch_ach = launch_bytes * S / (step_ms * 1e-3) / 1e9
+        launches = K * S
+        kname = "decode_step_kernel (one launch per stream token; the weight pass is not shared between streams)"
     line = {
         "metric": "decode tok/s", "value": round(replicas.aggregate_rate(K * S, world, ms_max), 2),
         "unit": "tok/s", "n_gpus": world, "steps": K, "warmup": W, "ms_per_step": round(step_ms, 5),
@@ -519,19 +529,18 @@ def run_batch(args, rank, world, local):
             "l2": f"inputs larger than L2: {info['layer_weight_bytes'] / 1e9:.2f} GB of weights per stream token",
             "input": "seeded token ids",
         },
-        "roofline": {"kernel": "decode_step_kernel (one launch per stream token; the weight pass is not "
-                               "shared between streams)", "bound": "hbm", "achieved": round(launch_ach, 1),
+        "roofline": {"kernel": kname, "bound": "hbm", "achieved": round(launch_ach, 1),
                      "peak": peak, "unit": "GB/s", "frac": round(launch_ach / peak, 4),
-                     "traffic": launch_traffic(args.workload),
+                     "traffic": launch_traffic(args.workload, "decode_batch_kernel" if batched else "decode_step_kernel"),
                      "bytes_per_launch": int(launch_bytes),
-                     "avg_launch_ms": round(step_ms / S, 5), "peak_source": f"{peak_kind} hbm_gbs"},
+                     "avg_launch_ms": round(step_ms * K / launches, 5), "peak_source": f"{peak_kind} hbm_gbs"},
         "batch_roofline": {"bytes_per_step": int(batch_bytes), "achieved": round(batch_ach, 1), "peak": peak,
                            "unit": "GB/s", "frac": round(batch_ach / peak, 4),
                            "note": "weights counted once per batched step"},
         "e2e": {"value": round(replicas.aggregate_rate(KE * S, world, e_ms_max), 2), "unit": "tok/s",
                 "steps": KE, "h2d_bytes_per_step": 4 * S,
                 "d2h_bytes_per_step": S * info["embedding_length"] * 4},
-        "gpu_launches": K * S,
+        "gpu_launches": launches,
         "clocks": clk,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

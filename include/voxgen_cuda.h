@@ -233,8 +233,15 @@ int vg_residual_step_host(vg_stream *stream, const float *base_hidden, const flo
 int vg_residual_state(const vg_stream *stream, int which, const float **device_buffer);
 /* Host copy of n <= H floats of one of those buffers, after the stream's work. */
 int vg_residual_copy_state(vg_stream *stream, int which, float *host, size_t n);
-/* prefill_tokens (src/baselm.rs:823-839): n decode_token steps, logits on the
- * last one only when want_logits_last is set. */
+/* prefill_tokens (src/baselm.rs:823-839): the n tokens at positions
+ * position..position+n-1, then position += n; logits of the last position
+ * only when want_logits_last is set. Results are those of n decode_token
+ * steps. With the persistent step kernel, runs of up to 16 positions go
+ * through the batched step kernel, one weight pass per run (the reference
+ * records 16 or 32 positions per command buffer, src/runtime.rs:490-522,
+ * and still reads the weights once per position); the LM head then runs once,
+ * on the last position. Every token and the cache room are checked before
+ * anything is enqueued. */
 int vg_prefill_tokens(vg_stream *stream, const uint32_t *tokens, uint32_t n,
                       int want_logits_last);
 
@@ -279,11 +286,22 @@ int vg_stream_profile_step(vg_stream *stream, uint32_t token, int want_logits,
 /* One decode step (decode_token_gpu_only semantics, no logits) for n distinct
  * streams of the same model: tokens[i] feeds streams[i] and each stream
  * advances by one position. n <= 16. Every argument is checked before any
- * stream is advanced. The steps are enqueued on the streams' own CUDA streams
- * (asynchronous, like vg_decode_token); each reads the weights once, i.e. the
- * weight pass is not yet shared between streams. The reference serialises
- * independent engines behind a Mutex (src/runtime.rs:177). */
+ * stream is advanced. With n >= 2 streams on the persistent step kernel, the
+ * step is one launch of the batched step kernel, which reads every weight byte
+ * once for all n streams (each stream attends over its own cache, at its own
+ * position); it is ordered after the work already enqueued on every stream and
+ * before their later work, and runs on a CUDA stream of the model (launches
+ * of one model are serialised). Otherwise each stream takes its own step on
+ * its own CUDA stream. Asynchronous, like vg_decode_token. The reference
+ * serialises independent engines behind a Mutex (src/runtime.rs:177). */
 int vg_decode_batch(vg_stream *const *streams, int n, const uint32_t *tokens);
+/* 16 when vg_decode_batch and vg_prefill_tokens can use the batched step
+ * kernel for this model (one weight format for every projection, cooperative
+ * launch, head_dim 32-256, at most 8 KV heads, query width = hidden width,
+ * VOXGEN_BATCH_KERNEL not 0), else 0 with the reason in vg_last_error. The
+ * first call plans the kernel and allocates its workspace (about 70 MB at the
+ * BaseLM backbone's shape with a 32768-position context). */
+int vg_model_batch_columns(vg_model *model, uint32_t *max_columns);
 
 /* ---- kernel-level entry points (parity tests and integration) ----------- */
 /* These run one kernel on raw device pointers on the given cudaStream_t

@@ -212,11 +212,14 @@ def test_attention_merge_long_context(ctx, model_dir, name):
     p.close()
 
 
-def test_decode_batch_matches_single_streams(ctx, model_dir):
-    """vg_decode_batch: every stream advances as if decoded alone (ragged positions)."""
+def test_decode_batch_matches_single_streams(ctx, model_dir, monkeypatch):
+    """vg_decode_batch without the batched kernel (VOXGEN_BATCH_KERNEL=0): each stream takes its
+    own step, bitwise the same as a stream decoded alone (ragged positions)."""
+    monkeypatch.setenv("VOXGEN_BATCH_KERNEL", "0")
     spec = synth.preset("tiny")
     path = spec_path(model_dir, "tiny")
     m = api.Model(ctx, path)
+    assert m.batch_columns == 0
     engines = [api.BaseLmEngine(m, 64) for _ in range(3)]
     solo = [api.BaseLmEngine(m, 64) for _ in range(3)]
     for i, (e, s) in enumerate(zip(engines, solo)):

@@ -39,7 +39,7 @@ EXPORTS = [
     "vg_k_residual_rmsnorm", "vg_k_attention", "vg_k_attention_noalloc",
     "vg_residual_load_gguf", "vg_residual_step", "vg_residual_step_host", "vg_residual_state",
     "vg_residual_copy_state", "vg_stream_seek", "vg_stream_set_wait_limit", "vg_test_stalled_step",
-    "vg_test_fake_event_status",
+    "vg_test_fake_event_status", "vg_model_batch_columns",
 ]
 
 # which buffer vg_residual_state / vg_residual_copy_state return
@@ -141,6 +141,7 @@ def lib() -> C.CDLL:
         "vg_stream_set_wait_limit": ([P, U64], I),
         "vg_test_stalled_step": ([P, U32], I),
         "vg_test_fake_event_status": ([I], I),
+        "vg_model_batch_columns": ([P, C.POINTER(U32)], I),
     }
     for name, (args, res) in sig.items():
         f = getattr(L, name)
@@ -225,6 +226,13 @@ class Model:
         ctx.check(lib().vg_model_info_get(h, C.byref(info)))
         self.info = info.as_dict()
         self.path = Path(path)
+
+    @property
+    def batch_columns(self) -> int:
+        """Columns of the batched step kernel for this model (16), or 0 when it is unavailable."""
+        n = C.c_uint32()
+        self.ctx.check(lib().vg_model_batch_columns(self.h, C.byref(n)))
+        return n.value
 
     def close(self) -> None:
         if getattr(self, "h", None):

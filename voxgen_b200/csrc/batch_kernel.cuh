@@ -1,0 +1,1019 @@
+// The batched decode-step kernel: one persistent launch advances up to 16
+// "columns" by one token each and reads every weight byte once for all of
+// them. A column is a decode position of a stream: one position each of up to
+// 16 independent streams (vg_decode_batch), or up to 16
+// consecutive positions of one stream (vg_prefill_tokens). The layer sequence
+// is record_transformer's (src/baselm.rs:892-1052), as in the single-stream
+// step kernel (step_kernel.cuh), whose grid barriers, producer warp and ring
+// this kernel shares.
+//
+// Matvec phases are split over the grid in two dimensions. For each matrix
+// kind the host picks C column groups and R = grid / C row groups; CTA
+// (r, c) owns the tiles of row group r and the segments of column group c.
+// It builds the operand of its K-slice only (S columns x Kc elements), so the
+// activation that every CTA would otherwise read whole from L2 is read once
+// per row group, and it writes fp32 partial sums for its tiles. After the C
+// CTAs of a row group have arrived on their counter, each reduces a share of
+// the group's tiles in a fixed order and runs the epilogue (RoPE + fp16 KV
+// store, residual add, SwiGLU) for every column.
+//
+// Operand: each column's slice is scaled by a power of two 2^-e (max below
+// 2^14) and split into fp16 hi + lo, so every element keeps 22 significant
+// bits whatever the other elements' magnitudes. The weights are the A operand
+// of mma.sync m16n8k16 (f16, fp32 accumulation): F16 tiles as stored, Q8_0
+// quants converted to fp16 in registers (exact for |q| <= 128). The 16
+// columns are two n8 tiles; hi and lo accumulate into one accumulator, and a
+// Q8_0 K-step's sum is scaled by the fp16 block scale of each row in fp32.
+//
+// Attention runs per column: split-K units (column, KV head, 64 positions)
+// over the column's own cache, then one merge slice per (column, query head).
+// Rows a column reads that this same launch writes (the column's own row, and
+// for a prefill run the rows of the earlier columns) are loaded from L2 after
+// the barrier; older rows stream through the ring.
+#pragma once
+#include "step_kernel.cuh"
+
+namespace vg {
+
+constexpr uint32_t kBatchMaxCols = 16;
+constexpr uint32_t kBatchMaxRowGroups = 148;
+constexpr uint32_t kBatchKinds = 4;  // matvec kinds: QKV, o_proj, gate/up, down
+
+// One column of a batched step. The position is ctrl[kCtrlPos] + off; rows at
+// or above ctrl[kCtrlPos] of the column's cache are written by this launch.
+struct BatchCol {
+  __half *kc, *vc;                 // layer-0 K and V caches of the stream, [kv_head][ctx][head_dim]
+  unsigned long long layer_elems;  // elements from one layer's cache to the next
+  uint32_t *ctrl;                  // the stream's control block (position; error flag)
+  float *out;                      // the stream's final hidden state (written by its last column)
+  uint32_t ctx;                    // the stream's cache capacity in positions
+  uint32_t off;                    // position of the column within its stream's run
+  uint32_t adv;                    // last column of a stream: the run length (position advance); else 0
+  uint32_t token;                  // input token id
+};
+
+// Split of one matvec kind over the grid: C column groups x R row groups.
+struct BatchSplit {
+  uint32_t C, R;
+};
+
+struct BatchParams {
+  const StepLayer *layers;  // [n_layers] (kc/vc unused: caches come from the columns)
+  uint32_t n_layers;
+  TileGeom g[kBatchKinds];  // QKV, o_proj, gate/up, down
+  BatchSplit split[kBatchKinds];
+  TileGeom g_tok;
+  const uint8_t *tok;       // token table (segmented tiles)
+  const float *out_norm;
+  const BatchCol *cols;     // [S]
+  uint32_t S;
+  float *hid_a, *hid_b, *q, *attn;  // [S][H]
+  float *gate;                      // [S][F]
+  float *part;              // matvec partials [C][part_tiles][16 rows][16 columns]
+  uint32_t part_tiles;
+  float *ssb;               // partial sums of squares [R][C][16]
+  float *apart;             // attention partials [S][kv_heads][max_chunks][G][head_dim]
+  float2 *apart_ml;         // their (max, sum) [S][kv_heads][max_chunks][G]
+  unsigned long long *ready;  // [S][kv_heads] unit arrivals, monotonic
+  unsigned long long *rgc;    // [kBatchKinds][kBatchMaxRowGroups] row-group arrivals, monotonic
+  unsigned long long *bar;    // grid-barrier arrivals
+  uint32_t *ctrl;             // the launch's control block (error flag, wait limit)
+  const float *inv_freq, *ext;
+  float rope_scaling, eps, res_scale, emb_scale, attn_scale;
+  uint32_t H, F, heads, kv_heads, head_dim;
+  uint32_t chunk, max_chunks;  // attention positions per unit; partial slots per (column, KV head)
+  // shared-memory plan (BatchSmem)
+  uint32_t nst, slot, aux_bytes;
+};
+
+// Shared memory of a batched-step CTA: the ring and its barriers, two staging
+// barriers, the aux region (matvec operand planes + staged input + norm
+// weight + per-column scalars, or the attention scratch), a small scratch
+// (unit-arrival bases) and the layer table.
+struct BatchSmem {
+  uint32_t ring, bars, sbar, aux, scr, layers, total;
+  __host__ __device__ BatchSmem(const BatchParams &p) {
+    ring = 0;
+    bars = ring + p.nst * p.slot;
+    sbar = bars + p.nst * 16u;
+    aux = (sbar + 16u + 127u) & ~127u;
+    scr = aux + ((p.aux_bytes + 127u) & ~127u);
+    layers = scr + 4096u;
+    total = layers + p.n_layers * (uint32_t)sizeof(StepLayer);
+  }
+};
+
+// Matvec operand region of the aux area for a K-slice of kc elements:
+// hi plane, lo plane (each 16 columns x kc fp16), the staged fp32 input
+// [16][kc], the staged norm weight [kc], then per column 2^e and the sum of
+// squares of the slice.
+struct BatchOperand {
+  uint32_t hi, lo, stg, stw, colv, total;
+  __host__ __device__ BatchOperand(uint32_t kc) {
+    hi = 0;
+    lo = hi + kc * kBatchMaxCols * 2u;
+    stg = lo + kc * kBatchMaxCols * 2u;
+    stw = stg + kc * kBatchMaxCols * 4u;
+    colv = stw + kc * 4u;
+    total = colv + 2u * kBatchMaxCols * 4u;
+  }
+};
+
+// Byte offset, inside a plane, of operand element k (0 <= k < kc) of column n.
+// Q8_0 (K-steps of 32): lane tq of an MMA reads, for K-step kk and column n,
+// 16 bytes holding elements 4tq..4tq+3 and 16+4tq..16+4tq+3 (the B fragments
+// of the two k16 MMAs of the K-step, in the k order the int8 A fragment
+// converts to). F16 (K-steps of 16): 8 bytes holding 2tq, 2tq+1, 8+2tq, 9+2tq.
+__host__ __device__ inline uint32_t batch_bfrag_off(bool q8, uint32_t k, uint32_t n) {
+  if (q8) {
+    const uint32_t kk = k >> 5, w = k & 31u;
+    return ((kk * kBatchMaxCols + n) * 4u + ((w & 15u) >> 2)) * 16u + (w >> 4) * 8u + (w & 3u) * 2u;
+  }
+  const uint32_t kk = k >> 4, w = k & 15u;
+  return ((kk * kBatchMaxCols + n) * 4u + ((w & 7u) >> 1)) * 8u + (w >> 3) * 4u + (w & 1u) * 2u;
+}
+
+// int8x4 -> two fp16x2 (elements 0,1 and 2,3), exactly: (q ^ 0x80) is q + 128,
+// and the fp16 with bits 0x6400 | u is 1024 + u, so subtracting 1152 gives q.
+__device__ __forceinline__ void i8x4_to_h2x2(uint32_t a, uint32_t &lo, uint32_t &hi) {
+  const uint32_t x = a ^ 0x80808080u;
+  const uint32_t l = __byte_perm(x, 0x64646464u, 0x4140u), h = __byte_perm(x, 0x64646464u, 0x4342u);
+  const __half2 bias = __halves2half2(__ushort_as_half(0x6480u), __ushort_as_half(0x6480u));  // 1152
+  const __half2 rl = __hsub2(*reinterpret_cast<const __half2 *>(&l), bias);
+  const __half2 rh = __hsub2(*reinterpret_cast<const __half2 *>(&h), bias);
+  lo = *reinterpret_cast<const uint32_t *>(&rl);
+  hi = *reinterpret_cast<const uint32_t *>(&rh);
+}
+
+// D = A * B + 0 (f16, fp32 accumulation): the first MMA of a block sum.
+__device__ __forceinline__ void mma_f16_zero(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%10, %10, %10, %10};"
+      : "=f"(c[0]), "=f"(c[1]), "=f"(c[2]), "=f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(0.0f));
+}
+
+// Activation operand of a batched matvec over the K-slice [k0, k0 + kc) of
+// an input of `ld` floats per column: the consumer warps (256 threads) take
+// one column per half-warp. The input slice of every column is in stg (fp32
+// [16][kc]) and, with rms, the norm weight slice in stw. With rms the operand
+// is x * w (RMSNorm deferred to the output rows) and the slice's sum of
+// squares of x goes to colv[16 + n]; colv[n] receives 2^e. Columns >= S are
+// zero.
+template <bool Q8>
+__device__ __forceinline__ void batch_activation(const BatchOperand &O, uint8_t *aux, uint32_t kc, uint32_t S,
+                                                 bool rms, uint32_t tid) {
+  const uint32_t n = tid >> 4, t16 = tid & 15u;  // column, thread within the half-warp
+  const float *stg = reinterpret_cast<const float *>(aux + O.stg) + n * kc;
+  const float *stw = reinterpret_cast<const float *>(aux + O.stw);
+  float *colv = reinterpret_cast<float *>(aux + O.colv);
+  uint8_t *hi = aux + O.hi, *lo = aux + O.lo;
+  const bool live = n < S;
+  float m = 0.f, ss = 0.f;
+  if (live) {
+#pragma unroll 1
+    for (uint32_t k = t16 * 4u; k < kc; k += 64u) {
+      float4 v = *reinterpret_cast<const float4 *>(stg + k);
+      ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+      if (rms) {
+        const float4 w = *reinterpret_cast<const float4 *>(stw + k);
+        v.x = __fmul_rn(v.x, w.x);
+        v.y = __fmul_rn(v.y, w.y);
+        v.z = __fmul_rn(v.z, w.z);
+        v.w = __fmul_rn(v.w, w.w);
+      }
+      m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    }
+  }
+  // half-warp reductions (xor offsets below 16 stay inside the half)
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) {
+    m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  }
+  const uint32_t ef = (__float_as_uint(m) >> 23) & 0xFFu;
+  const int e = ef < 20 ? 0 : (int)ef - 127 - 13;  // max |x| 2^-e < 2^14
+  const float inv = pow2f(-e);
+  if (t16 == 0) {
+    colv[n] = pow2f(e);
+    colv[kBatchMaxCols + n] = ss;
+  }
+#pragma unroll 1
+  for (uint32_t k = t16 * 4u; k < kc; k += 64u) {
+    float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (live) {
+      v = *reinterpret_cast<const float4 *>(stg + k);
+      if (rms) {
+        const float4 w = *reinterpret_cast<const float4 *>(stw + k);
+        v.x = __fmul_rn(v.x, w.x);
+        v.y = __fmul_rn(v.y, w.y);
+        v.z = __fmul_rn(v.z, w.z);
+        v.w = __fmul_rn(v.w, w.w);
+      }
+    }
+    const float vv[4] = {v.x * inv, v.y * inv, v.z * inv, v.w * inv};
+    __half h[4], l[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      h[i] = __float2half_rn(vv[i]);
+      l[i] = __float2half_rn(vv[i] - __half2float(h[i]));
+    }
+    if (Q8) {  // elements k..k+3 are 4 consecutive halves of one lane's 16 bytes
+      const uint32_t o = batch_bfrag_off(true, k, n);
+      *reinterpret_cast<uint2 *>(hi + o) = make_uint2(pack_half2(h[0], h[1]), pack_half2(h[2], h[3]));
+      *reinterpret_cast<uint2 *>(lo + o) = make_uint2(pack_half2(l[0], l[1]), pack_half2(l[2], l[3]));
+    } else {  // two pairs, in the 8-byte words of two lanes
+      const uint32_t o0 = batch_bfrag_off(false, k, n), o1 = batch_bfrag_off(false, k + 2u, n);
+      *reinterpret_cast<uint32_t *>(hi + o0) = pack_half2(h[0], h[1]);
+      *reinterpret_cast<uint32_t *>(lo + o0) = pack_half2(l[0], l[1]);
+      *reinterpret_cast<uint32_t *>(hi + o1) = pack_half2(h[2], h[3]);
+      *reinterpret_cast<uint32_t *>(lo + o1) = pack_half2(l[2], l[3]);
+    }
+  }
+}
+
+
+// The share of one matvec kind a CTA owns: tiles [t0, t0 + nt) of row group r
+// and segments [s0, s0 + ns) of every such tile (column group c).
+struct BatchRun {
+  uint32_t t0, nt, s0, ns, r, c;
+  bool live;
+};
+__device__ __forceinline__ BatchRun batch_run(const TileGeom &g, const BatchSplit &sp) {
+  BatchRun b{};
+  b.live = blockIdx.x < sp.R * sp.C;
+  if (!b.live) return b;
+  const uint32_t T = g.tiles(), NS = g.nseg();
+  b.r = blockIdx.x / sp.C;
+  b.c = blockIdx.x - b.r * sp.C;
+  b.t0 = T * b.r / sp.R;
+  b.nt = T * (b.r + 1u) / sp.R - b.t0;
+  b.s0 = NS * b.c / sp.C;
+  b.ns = NS * (b.c + 1u) / sp.C - b.s0;
+  return b;
+}
+__device__ __forceinline__ uint32_t batch_stages(const BatchRun &b) { return (b.nt * b.ns + kStageSegs - 1u) / kStageSegs; }
+
+// Ring stage k stages after rp: slot and the parity of that use.
+__device__ __forceinline__ void ring_at(const RingPos &rp, uint32_t k, uint32_t nst, uint32_t &slot, uint32_t &par) {
+  const uint32_t s = rp.slot + k;
+  slot = s % nst;
+  par = rp.phase ^ ((s / nst) & 1u);
+}
+
+// Producer side of a batched matvec: the CTA's items (tile, segment), tile
+// by tile, kStageSegs per stage; a stage is one bulk copy per tile it spans
+// (a tile's segments of one column group are contiguous in HBM).
+__device__ __forceinline__ bool batch_produce(const MvRing &R, const uint8_t *w, const TileGeom &g, const BatchRun &b,
+                                              RingPos &rp, const uint32_t *abort_flag, uint32_t *err) {
+  const uint32_t SEGB = g.seg_bytes(), NS = g.nseg(), n_items = b.nt * b.ns;
+  for (uint32_t i0 = 0; i0 < n_items; i0 += kStageSegs) {
+    const uint32_t n = min(kStageSegs, n_items - i0);
+    if (!ring_claim(R, rp, n * SEGB, abort_flag, err)) return false;
+    uint8_t *dst = R.ring + rp.slot * R.slot;
+    for (uint32_t i = i0; i < i0 + n;) {
+      const uint32_t t = i / b.ns, s = i - t * b.ns;
+      const uint32_t run = min(i0 + n - i, b.ns - s);
+      bulk_g2s(dst + (i - i0) * SEGB, w + ((uint64_t)(b.t0 + t) * NS + b.s0 + s) * SEGB, run * SEGB, &R.full[rp.slot]);
+      i += run;
+    }
+    rp.next(R.nst);
+  }
+  return true;
+}
+
+// Consumer side of a batched matvec, one warp: it owns the contiguous group of
+// tiles [nt * cw / 8, nt * (cw + 1) / 8) of the CTA's run and takes them up to
+// TB at a time, every K-step of its slice, the B fragments loaded once per
+// K-step for all of them. Partial sums (times each column's 2^e) go to
+// part[c][tile][row][column]. Every warp waits for and releases every stage
+// of the phase exactly once, in order (the empty barriers count 8 arrivals);
+// a batch spans at most 8 items, i.e. 3 stages, fewer than the ring holds.
+template <bool Q8>
+__device__ __forceinline__ void batch_consume(const MvRing &R, const RingPos &rp0, const BatchRun &b,
+                                              const TileGeom &g, const uint8_t *aux, const BatchOperand &O,
+                                              uint32_t S, float *part, uint32_t part_tiles, uint32_t cw, uint32_t lane,
+                                              const uint32_t *abort_flag, uint32_t *err, bool &ok) {
+  const uint32_t SEGB = g.seg_bytes(), n_items = b.nt * b.ns, nstg = batch_stages(b);
+  const uint32_t g0 = b.nt * cw / kMvConsumers, g1 = b.nt * (cw + 1u) / kMvConsumers;
+  const uint32_t TB = max(1u, min(4u, 8u / max(b.ns, 1u)));
+  const uint32_t gq = lane >> 2, tq = lane & 3u;
+  const bool two = S > 8u;  // the second n8 tile (columns 8-15) carries live columns
+  const float *colv = reinterpret_cast<const float *>(aux + O.colv);
+  const float sc[4] = {colv[2u * tq], colv[2u * tq + 1u], colv[8u + 2u * tq], colv[9u + 2u * tq]};
+  const uint8_t *hi = aux + O.hi, *lo = aux + O.lo;
+  auto wait_full = [&](uint32_t k) {
+    uint32_t sl, par;
+    ring_at(rp0, k, R.nst, sl, par);
+    if (!mbar_wait_bounded(&R.full[sl], par, abort_flag)) {
+      set_error(err, kErrConsumerWait);
+      ok = false;
+    }
+  };
+  auto release = [&](uint32_t k) {
+    uint32_t sl, par;
+    ring_at(rp0, k, R.nst, sl, par);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&R.empty[sl]);
+  };
+  uint32_t next = 0;  // first stage this warp has not released
+  for (uint32_t tb = g0; tb < g1; tb += TB) {
+    const uint32_t te = min(tb + TB, g1), nb = te - tb;
+    const uint32_t sa = tb * b.ns / kStageSegs, sb = (te * b.ns - 1u) / kStageSegs;
+    for (; next < sa; ++next) {
+      wait_full(next);
+      release(next);
+    }
+    for (uint32_t k = next; k <= sb; ++k) wait_full(k);
+    float tot[4][2][4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) tot[j][nt][i] = 0.f;
+#pragma unroll 1
+    for (uint32_t seg = 0; seg < b.ns; ++seg) {
+      const uint8_t *sg[4];
+#pragma unroll
+      for (uint32_t j = 0; j < 4; ++j) {
+        const uint32_t item = (tb + min(j, nb - 1u)) * b.ns + seg;
+        uint32_t sl, par;
+        ring_at(rp0, item / kStageSegs, R.nst, sl, par);
+        sg[j] = R.ring + sl * R.slot + (item % kStageSegs) * SEGB;
+      }
+#pragma unroll 2
+      for (uint32_t q = 0; q < kSegSteps; ++q) {
+        const uint32_t kk = seg * kSegSteps + q;  // K-step within the slice
+        if constexpr (Q8) {
+          const uint32_t bo = ((kk * kBatchMaxCols + gq) * 4u + tq) * 16u;
+          const uint4 bh0 = *reinterpret_cast<const uint4 *>(hi + bo), bl0 = *reinterpret_cast<const uint4 *>(lo + bo);
+          uint4 bh1 = make_uint4(0u, 0u, 0u, 0u), bl1 = bh1;
+          if (two) {
+            bh1 = *reinterpret_cast<const uint4 *>(hi + bo + 8u * 64u);
+            bl1 = *reinterpret_cast<const uint4 *>(lo + bo + 8u * 64u);
+          }
+#pragma unroll
+          for (uint32_t j = 0; j < 4; ++j) {
+            if (j >= nb) break;
+            uint32_t a[4], A1[4], A2[4];
+            ldmatrix_x4(a, sg[j] + q * kStepBytes + lane * 16u);
+            i8x4_to_h2x2(a[0], A1[0], A1[2]);
+            i8x4_to_h2x2(a[1], A1[1], A1[3]);
+            i8x4_to_h2x2(a[2], A2[0], A2[2]);
+            i8x4_to_h2x2(a[3], A2[1], A2[3]);
+            const float2 d = __half22float2(*reinterpret_cast<const __half2 *>(sg[j] + kSegQsBytes + gq * 32u + q * 4u));
+            float c[4];
+            mma_f16_zero(c, A1, bh0.x, bh0.y);
+            mma_f16(c, A1, bl0.x, bl0.y);
+            mma_f16(c, A2, bh0.z, bh0.w);
+            mma_f16(c, A2, bl0.z, bl0.w);
+            tot[j][0][0] = fmaf(c[0], d.x, tot[j][0][0]);
+            tot[j][0][1] = fmaf(c[1], d.x, tot[j][0][1]);
+            tot[j][0][2] = fmaf(c[2], d.y, tot[j][0][2]);
+            tot[j][0][3] = fmaf(c[3], d.y, tot[j][0][3]);
+            if (two) {
+              mma_f16_zero(c, A1, bh1.x, bh1.y);
+              mma_f16(c, A1, bl1.x, bl1.y);
+              mma_f16(c, A2, bh1.z, bh1.w);
+              mma_f16(c, A2, bl1.z, bl1.w);
+              tot[j][1][0] = fmaf(c[0], d.x, tot[j][1][0]);
+              tot[j][1][1] = fmaf(c[1], d.x, tot[j][1][1]);
+              tot[j][1][2] = fmaf(c[2], d.y, tot[j][1][2]);
+              tot[j][1][3] = fmaf(c[3], d.y, tot[j][1][3]);
+            }
+          }
+        } else {
+          const uint32_t bo = ((kk * kBatchMaxCols + gq) * 4u + tq) * 8u;
+          const uint2 bh0 = *reinterpret_cast<const uint2 *>(hi + bo), bl0 = *reinterpret_cast<const uint2 *>(lo + bo);
+          uint2 bh1 = make_uint2(0u, 0u), bl1 = bh1;
+          if (two) {
+            bh1 = *reinterpret_cast<const uint2 *>(hi + bo + 8u * 32u);
+            bl1 = *reinterpret_cast<const uint2 *>(lo + bo + 8u * 32u);
+          }
+#pragma unroll
+          for (uint32_t j = 0; j < 4; ++j) {
+            if (j >= nb) break;
+            uint32_t a[4];
+            ldmatrix_x4(a, sg[j] + q * kStepBytes + lane * 16u);
+            mma_f16(tot[j][0], a, bh0.x, bh0.y);
+            mma_f16(tot[j][0], a, bl0.x, bl0.y);
+            if (two) {
+              mma_f16(tot[j][1], a, bh1.x, bh1.y);
+              mma_f16(tot[j][1], a, bl1.x, bl1.y);
+            }
+          }
+        }
+      }
+    }
+    // partial sums of the batch's tiles; lane (gq, tq) holds rows gq, gq + 8 and
+    // columns 8 nt + 2 tq, 8 nt + 2 tq + 1
+#pragma unroll
+    for (uint32_t j = 0; j < 4; ++j) {
+      if (j >= nb) break;
+      float *pt = part + ((size_t)b.c * part_tiles + b.t0 + tb + j) * 256u;
+#pragma unroll
+      for (uint32_t nt = 0; nt < 2; ++nt) {
+        if (nt == 1 && !two) break;
+        const uint32_t col = nt * 8u + 2u * tq;
+        *reinterpret_cast<float2 *>(pt + gq * 16u + col) =
+            make_float2(tot[j][nt][0] * sc[2u * nt], tot[j][nt][1] * sc[2u * nt + 1u]);
+        *reinterpret_cast<float2 *>(pt + (gq + 8u) * 16u + col) =
+            make_float2(tot[j][nt][2] * sc[2u * nt], tot[j][nt][3] * sc[2u * nt + 1u]);
+      }
+    }
+    // stages done: all up to sb when this was the warp's last batch, else those
+    // before the stage its next batch starts in
+    const uint32_t done = te == g1 ? sb + 1u : te * b.ns / kStageSegs;
+    for (; next < done; ++next) release(next);
+  }
+  for (; next < nstg; ++next) {
+    wait_full(next);
+    release(next);
+  }
+  (void)n_items;
+}
+
+// Reduction of a row group's partials and the epilogue, after the C CTAs of
+// the group have arrived: this CTA takes the group's tiles c, c + C, ...; a
+// thread takes (tile, row pair p / p + 8, column n) and adds the C partials
+// in column-group order. rs[n] is the column's deferred RMSNorm scale (or 1).
+template <class Epi>
+__device__ __forceinline__ void batch_reduce(const BatchRun &b, uint32_t C, const float *part, uint32_t part_tiles,
+                                             const float *rs, uint32_t S, uint32_t tid, Epi epi) {
+  const uint32_t half = tid >> 7, pr = (tid >> 4) & 7u, n = tid & 15u;
+  const size_t stride = (size_t)part_tiles * 256u;
+  for (uint32_t i = half; b.c + i * C < b.nt; i += 2u) {
+    const uint32_t t = b.t0 + b.c + i * C;
+    const float *pt = part + (size_t)t * 256u + pr * 16u + n;
+    float a = 0.f, c2 = 0.f;
+    for (uint32_t cg = 0; cg < C; ++cg) {
+      a += __ldcg(pt + cg * stride);
+      c2 += __ldcg(pt + cg * stride + 128u);
+    }
+    if (n < S) epi(t * kTileRows + pr, n, a * rs[n], c2 * rs[n]);
+  }
+}
+
+enum : uint32_t { kBkQkv = 0, kBkO = 1, kBkGu = 2, kBkDown = 3 };
+
+// Attention unit u of a batched step: units are ordered by column, KV head,
+// chunk; cu0 holds each column's first unit.
+struct BatchUnit {
+  uint32_t n, kvh, c, r0, len, staged;
+};
+__device__ __forceinline__ BatchUnit batch_unit(uint32_t u, const uint32_t *cu0, const uint32_t *cnch,
+                                                const uint32_t *cpos, const uint32_t *cff, uint32_t S, uint32_t chunk) {
+  BatchUnit a;
+  uint32_t n = 0;
+  while (n + 1u < S && cu0[n + 1u] <= u) ++n;
+  const uint32_t w = u - cu0[n], nch = cnch[n];
+  a.n = n;
+  a.kvh = w / nch;
+  a.c = w - a.kvh * nch;
+  a.r0 = a.c * chunk;
+  const uint32_t r1 = min(a.r0 + chunk, cpos[n] + 1u);
+  a.len = r1 - a.r0;
+  const uint32_t f = min(r1, cff[n]);  // rows below f were written by earlier launches
+  a.staged = f > a.r0 ? f - a.r0 : 0u;
+  return a;
+}
+
+// One CTA of kMvThreads (8 consumer warps + the producer warp) per SM.
+template <bool Q8, int DPL>
+__global__ void __launch_bounds__(kMvThreads, 1) decode_batch_kernel(const __grid_constant__ BatchParams p) {
+  constexpr uint32_t NCT = kMvConsumers * 32;
+  constexpr uint32_t D = 32u * DPL;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const BatchSmem L(p);
+  MvRing R;
+  R.ring = smem + L.ring;
+  R.full = reinterpret_cast<uint64_t *>(smem + L.bars);
+  R.empty = R.full + p.nst;
+  R.nst = p.nst;
+  R.slot = p.slot;
+  uint8_t *aux = smem + L.aux;
+  uint64_t *sbar = reinterpret_cast<uint64_t *>(smem + L.sbar);  // staging: input rows, norm weight
+  StepLayer *layers = reinterpret_cast<StepLayer *>(smem + L.layers);
+  // scratch: per-column state, row scales, barrier bases, unit-arrival bases
+  uint32_t *cpos = reinterpret_cast<uint32_t *>(smem + L.scr);  // [16] position
+  uint32_t *cff = cpos + 16;                                     // [16] first row written by this launch
+  uint32_t *cnch = cpos + 32;                                    // [16] attention chunks
+  uint32_t *cu0 = cpos + 48;                                     // [17] first unit of each column
+  float *rsc = reinterpret_cast<float *>(smem + L.scr + 384u);    // [16] deferred RMSNorm scales
+  float *red = reinterpret_cast<float *>(smem + L.scr + 448u);    // [16] final-norm reduction
+  unsigned long long *sb = reinterpret_cast<unsigned long long *>(smem + L.scr + 512u);  // [1 + 4]
+  unsigned long long *srdy = reinterpret_cast<unsigned long long *>(smem + L.scr + 1024u);  // [S * kv_heads]
+  BatchCol *scol = reinterpret_cast<BatchCol *>(smem + L.scr + 2048u);  // [16]
+
+  const uint32_t warp = threadIdx.x >> 5, lane = threadIdx.x & 31u;
+  uint32_t *err = p.ctrl + kCtrlErr;
+  const uint32_t nb = p.n_layers * kPhasesPerLayer;
+  const uint32_t G = p.heads / p.kv_heads, S = p.S;
+
+  if (threadIdx.x == 0) {
+    for (uint32_t i = 0; i < R.nst; ++i) {
+      mbar_init(&R.full[i], 1);
+      mbar_init(&R.empty[i], kMvConsumers);
+    }
+    mbar_init(&sbar[0], 1);
+    mbar_init(&sbar[1], 1);
+    fence_mbar_init();
+    // every CTA arrives nb times per launch at the grid barrier, and the C
+    // CTAs of a row group C times per layer at the group's counter
+    const unsigned long long c = ld_acquire_u64(p.bar), unit = (unsigned long long)nb * gridDim.x;
+    sb[0] = c - c % unit;
+    for (uint32_t k = 0; k < kBatchKinds; ++k) {
+      const BatchSplit sp = p.split[k];
+      sb[1 + k] = 0;
+      if (blockIdx.x < sp.R * sp.C) {
+        const unsigned long long v = ld_acquire_u64(p.rgc + k * kBatchMaxRowGroups + blockIdx.x / sp.C);
+        sb[1 + k] = v - v % ((unsigned long long)sp.C * p.n_layers);
+      }
+    }
+  }
+  for (uint32_t i = threadIdx.x; i < p.n_layers * (uint32_t)sizeof(StepLayer) / 8u; i += blockDim.x)
+    reinterpret_cast<unsigned long long *>(layers)[i] = reinterpret_cast<const unsigned long long *>(p.layers)[i];
+  for (uint32_t i = threadIdx.x; i < S * (uint32_t)sizeof(BatchCol) / 8u; i += blockDim.x)
+    reinterpret_cast<unsigned long long *>(scol)[i] = reinterpret_cast<const unsigned long long *>(p.cols)[i];
+  // read before this CTA's first arrival (the first unit release of the
+  // launch comes after the first grid barrier)
+  for (uint32_t i = threadIdx.x; i < S * p.kv_heads; i += blockDim.x) srdy[i] = ld_acquire_u64(p.ready + i);
+  __syncthreads();
+  if (threadIdx.x < S) {
+    const BatchCol &cl = scol[threadIdx.x];
+    const uint32_t f = cl.ctrl[kCtrlPos];
+    uint32_t pos = f + cl.off;
+    if (pos >= cl.ctx) {
+      set_error(err, kErrPosition);
+      pos = cl.ctx - 1u;
+    }
+    cpos[threadIdx.x] = pos;
+    cff[threadIdx.x] = min(f, pos);
+    cnch[threadIdx.x] = (pos + p.chunk) / p.chunk;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    uint32_t u = 0;
+    for (uint32_t n = 0; n < S; ++n) {
+      cu0[n] = u;
+      u += p.kv_heads * cnch[n];
+    }
+    cu0[S] = u;
+  }
+  __syncthreads();
+  const unsigned long long base = sb[0];
+  const uint32_t n_units = cu0[S];
+
+  // ---------------- producer ----------------
+  if (warp == kMvConsumers) {
+    if (lane == 0) {
+      RingPos rp;
+      bool live = true;
+      auto rows = [&](const __half *src, uint32_t n) {  // one stage of n cached K or V rows
+        if (!live) return;
+        live = ring_claim(R, rp, n * D * 2u, err, err);
+        if (!live) return;
+        if (n) bulk_g2s(R.ring + rp.slot * R.slot, src, n * D * 2u, &R.full[rp.slot]);
+        rp.next(R.nst);
+      };
+      for (uint32_t ph = 0; ph < nb && live; ++ph) {
+        const uint32_t l = ph / kPhasesPerLayer, kind = ph - l * kPhasesPerLayer;
+        const StepLayer &Ly = layers[l];
+        if (kind == kPhAttn) {
+          for (uint32_t u = blockIdx.x; u < n_units; u += gridDim.x) {
+            const BatchUnit a = batch_unit(u, cu0, cnch, cpos, cff, S, p.chunk);
+            const BatchCol &cl = scol[a.n];
+            const size_t off = (size_t)l * cl.layer_elems + ((size_t)a.kvh * cl.ctx + a.r0) * D;
+            rows(cl.kc + off, a.staged);
+            rows(cl.vc + off, a.staged);
+          }
+          continue;
+        }
+        const uint32_t k = kind == kPhQkv ? kBkQkv : kind == kPhO ? kBkO : kind == kPhGu ? kBkGu : kBkDown;
+        const uint8_t *w = k == kBkQkv ? Ly.qkv : k == kBkO ? Ly.o : k == kBkGu ? Ly.gateup : Ly.down;
+        const BatchRun b = batch_run(p.g[k], p.split[k]);
+        if (b.live) live = batch_produce(R, w, p.g[k], b, rp, err, err);
+      }
+      if (live) mv_drain(R, rp, err);
+    }
+    return;
+  }
+
+  // ---------------- consumers ----------------
+  const uint32_t cw = warp, tid = cw * 32u + lane;
+  RingPos rp;
+  bool ok = true;
+  uint32_t spar = 0;  // parities of the two staging barriers
+  auto wait_phase = [&](uint32_t ph) {
+    if (tid == 0 && ph > 0 && !grid_wait(p.bar, base + (unsigned long long)ph * gridDim.x, err))
+      set_error(err, kErrGridWait);
+    named_bar(1, NCT);
+  };
+  auto arrive = [&] {
+    named_bar(1, NCT);
+    if (tid == 0) grid_arrive(p.bar);
+  };
+
+  // One matvec phase of kind k at layer l: operand of this CTA's K-slice, K
+  // loop, partials, row-group arrival, reduction of its share and epilogue.
+  auto matvec = [&](uint32_t k, uint32_t ph, uint32_t l) {
+    const StepLayer &Ly = layers[l];
+    const TileGeom &g = p.g[k];
+    const BatchSplit sp = p.split[k];
+    const BatchRun b = batch_run(g, sp);
+    const uint32_t kc = b.ns * g.seg_cols(), k0 = b.s0 * g.seg_cols();
+    const BatchOperand O(kc);
+    const bool rms = k == kBkQkv || k == kBkGu;
+    const bool tokin = k == kBkQkv && l == 0;  // layer 0 reads the token rows
+    const float *src = k == kBkQkv ? p.hid_a : k == kBkO ? p.attn : k == kBkGu ? p.hid_b : p.gate;
+    const uint32_t ld = k == kBkDown ? p.F : p.H;
+    const uint32_t cols = g.cols;
+    // the slice's columns inside the input (the last group may reach into the
+    // matrix's zero padding, where the staged input must be zero as well)
+    const uint32_t valid = b.live ? min(kc, cols - k0) : 0u;
+    // the norm weight does not depend on the step: copied before the wait
+    if (b.live && rms && tid == 0) {
+      mbar_arrive_expect_tx(sbar + 1, valid * 4u);
+      bulk_g2s(aux + O.stw, (k == kBkQkv ? Ly.attn_norm : Ly.ffn_norm) + k0, valid * 4u, sbar + 1);
+    }
+    if (tid == 0) {
+      if (ph > 0 && !grid_wait(p.bar, base + (unsigned long long)ph * gridDim.x, err)) set_error(err, kErrGridWait);
+      if (b.live && !tokin) {
+        fence_proxy_async_global();
+        mbar_arrive_expect_tx(sbar, S * valid * 4u);
+        for (uint32_t n = 0; n < S; ++n)
+          bulk_g2s(aux + O.stg + n * kc * 4u, src + (size_t)n * ld + k0, valid * 4u, sbar);
+      }
+    }
+    if (b.live && valid < kc) {  // the padding part of the slice: zero input and weight
+      float *stg = reinterpret_cast<float *>(aux + O.stg), *stw = reinterpret_cast<float *>(aux + O.stw);
+      const uint32_t pad = kc - valid;
+      for (uint32_t i = tid; i < S * pad; i += NCT) stg[(i / pad) * kc + valid + i % pad] = 0.f;
+      for (uint32_t i = tid; i < pad; i += NCT) stw[valid + i] = 0.f;
+    }
+    named_bar(1, NCT);
+    if (b.live) {
+      float *stg = reinterpret_cast<float *>(aux + O.stg);
+      if (tokin) {
+        // embedding.comp:28-47 for every column; row group 0 also stores the
+        // rows as the residual stream
+        XSrc ts{};
+        ts.tab = p.tok;
+        ts.g = p.g_tok;
+        ts.alpha = p.emb_scale;
+        for (uint32_t i = tid; i < S * valid; i += NCT) {
+          const uint32_t n = i / valid, kk = i - n * valid;
+          ts.token = scol[n].token;
+          const float v = xsrc_elem<true>(ts, k0 + kk);
+          stg[n * kc + kk] = v;
+          if (b.r == 0) p.hid_a[(size_t)n * p.H + k0 + kk] = v;
+        }
+        named_bar(1, NCT);
+      } else {
+        if (!mbar_wait_bounded(sbar, spar & 1u, err)) {
+          set_error(err, kErrConsumerWait);
+          ok = false;
+        }
+        spar ^= 1u;
+      }
+      if (rms) {
+        if (!mbar_wait_bounded(sbar + 1, (spar >> 1) & 1u, err)) {
+          set_error(err, kErrConsumerWait);
+          ok = false;
+        }
+        spar ^= 2u;
+      }
+      batch_activation<Q8>(O, aux, kc, S, rms, tid);
+      named_bar(1, NCT);
+      if (tid < kBatchMaxCols) p.ssb[(b.r * sp.C + b.c) * kBatchMaxCols + tid] =
+          reinterpret_cast<const float *>(aux + O.colv)[kBatchMaxCols + tid];
+      batch_consume<Q8>(R, rp, b, g, aux, O, S, p.part, p.part_tiles, cw, lane, err, err, ok);
+      // every partial of the CTA is written: one arrival at the row group
+      named_bar(1, NCT);
+      if (tid == 0) grid_arrive(p.rgc + k * kBatchMaxRowGroups + b.r);
+    }
+    for (uint32_t i = 0; i < batch_stages(b); ++i) rp.next(R.nst);
+    if (!b.live) return;
+    // wait for the C CTAs of the row group, then reduce this CTA's share
+    if (tid == 0 && !grid_wait(p.rgc + k * kBatchMaxRowGroups + b.r,
+                               sb[1 + k] + (unsigned long long)sp.C * (l + 1u), err))
+      set_error(err, kErrGridWait);
+    named_bar(1, NCT);
+    if (tid < kBatchMaxCols) {
+      float r = 1.0f;
+      if (rms) {
+        float ss = 0.f;
+        for (uint32_t cg = 0; cg < sp.C; ++cg) ss += __ldcg(p.ssb + (b.r * sp.C + cg) * kBatchMaxCols + tid);
+        r = 1.0f / sqrtf(ss / (float)cols + p.eps);  // rmsnorm.comp:21-42, deferred to the rows
+      }
+      rsc[tid] = r;
+    }
+    named_bar(1, NCT);
+    batch_reduce(b, sp.C, p.part, p.part_tiles, rsc, S, tid, [&](uint32_t R0, uint32_t n, float a, float c2) {
+      const uint32_t R1 = R0 + 8u;
+      if (k == kBkQkv) {
+        // QKV: RoPE on the (i, i + d/2) pair in rows R0 / R1, fp16 K and V rows
+        // (rope.comp:22-51, store_kv.comp:16-24)
+        if (R0 >= g.rows) return;
+        const uint32_t H = p.H, KV = p.kv_heads * D, hd = D / 2u, pos = cpos[n];
+        const BatchCol &cl = scol[n];
+        if (R0 < H + KV) {
+          const bool isq = R0 < H;
+          const uint32_t Rr = isq ? R0 : R0 - H;
+          const uint32_t head = Rr / D, wr = Rr % D, i = (wr / kTileRows) * 8u + (wr % kTileRows);
+          rope_pair(a, c2, pos, i, p.inv_freq, p.ext, p.rope_scaling);
+          if (isq) {
+            p.q[(size_t)n * H + head * D + i] = a;
+            p.q[(size_t)n * H + head * D + i + hd] = c2;
+          } else {
+            __half *dst = cl.kc + (size_t)l * cl.layer_elems + ((size_t)head * cl.ctx + pos) * D;
+            dst[i] = __float2half_rn(a);
+            dst[i + hd] = __float2half_rn(c2);
+          }
+        } else {
+          const uint32_t v = R0 - H - KV, kvh = v / D, j = v % D;
+          __half *dst = cl.vc + (size_t)l * cl.layer_elems + ((size_t)kvh * cl.ctx + pos) * D;
+          dst[j] = __float2half_rn(a);
+          dst[j + 8u] = __float2half_rn(c2);
+        }
+      } else if (k == kBkGu) {
+        // matvec_swiglu.comp:67: gate row t * 8 + p (rows R0 / R1 hold gate / up)
+        const uint32_t o = (R0 / kTileRows) * 8u + (R0 % kTileRows);
+        if (2u * o < g.rows)
+          p.gate[(size_t)n * p.F + o] = __fmul_rn(__fdiv_rn(a, __fadd_rn(1.0f, expf(-a))), c2);
+      } else {
+        // residual_rmsnorm.comp:27: hidden + scale * branch
+        float *out = k == kBkO ? p.hid_b : p.hid_a;
+        const float *res = k == kBkO ? p.hid_a : p.hid_b;
+        const size_t rb = (size_t)n * p.H;
+        if (R0 < g.rows) out[rb + R0] = __fadd_rn(__ldcg(res + rb + R0), __fmul_rn(a, p.res_scale));
+        if (R1 < g.rows) out[rb + R1] = __fadd_rn(__ldcg(res + rb + R1), __fmul_rn(c2, p.res_scale));
+      }
+    });
+  };
+
+  // One attention phase at layer l (attn_scores / softmax / attn_values,
+  // split-K): this CTA's units, then its merge slices.
+  auto attention = [&](uint32_t ph, uint32_t l) {
+    wait_phase(ph);
+    constexpr uint32_t KS = D / 16u;              // K-steps of a head row
+    const uint32_t HT = (G + 7u) / 8u;            // tiles of 8 heads
+    const uint32_t SST = p.chunk + 4u;            // row stride of sS (padded)
+    uint2 *sQB = reinterpret_cast<uint2 *>(aux);  // [HT][KS][2][32] q fragments
+    float *sS = reinterpret_cast<float *>(aux + HT * KS * 2u * 32u * 8u);  // [G][SST]
+    constexpr uint32_t W2 = D / 2u;               // 32-bit words of a row
+    for (uint32_t u = blockIdx.x; u < n_units; u += gridDim.x) {
+      const BatchUnit a = batch_unit(u, cu0, cnch, cpos, cff, S, p.chunk);
+      const BatchCol &cl = scol[a.n];
+      const size_t lo = (size_t)l * cl.layer_elems + (size_t)a.kvh * cl.ctx * D;
+      const __half *kg = cl.kc + lo, *vg = cl.vc + lo;
+      // rows this launch wrote (positions >= cff): from L2; the first word of
+      // each thread is loaded here, so its round trip overlaps the q loads
+      const uint32_t nfw = (a.len - a.staged) * W2, fr = a.r0 + a.staged;
+      uint32_t kw0 = 0, vw0 = 0;
+      if (tid < nfw) {
+        kw0 = __ldcg(reinterpret_cast<const unsigned int *>(kg + (size_t)fr * D) + tid);
+        vw0 = __ldcg(reinterpret_cast<const unsigned int *>(vg + (size_t)fr * D) + tid);
+      }
+      for (uint32_t e = tid; e < HT * KS * 32u; e += NCT) {
+        const uint32_t ln = e & 31u, ks = (e >> 5) % KS, ht = (e >> 5) / KS;
+        const uint32_t g = ht * 8u + (ln >> 2), d0 = ks * 16u + (ln & 3u) * 2u;
+        float v[4] = {0.f, 0.f, 0.f, 0.f};
+        if (g < G) {
+          const float *qg = p.q + (size_t)a.n * p.H + ((size_t)a.kvh * G + g) * D + d0;
+          v[0] = __ldcg(qg);
+          v[1] = __ldcg(qg + 1);
+          v[2] = __ldcg(qg + 8);
+          v[3] = __ldcg(qg + 9);
+        }
+        uint32_t hw[2], lw[2];
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const __half h0 = __float2half_rn(v[2 * j]), h1 = __float2half_rn(v[2 * j + 1]);
+          hw[j] = pack_half2(h0, h1);
+          lw[j] = pack_half2(__float2half_rn(v[2 * j] - __half2float(h0)), __float2half_rn(v[2 * j + 1] - __half2float(h1)));
+        }
+        sQB[((ht * KS + ks) * 2u + 0u) * 32u + ln] = make_uint2(hw[0], hw[1]);
+        sQB[((ht * KS + ks) * 2u + 1u) * 32u + ln] = make_uint2(lw[0], lw[1]);
+      }
+      const uint32_t sK = rp.slot, pK = rp.phase;
+      rp.next(R.nst);
+      const uint32_t sV = rp.slot, pV = rp.phase;
+      rp.next(R.nst);
+      if (!mbar_wait_bounded(&R.full[sK], pK, err) || !mbar_wait_bounded(&R.full[sV], pV, err)) {
+        set_error(err, kErrConsumerWait);
+        ok = false;
+      }
+      __half *kS = reinterpret_cast<__half *>(R.ring + sK * R.slot);
+      __half *vS = reinterpret_cast<__half *>(R.ring + sV * R.slot);
+      const uint32_t len16 = (a.len + 15u) & ~15u;
+      if (tid < nfw) {
+        reinterpret_cast<uint32_t *>(kS + a.staged * D)[tid] = kw0;
+        reinterpret_cast<uint32_t *>(vS + a.staged * D)[tid] = vw0;
+      }
+      for (uint32_t i = tid + NCT; i < nfw; i += NCT) {
+        reinterpret_cast<uint32_t *>(kS + a.staged * D)[i] =
+            __ldcg(reinterpret_cast<const unsigned int *>(kg + (size_t)fr * D) + i);
+        reinterpret_cast<uint32_t *>(vS + a.staged * D)[i] =
+            __ldcg(reinterpret_cast<const unsigned int *>(vg + (size_t)fr * D) + i);
+      }
+      // V rows past the chunk's end meet zero weights; make them zero too
+      for (uint32_t i = a.len * W2 + tid; i < len16 * W2; i += NCT) reinterpret_cast<uint32_t *>(vS)[i] = 0u;
+      named_bar(1, NCT);
+      // scores (attn_scores.comp:27-44) on the tensor cores: warp per (16 positions, 8 heads)
+      for (uint32_t it = cw; it < (len16 / 16u) * HT; it += kMvConsumers) {
+        const uint32_t pt = it / HT, ht = it % HT;
+        float c[4] = {0.f, 0.f, 0.f, 0.f}, cl2[4] = {0.f, 0.f, 0.f, 0.f};
+        const __half *kb = kS + (pt * 16u + (lane & 15u)) * D + (lane >> 4) * 8u;
+#pragma unroll 4
+        for (uint32_t ks = 0; ks < KS; ++ks) {
+          uint32_t af[4];
+          ldmatrix_x4(af, kb + ks * 16u);
+          const uint2 bh = sQB[((ht * KS + ks) * 2u + 0u) * 32u + lane];
+          const uint2 bl = sQB[((ht * KS + ks) * 2u + 1u) * 32u + lane];
+          mma_f16(c, af, bh.x, bh.y);
+          mma_f16(cl2, af, bl.x, bl.y);
+        }
+        const uint32_t t = pt * 16u + (lane >> 2), g = ht * 8u + (lane & 3u) * 2u;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t tt = t + (j >> 1) * 8u, gg = g + (j & 1);
+          if (tt < a.len && gg < G) sS[gg * SST + tt] = __fmul_rn(__fadd_rn(c[j], cl2[j]), p.attn_scale);
+        }
+      }
+      named_bar(1, NCT);
+      const size_t pslot = ((size_t)a.n * p.kv_heads + a.kvh) * p.max_chunks + a.c;  // (column, KV head, chunk)
+      // chunk softmax (softmax.comp): warp per head
+      for (uint32_t g0 = cw; g0 < G; g0 += kMvConsumers) {
+        float *sg = sS + g0 * SST;
+        float m = -INFINITY;
+        for (uint32_t t = lane; t < a.len; t += 32) m = fmaxf(m, sg[t]);
+        m = warp_max(m);
+        float lsum = 0.f;
+        for (uint32_t t = lane; t < a.len; t += 32) {
+          const float e = expf(sg[t] - m);
+          sg[t] = e;
+          lsum += e;
+        }
+        lsum = warp_sum(lsum);
+        if (lane == 0) p.apart_ml[pslot * G + g0] = make_float2(m, lsum);
+      }
+      named_bar(1, NCT);
+      // values (attn_values.comp) as (V^T)(P^T): warp per (16 dims, 8 heads)
+      for (uint32_t it = cw; it < KS * HT; it += kMvConsumers) {
+        const uint32_t dt = it / HT, ht = it % HT;
+        float c[4] = {0.f, 0.f, 0.f, 0.f}, cl2[4] = {0.f, 0.f, 0.f, 0.f};
+        const uint32_t gb = ht * 8u + (lane >> 2);
+        const float *pg = sS + (gb < G ? gb : 0u) * SST;
+        const __half *vb = vS + (((lane >> 4) & 1u) * 8u + (lane & 7u)) * D + dt * 16u + ((lane >> 3) & 1u) * 8u;
+        for (uint32_t kk = 0; kk < len16 / 16u; ++kk) {
+          uint32_t af[4];
+          ldmatrix_x4_trans(af, vb + kk * 16u * D);
+          float w[4];
+          const uint32_t t0w = kk * 16u + (lane & 3u) * 2u;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint32_t tt = t0w + (j & 1) + (j >> 1) * 8u;
+            w[j] = (gb < G && tt < a.len) ? pg[tt] : 0.f;
+          }
+          uint32_t bh[2], bl[2];
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const __half h0 = __float2half_rn(w[2 * j]), h1 = __float2half_rn(w[2 * j + 1]);
+            bh[j] = pack_half2(h0, h1);
+            bl[j] = pack_half2(__float2half_rn(w[2 * j] - __half2float(h0)), __float2half_rn(w[2 * j + 1] - __half2float(h1)));
+          }
+          mma_f16(c, af, bh[0], bh[1]);
+          mma_f16(cl2, af, bl[0], bl[1]);
+        }
+        const uint32_t d = dt * 16u + (lane >> 2), g = ht * 8u + (lane & 3u) * 2u;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t dd = d + (j >> 1) * 8u, gg = g + (j & 1);
+          if (gg < G) p.apart[(pslot * G + gg) * D + dd] = __fadd_rn(c[j], cl2[j]);
+        }
+      }
+      named_bar(1, NCT);
+      if (lane == 0) {
+        mbar_arrive(&R.empty[sK]);
+        mbar_arrive(&R.empty[sV]);
+      }
+      if (tid == 0) grid_arrive(p.ready + a.n * p.kv_heads + a.kvh);
+      named_bar(1, NCT);  // sQB / sS reuse
+    }
+    // merge slices, one per (column, query head), from the end of the grid:
+    // o = sum_c exp(m_c - M) o_c / sum_c exp(m_c - M) l_c over the chunks
+    for (uint32_t m = gridDim.x - 1u - blockIdx.x; m < S * p.heads; m += gridDim.x) {
+      const uint32_t n = m / p.heads, h = m - n * p.heads, kvh = h / G, g0 = h - kvh * G;
+      const uint32_t nch = cnch[n];
+      if (tid == 0 && !grid_wait(p.ready + n * p.kv_heads + kvh, srdy[n * p.kv_heads + kvh] +
+                                                                     (unsigned long long)(l + 1u) * nch, err))
+        set_error(err, kErrGridWait);
+      named_bar(1, NCT);
+      constexpr uint32_t NCOL = D / 4u, NGR = NCT / NCOL, MR = 8u;
+      static_assert(NCT % NCOL == 0, "whole chunk groups");
+      float *sW = reinterpret_cast<float *>(aux);
+      float4 *sO = reinterpret_cast<float4 *>(aux + step_merge_w_bytes(p.max_chunks));
+      const uint32_t col = tid % NCOL, grp = tid / NCOL;
+      const size_t hb = ((size_t)n * p.kv_heads + kvh) * p.max_chunks * G + g0;  // slot of chunk 0
+      const float4 *ob = reinterpret_cast<const float4 *>(p.apart + hb * D) + col;
+      auto row = [&](uint32_t c) { return __ldcg(ob + (size_t)c * G * NCOL); };
+      float4 v[MR];
+#pragma unroll
+      for (uint32_t i = 0; i < MR; ++i) {
+        const uint32_t c = grp + i * NGR;
+        v[i] = c < nch ? row(c) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      if (cw == 0) {
+        float M = -INFINITY;
+        for (uint32_t c = lane; c < nch; c += 32u) M = fmaxf(M, __ldcg(&p.apart_ml[hb + (size_t)c * G]).x);
+        M = warp_max(M);
+        float Ls = 0.f;
+        for (uint32_t c = lane; c < nch; c += 32u) {
+          const float2 m2 = __ldcg(&p.apart_ml[hb + (size_t)c * G]);
+          const float w = m2.x == -INFINITY ? 0.f : expf(m2.x - M);
+          sW[c] = w;
+          Ls = fmaf(w, m2.y, Ls);
+        }
+        Ls = warp_sum(Ls);
+        if (lane == 0) sW[p.max_chunks] = 1.0f / Ls;
+      }
+      named_bar(1, NCT);
+      float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+      auto acc = [&](uint32_t c, const float4 &r) {
+        const float w = sW[c];
+        o.x = fmaf(w, r.x, o.x);
+        o.y = fmaf(w, r.y, o.y);
+        o.z = fmaf(w, r.z, o.z);
+        o.w = fmaf(w, r.w, o.w);
+      };
+#pragma unroll
+      for (uint32_t i = 0; i < MR; ++i)
+        if (grp + i * NGR < nch) acc(grp + i * NGR, v[i]);
+      for (uint32_t c = grp + MR * NGR; c < nch; c += NGR) acc(c, row(c));
+      sO[grp * NCOL + col] = o;
+      named_bar(1, NCT);
+      if (tid < NCOL) {
+        float4 t = sO[tid];
+        for (uint32_t gi = 1; gi < NGR; ++gi) {
+          const float4 u2 = sO[gi * NCOL + tid];
+          t.x += u2.x;
+          t.y += u2.y;
+          t.z += u2.z;
+          t.w += u2.w;
+        }
+        const float inv = sW[p.max_chunks];
+        reinterpret_cast<float4 *>(p.attn + (size_t)n * p.H + ((size_t)kvh * G + g0) * D)[tid] =
+            make_float4(t.x * inv, t.y * inv, t.z * inv, t.w * inv);
+      }
+      named_bar(1, NCT);
+    }
+    arrive();
+  };
+
+  for (uint32_t ph = 0; ph < nb; ++ph) {
+    const uint32_t l = ph / kPhasesPerLayer, kind = ph - l * kPhasesPerLayer;
+    if (kind == kPhAttn) {
+      attention(ph, l);
+      continue;
+    }
+    matvec(kind == kPhQkv ? kBkQkv : kind == kPhO ? kBkO : kind == kPhGu ? kBkGu : kBkDown, ph, l);
+    arrive();
+  }
+
+  // final RMSNorm (rmsnorm.comp:21-42 with output_norm) of column blockIdx.x,
+  // into its stream's output when it is the stream's last column
+  if (blockIdx.x < S) {
+    wait_phase(nb);
+    const uint32_t n = blockIdx.x;
+    const float *h = p.hid_a + (size_t)n * p.H;
+    float ss = 0.f;
+    for (uint32_t i = tid; i < p.H; i += NCT) {
+      const float v = __ldcg(h + i);
+      ss += v * v;
+    }
+    ss = warp_sum(ss);
+    if (lane == 0) red[cw] = ss;
+    named_bar(1, NCT);
+    float tot = 0.f;
+#pragma unroll
+    for (int w = 0; w < kMvConsumers; ++w) tot += red[w];
+    const float inv_rms = 1.0f / sqrtf(tot / (float)p.H + p.eps);
+    if (scol[n].adv)
+      for (uint32_t i = tid; i < p.H; i += NCT)
+        scol[n].out[i] = __fmul_rn(__fmul_rn(__ldcg(h + i), inv_rms), p.out_norm[i]);
+  }
+  named_bar(1, NCT);
+  if (tid == 0) {
+    // this CTA's errors go to every stream of the launch
+    const uint32_t e = ld_volatile_u32(err);
+    if (e)
+      for (uint32_t n = 0; n < S; ++n) atomicOr(scol[n].ctrl + kCtrlErr, e);
+    // positions advance once every CTA has read them (they all passed the last barrier)
+    if (blockIdx.x == 0)
+      for (uint32_t n = 0; n < S; ++n)
+        if (scol[n].adv) scol[n].ctrl[kCtrlPos] = cff[n] + scol[n].adv;
+  }
+}
+}  // namespace vg

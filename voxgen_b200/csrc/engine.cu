@@ -32,7 +32,7 @@
 
 #include "../../include/voxgen_cuda.h"
 #include "gguf_loader.h"
-#include "step_kernel.cuh"
+#include "batch_kernel.cuh"
 
 using namespace vg;
 
@@ -253,6 +253,24 @@ AttnFn pick_attention(uint32_t head_dim) {
 
 }  // namespace
 
+// Plan and workspace of decode_batch_kernel (batch_kernel.cuh) for one model,
+// made at the first vg_decode_batch / vg_prefill_tokens that can use it.
+constexpr uint32_t kBatchStaging = 4;  // pinned slots of column tables in flight
+
+struct BatchWork {
+  std::string why;  // why the batched kernel is unavailable for this model ("": available)
+  BatchParams p{};
+  void (*fn)(BatchParams) = nullptr;
+  uint32_t smem = 0, grid = 0;
+  void *dev = nullptr;            // device workspace
+  uint8_t *pin = nullptr;         // kBatchStaging x (column table + control block)
+  size_t pin_stride = 0, table_bytes = 0;
+  cudaEvent_t pin_ev[kBatchStaging] = {};
+  uint32_t pin_next = 0;
+  cudaStream_t st = nullptr;      // every launch of the model's batched kernel goes here
+  cudaEvent_t ev_done = nullptr;
+};
+
 struct vg_model {
   vg_ctx *ctx = nullptr;
   BaseLmConfig cfg;
@@ -271,6 +289,10 @@ struct vg_model {
   AcousticConfig acoustic;
   DevMat fsq_in, fsq_out, fuse;  // [latent x H], [H x latent], [H x 2H]
   float *fsq_in_b = nullptr, *fsq_out_b = nullptr, *fuse_b = nullptr;
+  // workspace of the batched step kernel (vg_decode_batch, vg_prefill_tokens),
+  // made at first use; batch_mu serialises its use by host threads
+  BatchWork *batch = nullptr;
+  std::mutex batch_mu;
 };
 
 struct vg_stream {
@@ -305,6 +327,9 @@ struct vg_stream {
   // output (snapshot), and the three matvec plans of the per-kernel path
   float *res_base = nullptr, *fsq_lat = nullptr, *fsq_res = nullptr, *fuse_in = nullptr, *fused = nullptr;
   MvPlan fsq_in_p{}, fsq_out_p{}, fuse_p{};
+  // the LM head as its own launch on the output (logits after a batched prefill)
+  MvPlan head_plan{};
+  bool head_planned = false;
 };
 
 namespace {
@@ -960,6 +985,249 @@ void destroy_stream(vg_stream *s) {
   if (s->pin_out) cudaFreeHost(s->pin_out);
 }
 
+// ---- batched step kernel ---------------------------------------------------
+using BatchFn = void (*)(BatchParams);
+template <bool Q8>
+BatchFn pick_batch_dpl(uint32_t head_dim) {
+  switch (head_dim) {
+    case 32: return decode_batch_kernel<Q8, 1>;
+    case 64: return decode_batch_kernel<Q8, 2>;
+    case 128: return decode_batch_kernel<Q8, 4>;
+    case 256: return decode_batch_kernel<Q8, 8>;
+  }
+  return nullptr;
+}
+
+// Column groups of one matvec kind: the split with the smallest estimate of
+// the phase time, the heaviest CTA's weight bytes at its share of HBM
+// bandwidth plus the L2 traffic of operand slices (one read per row group)
+// and partial sums (written and read once per column group). A CTA's slice
+// must fit the operand region and span at most 8 segments.
+BatchSplit choose_split(const TileGeom &g, uint32_t S, uint32_t grid, uint32_t max_aux) {
+  const double sm_bw = 6.5e12 / grid, l2_bw = 10e12;  // B/s: HBM share of one SM; L2 (estimate)
+  BatchSplit best{0, 0};
+  double bc = 1e300;
+  for (uint32_t C = 1; C <= std::min(g.nseg(), grid); ++C) {
+    const uint32_t R = grid / C;
+    const uint32_t ns = (g.nseg() + C - 1) / C, nt = (g.tiles() + R - 1) / R;
+    if (ns > 8 || BatchOperand(ns * g.seg_cols()).total > max_aux) continue;
+    const double hbm = (double)nt * ns * g.seg_bytes() / sm_bw;
+    const double l2 = ((double)R * S * g.cols * 4.0 + (double)C * g.tiles() * 256.0 * 4.0 * 2.0) / l2_bw;
+    if (hbm + l2 < bc) {
+      bc = hbm + l2;
+      best = {C, R};
+    }
+  }
+  return best;
+}
+
+void destroy_batch(vg_model *m) {
+  BatchWork *w = m->batch;
+  if (!w) return;
+  if (w->st) cudaStreamSynchronize(w->st);
+  for (auto &e : w->pin_ev)
+    if (e) cudaEventDestroy(e);
+  if (w->ev_done) cudaEventDestroy(w->ev_done);
+  if (w->st) cudaStreamDestroy(w->st);
+  if (w->dev) cudaFree(w->dev);
+  if (w->pin) cudaFreeHost(w->pin);
+  delete w;
+  m->batch = nullptr;
+}
+
+// Plans the batched kernel for model m into w; returns "" or why it cannot run.
+std::string plan_batch(vg_model *m, BatchWork &w) {
+  const char *env = getenv("VOXGEN_BATCH_KERNEL");
+  if (env && env[0] == '0') return "disabled by VOXGEN_BATCH_KERNEL=0";
+  if (m->residual) return "a ResidualLM model";
+  const BaseLmConfig &c = m->cfg;
+  const uint32_t type = m->layers[0].qkv.type;
+  for (const Layer &L : m->layers)
+    for (const DevMat *d : {&L.qkv, &L.o, &L.gateup, &L.down})
+      if (d->type != type) return "the projections do not share one weight format";
+  const int dev = m->ctx->device;
+  int coop = 0;
+  CK(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, dev));
+  if (!coop) return "the device has no cooperative launch";
+  const uint32_t D = c.head_dim, G = c.head_count / c.head_count_kv, H = c.embedding_length;
+  if (c.head_count_kv > 8) return strf("%u KV heads (at most 8)", c.head_count_kv);
+  if (c.head_count * D != H) return "the query width differs from the hidden width";
+  w.fn = type == GGML_Q8_0 ? pick_batch_dpl<true>(D) : pick_batch_dpl<false>(D);
+  if (!w.fn) return strf("head_dim %u", D);
+  BatchParams &p = w.p;
+  p = BatchParams{};
+  const Layer &L0 = m->layers[0];
+  p.g[kBkQkv] = L0.qkv.g;
+  p.g[kBkO] = L0.o.g;
+  p.g[kBkGu] = L0.gateup.g;
+  p.g[kBkDown] = L0.down.g;
+  p.g_tok = m->tok.g;
+  p.n_layers = c.block_count;
+  uint32_t segb = 0, part_tiles = 0;
+  for (const TileGeom &g : p.g) {
+    if (g.cols % 4u) return strf("a matvec input of %u columns is not a whole number of 16-byte copies", g.cols);
+    segb = std::max(segb, g.seg_bytes());
+    part_tiles = std::max(part_tiles, g.tiles());
+  }
+  p.slot = kStageSegs * segb;
+  p.chunk = std::min<uint32_t>(64u, p.slot / (2u * D)) & ~15u;
+  if (p.chunk == 0) return strf("a stage slot of %u bytes holds no 16 rows of head_dim %u", p.slot, D);
+  p.max_chunks = (c.context_length + p.chunk - 1) / p.chunk;
+  const uint32_t grid = (uint32_t)m->ctx->sms;
+  if (grid > kBatchMaxRowGroups) return strf("%u SMs (the row-group counters cover %u)", grid, kBatchMaxRowGroups);
+  constexpr uint32_t kMaxAux = 72u * 1024u;  // operand region: leaves the ring 8 or more stages
+  uint32_t aux = step_attn_bytes(G, D, p.chunk, p.max_chunks), maxc = 1;
+  for (uint32_t k = 0; k < kBatchKinds; ++k) {
+    const TileGeom &g = p.g[k];
+    p.split[k] = choose_split(g, kBatchMaxCols, grid, kMaxAux);
+    if (p.split[k].C == 0) return strf("no split of a %u x %u matrix fits the operand region", g.rows, g.cols);
+    const uint32_t ns = (g.nseg() + p.split[k].C - 1) / p.split[k].C;
+    aux = std::max(aux, BatchOperand(ns * g.seg_cols()).total);
+    maxc = std::max(maxc, p.split[k].C);
+  }
+  p.aux_bytes = aux;
+  p.nst = 0;
+  const uint32_t fixed = BatchSmem(p).total;
+  if (fixed + 4u * (p.slot + 16u) > kSmemMax) return strf("shared-memory plan of %u bytes does not fit", fixed);
+  p.nst = std::min<uint32_t>(16u, (kSmemMax - fixed) / (p.slot + 16u));
+  w.smem = BatchSmem(p).total;
+  ensure_smem((const void *)w.fn, dev, w.smem);
+  int per_sm = 0;
+  CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, w.fn, kMvThreads, w.smem));
+  if (per_sm < 1) return strf("no CTA with %u bytes of shared memory fits on an SM", w.smem);
+  w.grid = grid;
+  // workspace
+  const uint32_t S = kBatchMaxCols, F = c.feed_forward_length, KVH = c.head_count_kv;
+  size_t off = 0;
+  auto take = [&](size_t b) {
+    size_t o = off;
+    off = round_up_sz(off + b, 256);
+    return o;
+  };
+  w.table_bytes = S * sizeof(BatchCol) + kCtrlWords * 4;
+  const size_t o_cols = take(w.table_bytes);
+  const size_t o_a = take((size_t)S * H * 4), o_b = take((size_t)S * H * 4), o_q = take((size_t)S * H * 4),
+               o_at = take((size_t)S * H * 4), o_g = take((size_t)S * F * 4),
+               o_part = take((size_t)maxc * part_tiles * 256 * 4), o_ssb = take((size_t)grid * S * 4),
+               o_ap = take((size_t)S * KVH * p.max_chunks * G * D * 4),
+               o_ml = take((size_t)S * KVH * p.max_chunks * G * 8), o_rdy = take((size_t)S * KVH * 8),
+               o_rgc = take((size_t)kBatchKinds * kBatchMaxRowGroups * 8), o_bar = take(8),
+               o_ly = take((size_t)c.block_count * sizeof(StepLayer));
+  CK(cudaMalloc(&w.dev, off));
+  CK(cudaMemset(w.dev, 0, off));
+  uint8_t *b = static_cast<uint8_t *>(w.dev);
+  p.cols = reinterpret_cast<const BatchCol *>(b + o_cols);
+  p.ctrl = reinterpret_cast<uint32_t *>(b + o_cols + S * sizeof(BatchCol));
+  p.hid_a = (float *)(b + o_a);
+  p.hid_b = (float *)(b + o_b);
+  p.q = (float *)(b + o_q);
+  p.attn = (float *)(b + o_at);
+  p.gate = (float *)(b + o_g);
+  p.part = (float *)(b + o_part);
+  p.part_tiles = part_tiles;
+  p.ssb = (float *)(b + o_ssb);
+  p.apart = (float *)(b + o_ap);
+  p.apart_ml = (float2 *)(b + o_ml);
+  p.ready = (unsigned long long *)(b + o_rdy);
+  p.rgc = (unsigned long long *)(b + o_rgc);
+  p.bar = (unsigned long long *)(b + o_bar);
+  std::vector<StepLayer> tab(c.block_count);
+  for (uint32_t l = 0; l < c.block_count; ++l) {
+    const Layer &L = m->layers[l];
+    tab[l] = StepLayer{L.qkv.w, L.o.w, L.gateup.w, L.down.w, L.attn_norm, L.ffn_norm, nullptr, nullptr};
+  }
+  CK(cudaMemcpy(b + o_ly, tab.data(), tab.size() * sizeof(StepLayer), cudaMemcpyHostToDevice));
+  p.layers = (const StepLayer *)(b + o_ly);
+  p.tok = m->tok.w;
+  p.out_norm = m->out_norm;
+  p.inv_freq = m->inv_freq;
+  p.ext = m->ext;
+  p.rope_scaling = c.rope_scaling_factor();
+  p.eps = c.rms_epsilon;
+  p.res_scale = eff_scale(c.residual_scale);
+  p.emb_scale = eff_scale(c.embedding_scale);
+  p.attn_scale = 1.0f / sqrtf((float)D);
+  p.H = H;
+  p.F = F;
+  p.heads = c.head_count;
+  p.kv_heads = KVH;
+  p.head_dim = D;
+  CK(cudaStreamCreateWithFlags(&w.st, cudaStreamNonBlocking));
+  CK(cudaEventCreateWithFlags(&w.ev_done, cudaEventDisableTiming));
+  w.pin_stride = round_up_sz(w.table_bytes, 256);
+  CK(cudaMallocHost(&w.pin, w.pin_stride * kBatchStaging));
+  for (auto &e : w.pin_ev) {
+    CK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+    CK(cudaEventRecord(e, w.st));
+  }
+  CK(cudaStreamSynchronize(w.st));
+  return "";
+}
+
+// The model's batch plan, made at first use (caller holds m->batch_mu).
+BatchWork *get_batch(vg_model *m) {
+  if (!m->batch) {
+    m->batch = new BatchWork();
+    try {
+      m->batch->why = plan_batch(m, *m->batch);
+    } catch (...) {
+      destroy_batch(m);
+      throw;
+    }
+  }
+  return m->batch;
+}
+
+BatchCol batch_col(const vg_stream *s, uint32_t off, uint32_t adv, uint32_t token) {
+  const BaseLmConfig &c = s->m->cfg;
+  BatchCol col{};
+  col.kc = s->kc;
+  col.vc = s->vc;
+  col.layer_elems = (unsigned long long)c.head_count_kv * s->max_ctx * c.head_dim;
+  col.ctrl = s->ctrl;
+  col.out = s->out_norm;
+  col.ctx = s->max_ctx;
+  col.off = off;
+  col.adv = adv;
+  col.token = token;
+  return col;
+}
+
+// One launch of the batched kernel over cols (caller holds m->batch_mu),
+// ordered after the work already enqueued on every stream involved and
+// before their later work. The column table and a clean control block travel
+// with the launch.
+void batch_launch(BatchWork &w, const std::vector<BatchCol> &cols, const std::vector<vg_stream *> &streams) {
+  const uint32_t i = w.pin_next;
+  w.pin_next = (w.pin_next + 1) % kBatchStaging;
+  int rc = host_wait(w.pin_ev[i], 10ull * 1000000000ull);
+  if (rc) fail(rc, "timed out waiting for a batch staging buffer");
+  uint8_t *slot = w.pin + (size_t)i * w.pin_stride;
+  std::memset(slot, 0, w.table_bytes);
+  std::memcpy(slot, cols.data(), cols.size() * sizeof(BatchCol));
+  for (vg_stream *s : streams) {
+    CK(cudaEventRecord(s->ev_done, s->st));
+    CK(cudaStreamWaitEvent(w.st, s->ev_done, 0));
+  }
+  CK(cudaMemcpyAsync((void *)w.p.cols, slot, w.table_bytes, cudaMemcpyHostToDevice, w.st));
+  CK(cudaEventRecord(w.pin_ev[i], w.st));
+  BatchParams p = w.p;
+  p.S = (uint32_t)cols.size();
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(w.grid);
+  cfg.blockDim = dim3(kMvThreads);
+  cfg.dynamicSmemBytes = w.smem;
+  cfg.stream = w.st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeCooperative;
+  at[0].val.cooperative = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  CK(cudaLaunchKernelEx(&cfg, w.fn, p));
+  CK(cudaEventRecord(w.ev_done, w.st));
+  for (vg_stream *s : streams) CK(cudaStreamWaitEvent(s->st, w.ev_done, 0));
+}
+
 }  // namespace
 
 // ===========================================================================
@@ -1107,6 +1375,7 @@ int vg_model_destroy(vg_model *m) {
   }
   live_del(m);
   cudaSetDevice(m->ctx->device);
+  destroy_batch(m);
   if (m->arena) cudaFree(m->arena);
   delete m;
   return VG_OK;
@@ -1571,11 +1840,69 @@ int vg_prefill_tokens(vg_stream *s, const uint32_t *tokens, uint32_t n, int want
     return VG_EINVAL;
   }
   if (!tokens) return VG_EINVAL;
+  vg_model *m = s->m;
+  bool batched = false;
+  int rc = guard(m->ctx, [&] {
+    for (uint32_t i = 0; i < n; ++i)
+      if (tokens[i] >= m->cfg.vocab_size)
+        fail(VG_ERANGE, strf("token id %u is outside vocabulary 0..%u", tokens[i], m->cfg.vocab_size));
+    check_step(s);
+    if ((uint64_t)s->pos + n > s->max_ctx)
+      fail(VG_EFULL, strf("BaseLM KV cache is full at %u tokens; reset or increase --max-context", s->max_ctx));
+    if (want_logits_last && m->cfg.vocab_size == 0) fail(VG_EUNSUPPORTED, "this model has no LM head");
+    if (n < 2 || !s->use_step) return VG_OK;
+    CK(cudaSetDevice(m->ctx->device));
+    std::lock_guard<std::mutex> lk(m->batch_mu);
+    BatchWork *w = get_batch(m);
+    if (!w->why.empty()) return VG_OK;
+    // runs of up to 16 consecutive positions, one weight pass each
+    for (uint32_t i0 = 0; i0 < n; i0 += kBatchMaxCols) {
+      const uint32_t k = std::min<uint32_t>(kBatchMaxCols, n - i0);
+      std::vector<BatchCol> cols;
+      for (uint32_t j = 0; j < k; ++j) cols.push_back(batch_col(s, j, j + 1 == k ? k : 0u, tokens[i0 + j]));
+      batch_launch(*w, cols, {s});
+      s->pos += k;
+    }
+    if (want_logits_last) {
+      if (!s->head_planned) {
+        if (s->step_head_apart) {
+          s->head_plan = s->step_head;
+        } else {
+          s->head_plan = plan_matvec<Mode::PLAIN, Pro::COPY>(m->out, m->ctx->device, (uint32_t)m->ctx->sms);
+          s->head_plan.p.xsrc = s->out_norm;
+          s->head_plan.p.out = s->logits;
+          s->head_plan.p.alpha = eff_scale(m->cfg.logit_scale);
+          s->head_plan.p.ctrl = s->ctrl;
+        }
+        s->head_planned = true;
+      }
+      CK(run_matvec(s->head_plan, s->st, false));
+    }
+    s->logits_valid = want_logits_last != 0;
+    batched = true;
+    return VG_OK;
+  });
+  if (rc || batched) return rc;
+  // one decode step per token: a stream on the per-kernel program, a model the
+  // batched kernel does not take, or a single token
   for (uint32_t i = 0; i < n; ++i) {
-    int rc = vg_decode_token(s, tokens[i], (i + 1 == n) ? want_logits_last : 0);
+    rc = vg_decode_token(s, tokens[i], (i + 1 == n) ? want_logits_last : 0);
     if (rc) return rc;
   }
   return VG_OK;
+}
+
+int vg_model_batch_columns(vg_model *m, uint32_t *max_columns) {
+  if (!live(m)) return VG_ESTATE;
+  if (!max_columns) return VG_EINVAL;
+  return guard(m->ctx, [&] {
+    CK(cudaSetDevice(m->ctx->device));
+    std::lock_guard<std::mutex> lk(m->batch_mu);
+    BatchWork *w = get_batch(m);
+    *max_columns = w->why.empty() ? kBatchMaxCols : 0u;
+    if (!w->why.empty()) set_err(m->ctx, "batched step kernel unavailable: " + w->why);
+    return VG_OK;
+  });
 }
 
 int vg_stream_output(const vg_stream *s, const float **dev) {
@@ -1772,6 +2099,27 @@ int vg_decode_batch(vg_stream *const *streams, int n, const uint32_t *tokens) {
       check_step(s);
     }
     CK(cudaSetDevice(m->ctx->device));
+    bool all_step = n >= 2;
+    for (int i = 0; i < n; ++i) all_step = all_step && streams[i]->use_step;
+    if (all_step) {
+      // one launch of the batched kernel: one weight pass for every stream
+      std::lock_guard<std::mutex> lk(m->batch_mu);
+      BatchWork *w = get_batch(m);
+      if (w->why.empty()) {
+        std::vector<BatchCol> cols;
+        std::vector<vg_stream *> ss;
+        for (int i = 0; i < n; ++i) {
+          cols.push_back(batch_col(streams[i], 0u, 1u, tokens[i]));
+          ss.push_back(streams[i]);
+        }
+        batch_launch(*w, cols, ss);
+        for (vg_stream *s : ss) {
+          s->pos += 1;
+          s->logits_valid = false;
+        }
+        return VG_OK;
+      }
+    }
     // one step per stream, each on its own CUDA stream (the weights are read once per stream)
     for (int i = 0; i < n; ++i) {
       vg_stream *s = streams[i];
