@@ -103,17 +103,23 @@ struct BatchSmem {
   }
 };
 
+// Bytes of the warps' partial sums of one group of 4 tiles: [warp][tile][16 rows][16 columns].
+constexpr uint32_t kBatchRedBytes = kMvConsumers * 4u * 256u * 4u;
+
 // Matvec operand region of the aux area for a K-slice of kc elements:
 // hi plane, lo plane (each 16 columns x kc fp16), the staged fp32 input
-// [16][kc], the staged norm weight [kc], then per column 2^e and the sum of
-// squares of the slice.
+// [16][kc] (after the prologue the same bytes hold the warps' partial sums,
+// so the region is at least kBatchRedBytes), the staged norm weight [kc],
+// then per column 2^e and the sum of squares of the slice.
 struct BatchOperand {
-  uint32_t hi, lo, stg, stw, colv, total;
+  uint32_t hi, lo, stg, red, stw, colv, total;
   __host__ __device__ BatchOperand(uint32_t kc) {
     hi = 0;
     lo = hi + kc * kBatchMaxCols * 2u;
     stg = lo + kc * kBatchMaxCols * 2u;
-    stw = stg + kc * kBatchMaxCols * 4u;
+    red = stg;
+    const uint32_t sb = kc * kBatchMaxCols * 4u;
+    stw = stg + (sb > kBatchRedBytes ? sb : kBatchRedBytes);
     colv = stw + kc * 4u;
     total = colv + 2u * kBatchMaxCols * 4u;
   }
@@ -252,7 +258,11 @@ __device__ __forceinline__ BatchRun batch_run(const TileGeom &g, const BatchSpli
   b.ns = NS * (b.c + 1u) / sp.C - b.s0;
   return b;
 }
-__device__ __forceinline__ uint32_t batch_stages(const BatchRun &b) { return (b.nt * b.ns + kStageSegs - 1u) / kStageSegs; }
+// Tile groups of a run: groups of 4 consecutive tiles (the last may hold fewer),
+// each streamed segment by segment. A stage is one group's tiles at one
+// segment, so the phase has groups x ns stages.
+__device__ __forceinline__ uint32_t batch_groups(const BatchRun &b) { return (b.nt + 3u) / 4u; }
+__device__ __forceinline__ uint32_t batch_stages(const BatchRun &b) { return batch_groups(b) * b.ns; }
 
 // Ring stage k stages after rp: slot and the parity of that use.
 __device__ __forceinline__ void ring_at(const RingPos &rp, uint32_t k, uint32_t nst, uint32_t &slot, uint32_t &par) {
@@ -261,70 +271,45 @@ __device__ __forceinline__ void ring_at(const RingPos &rp, uint32_t k, uint32_t 
   par = rp.phase ^ ((s / nst) & 1u);
 }
 
-// Producer side of a batched matvec: the CTA's items (tile, segment), tile
-// by tile, kStageSegs per stage; a stage is one bulk copy per tile it spans
-// (a tile's segments of one column group are contiguous in HBM).
+// Producer side of a batched matvec: for every group of up to 4 tiles and
+// every segment of the slice, one stage holding that segment of each tile of
+// the group (one bulk copy per tile).
 __device__ __forceinline__ bool batch_produce(const MvRing &R, const uint8_t *w, const TileGeom &g, const BatchRun &b,
                                               RingPos &rp, const uint32_t *abort_flag, uint32_t *err) {
-  const uint32_t SEGB = g.seg_bytes(), NS = g.nseg(), n_items = b.nt * b.ns;
-  for (uint32_t i0 = 0; i0 < n_items; i0 += kStageSegs) {
-    const uint32_t n = min(kStageSegs, n_items - i0);
-    if (!ring_claim(R, rp, n * SEGB, abort_flag, err)) return false;
-    uint8_t *dst = R.ring + rp.slot * R.slot;
-    for (uint32_t i = i0; i < i0 + n;) {
-      const uint32_t t = i / b.ns, s = i - t * b.ns;
-      const uint32_t run = min(i0 + n - i, b.ns - s);
-      bulk_g2s(dst + (i - i0) * SEGB, w + ((uint64_t)(b.t0 + t) * NS + b.s0 + s) * SEGB, run * SEGB, &R.full[rp.slot]);
-      i += run;
+  const uint32_t SEGB = g.seg_bytes(), NS = g.nseg();
+  for (uint32_t q = 0; q < batch_groups(b); ++q) {
+    const uint32_t nq = min(4u, b.nt - 4u * q);
+    for (uint32_t sgi = 0; sgi < b.ns; ++sgi) {
+      if (!ring_claim(R, rp, nq * SEGB, abort_flag, err)) return false;
+      uint8_t *dst = R.ring + rp.slot * R.slot;
+      for (uint32_t j = 0; j < nq; ++j)
+        bulk_g2s(dst + j * SEGB, w + ((uint64_t)(b.t0 + 4u * q + j) * NS + b.s0 + sgi) * SEGB, SEGB, &R.full[rp.slot]);
+      rp.next(R.nst);
     }
-    rp.next(R.nst);
   }
   return true;
 }
 
-// Consumer side of a batched matvec, one warp: it owns the contiguous group of
-// tiles [nt * cw / 8, nt * (cw + 1) / 8) of the CTA's run and takes them up to
-// TB at a time, every K-step of its slice, the B fragments loaded once per
-// K-step for all of them. Partial sums (times each column's 2^e) go to
-// part[c][tile][row][column]. Every warp waits for and releases every stage
-// of the phase exactly once, in order (the empty barriers count 8 arrivals);
-// a batch spans at most 8 items, i.e. 3 stages, fewer than the ring holds.
+// Consumer side of a batched matvec. Every warp takes every stage: warp cw
+// does K-step cw of the stage's segment for each of its (up to 4) tiles, the
+// B fragments loaded once for all of them, and accumulates over the group's
+// segments. After a group the warps' sums go to shared memory (red), and the
+// CTA adds them in warp order, times each column's 2^e, into
+// part[c][tile][row][column].
 template <bool Q8>
-__device__ __forceinline__ void batch_consume(const MvRing &R, const RingPos &rp0, const BatchRun &b,
-                                              const TileGeom &g, const uint8_t *aux, const BatchOperand &O,
-                                              uint32_t S, float *part, uint32_t part_tiles, uint32_t cw, uint32_t lane,
+__device__ __forceinline__ void batch_consume(const MvRing &R, RingPos &rp, const BatchRun &b, const TileGeom &g,
+                                              uint8_t *aux, const BatchOperand &O, uint32_t S, float *part,
+                                              uint32_t part_tiles, uint32_t cw, uint32_t lane,
                                               const uint32_t *abort_flag, uint32_t *err, bool &ok) {
-  const uint32_t SEGB = g.seg_bytes(), n_items = b.nt * b.ns, nstg = batch_stages(b);
-  const uint32_t g0 = b.nt * cw / kMvConsumers, g1 = b.nt * (cw + 1u) / kMvConsumers;
-  const uint32_t TB = max(1u, min(4u, 8u / max(b.ns, 1u)));
+  constexpr uint32_t NCT = kMvConsumers * 32;
+  const uint32_t SEGB = g.seg_bytes(), tid = cw * 32u + lane;
   const uint32_t gq = lane >> 2, tq = lane & 3u;
   const bool two = S > 8u;  // the second n8 tile (columns 8-15) carries live columns
   const float *colv = reinterpret_cast<const float *>(aux + O.colv);
-  const float sc[4] = {colv[2u * tq], colv[2u * tq + 1u], colv[8u + 2u * tq], colv[9u + 2u * tq]};
   const uint8_t *hi = aux + O.hi, *lo = aux + O.lo;
-  auto wait_full = [&](uint32_t k) {
-    uint32_t sl, par;
-    ring_at(rp0, k, R.nst, sl, par);
-    if (!mbar_wait_bounded(&R.full[sl], par, abort_flag)) {
-      set_error(err, kErrConsumerWait);
-      ok = false;
-    }
-  };
-  auto release = [&](uint32_t k) {
-    uint32_t sl, par;
-    ring_at(rp0, k, R.nst, sl, par);
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&R.empty[sl]);
-  };
-  uint32_t next = 0;  // first stage this warp has not released
-  for (uint32_t tb = g0; tb < g1; tb += TB) {
-    const uint32_t te = min(tb + TB, g1), nb = te - tb;
-    const uint32_t sa = tb * b.ns / kStageSegs, sb = (te * b.ns - 1u) / kStageSegs;
-    for (; next < sa; ++next) {
-      wait_full(next);
-      release(next);
-    }
-    for (uint32_t k = next; k <= sb; ++k) wait_full(k);
+  float *red = reinterpret_cast<float *>(aux + O.red);
+  for (uint32_t q = 0; q < batch_groups(b); ++q) {
+    const uint32_t nq = min(4u, b.nt - 4u * q);
     float tot[4][2][4];
 #pragma unroll
     for (int j = 0; j < 4; ++j)
@@ -333,105 +318,100 @@ __device__ __forceinline__ void batch_consume(const MvRing &R, const RingPos &rp
 #pragma unroll
         for (int i = 0; i < 4; ++i) tot[j][nt][i] = 0.f;
 #pragma unroll 1
-    for (uint32_t seg = 0; seg < b.ns; ++seg) {
-      const uint8_t *sg[4];
-#pragma unroll
-      for (uint32_t j = 0; j < 4; ++j) {
-        const uint32_t item = (tb + min(j, nb - 1u)) * b.ns + seg;
-        uint32_t sl, par;
-        ring_at(rp0, item / kStageSegs, R.nst, sl, par);
-        sg[j] = R.ring + sl * R.slot + (item % kStageSegs) * SEGB;
+    for (uint32_t sgi = 0; sgi < b.ns; ++sgi) {
+      if (!mbar_wait_bounded(&R.full[rp.slot], rp.phase, abort_flag)) {
+        set_error(err, kErrConsumerWait);
+        ok = false;
       }
-#pragma unroll 2
-      for (uint32_t q = 0; q < kSegSteps; ++q) {
-        const uint32_t kk = seg * kSegSteps + q;  // K-step within the slice
-        if constexpr (Q8) {
-          const uint32_t bo = ((kk * kBatchMaxCols + gq) * 4u + tq) * 16u;
-          const uint4 bh0 = *reinterpret_cast<const uint4 *>(hi + bo), bl0 = *reinterpret_cast<const uint4 *>(lo + bo);
-          uint4 bh1 = make_uint4(0u, 0u, 0u, 0u), bl1 = bh1;
-          if (two) {
-            bh1 = *reinterpret_cast<const uint4 *>(hi + bo + 8u * 64u);
-            bl1 = *reinterpret_cast<const uint4 *>(lo + bo + 8u * 64u);
-          }
+      const uint8_t *st = R.ring + rp.slot * R.slot;
+      const uint32_t kk = sgi * kSegSteps + cw;  // K-step within the slice
+      if constexpr (Q8) {
+        const uint32_t bo = ((kk * kBatchMaxCols + gq) * 4u + tq) * 16u;
+        const uint4 bh0 = *reinterpret_cast<const uint4 *>(hi + bo), bl0 = *reinterpret_cast<const uint4 *>(lo + bo);
+        uint4 bh1 = make_uint4(0u, 0u, 0u, 0u), bl1 = bh1;
+        if (two) {
+          bh1 = *reinterpret_cast<const uint4 *>(hi + bo + 8u * 64u);
+          bl1 = *reinterpret_cast<const uint4 *>(lo + bo + 8u * 64u);
+        }
 #pragma unroll
-          for (uint32_t j = 0; j < 4; ++j) {
-            if (j >= nb) break;
-            uint32_t a[4], A1[4], A2[4];
-            ldmatrix_x4(a, sg[j] + q * kStepBytes + lane * 16u);
-            i8x4_to_h2x2(a[0], A1[0], A1[2]);
-            i8x4_to_h2x2(a[1], A1[1], A1[3]);
-            i8x4_to_h2x2(a[2], A2[0], A2[2]);
-            i8x4_to_h2x2(a[3], A2[1], A2[3]);
-            const float2 d = __half22float2(*reinterpret_cast<const __half2 *>(sg[j] + kSegQsBytes + gq * 32u + q * 4u));
-            float c[4];
-            mma_f16_zero(c, A1, bh0.x, bh0.y);
-            mma_f16(c, A1, bl0.x, bl0.y);
-            mma_f16(c, A2, bh0.z, bh0.w);
-            mma_f16(c, A2, bl0.z, bl0.w);
-            tot[j][0][0] = fmaf(c[0], d.x, tot[j][0][0]);
-            tot[j][0][1] = fmaf(c[1], d.x, tot[j][0][1]);
-            tot[j][0][2] = fmaf(c[2], d.y, tot[j][0][2]);
-            tot[j][0][3] = fmaf(c[3], d.y, tot[j][0][3]);
-            if (two) {
-              mma_f16_zero(c, A1, bh1.x, bh1.y);
-              mma_f16(c, A1, bl1.x, bl1.y);
-              mma_f16(c, A2, bh1.z, bh1.w);
-              mma_f16(c, A2, bl1.z, bl1.w);
-              tot[j][1][0] = fmaf(c[0], d.x, tot[j][1][0]);
-              tot[j][1][1] = fmaf(c[1], d.x, tot[j][1][1]);
-              tot[j][1][2] = fmaf(c[2], d.y, tot[j][1][2]);
-              tot[j][1][3] = fmaf(c[3], d.y, tot[j][1][3]);
-            }
-          }
-        } else {
-          const uint32_t bo = ((kk * kBatchMaxCols + gq) * 4u + tq) * 8u;
-          const uint2 bh0 = *reinterpret_cast<const uint2 *>(hi + bo), bl0 = *reinterpret_cast<const uint2 *>(lo + bo);
-          uint2 bh1 = make_uint2(0u, 0u), bl1 = bh1;
+        for (uint32_t j = 0; j < 4; ++j) {
+          if (j >= nq) break;
+          const uint8_t *sg = st + j * SEGB;
+          uint32_t a[4], A1[4], A2[4];
+          ldmatrix_x4(a, sg + cw * kStepBytes + lane * 16u);
+          i8x4_to_h2x2(a[0], A1[0], A1[2]);
+          i8x4_to_h2x2(a[1], A1[1], A1[3]);
+          i8x4_to_h2x2(a[2], A2[0], A2[2]);
+          i8x4_to_h2x2(a[3], A2[1], A2[3]);
+          const float2 d = __half22float2(*reinterpret_cast<const __half2 *>(sg + kSegQsBytes + gq * 32u + cw * 4u));
+          float c[4];
+          mma_f16_zero(c, A1, bh0.x, bh0.y);
+          mma_f16(c, A1, bl0.x, bl0.y);
+          mma_f16(c, A2, bh0.z, bh0.w);
+          mma_f16(c, A2, bl0.z, bl0.w);
+          tot[j][0][0] = fmaf(c[0], d.x, tot[j][0][0]);
+          tot[j][0][1] = fmaf(c[1], d.x, tot[j][0][1]);
+          tot[j][0][2] = fmaf(c[2], d.y, tot[j][0][2]);
+          tot[j][0][3] = fmaf(c[3], d.y, tot[j][0][3]);
           if (two) {
-            bh1 = *reinterpret_cast<const uint2 *>(hi + bo + 8u * 32u);
-            bl1 = *reinterpret_cast<const uint2 *>(lo + bo + 8u * 32u);
+            mma_f16_zero(c, A1, bh1.x, bh1.y);
+            mma_f16(c, A1, bl1.x, bl1.y);
+            mma_f16(c, A2, bh1.z, bh1.w);
+            mma_f16(c, A2, bl1.z, bl1.w);
+            tot[j][1][0] = fmaf(c[0], d.x, tot[j][1][0]);
+            tot[j][1][1] = fmaf(c[1], d.x, tot[j][1][1]);
+            tot[j][1][2] = fmaf(c[2], d.y, tot[j][1][2]);
+            tot[j][1][3] = fmaf(c[3], d.y, tot[j][1][3]);
           }
+        }
+      } else {
+        const uint32_t bo = ((kk * kBatchMaxCols + gq) * 4u + tq) * 8u;
+        const uint2 bh0 = *reinterpret_cast<const uint2 *>(hi + bo), bl0 = *reinterpret_cast<const uint2 *>(lo + bo);
+        uint2 bh1 = make_uint2(0u, 0u), bl1 = bh1;
+        if (two) {
+          bh1 = *reinterpret_cast<const uint2 *>(hi + bo + 8u * 32u);
+          bl1 = *reinterpret_cast<const uint2 *>(lo + bo + 8u * 32u);
+        }
 #pragma unroll
-          for (uint32_t j = 0; j < 4; ++j) {
-            if (j >= nb) break;
-            uint32_t a[4];
-            ldmatrix_x4(a, sg[j] + q * kStepBytes + lane * 16u);
-            mma_f16(tot[j][0], a, bh0.x, bh0.y);
-            mma_f16(tot[j][0], a, bl0.x, bl0.y);
-            if (two) {
-              mma_f16(tot[j][1], a, bh1.x, bh1.y);
-              mma_f16(tot[j][1], a, bl1.x, bl1.y);
-            }
+        for (uint32_t j = 0; j < 4; ++j) {
+          if (j >= nq) break;
+          uint32_t a[4];
+          ldmatrix_x4(a, st + j * SEGB + cw * kStepBytes + lane * 16u);
+          mma_f16(tot[j][0], a, bh0.x, bh0.y);
+          mma_f16(tot[j][0], a, bl0.x, bl0.y);
+          if (two) {
+            mma_f16(tot[j][1], a, bh1.x, bh1.y);
+            mma_f16(tot[j][1], a, bl1.x, bl1.y);
           }
         }
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&R.empty[rp.slot]);
+      rp.next(R.nst);
     }
-    // partial sums of the batch's tiles; lane (gq, tq) holds rows gq, gq + 8 and
-    // columns 8 nt + 2 tq, 8 nt + 2 tq + 1
+    // the warps' sums of the group: red[warp][tile][row][column]; lane (gq, tq)
+    // holds rows gq, gq + 8 and columns 8 nt + 2 tq, 8 nt + 2 tq + 1
 #pragma unroll
     for (uint32_t j = 0; j < 4; ++j) {
-      if (j >= nb) break;
-      float *pt = part + ((size_t)b.c * part_tiles + b.t0 + tb + j) * 256u;
+      if (j >= nq) break;
+      float *rt = red + (cw * 4u + j) * 256u;
 #pragma unroll
       for (uint32_t nt = 0; nt < 2; ++nt) {
-        if (nt == 1 && !two) break;
         const uint32_t col = nt * 8u + 2u * tq;
-        *reinterpret_cast<float2 *>(pt + gq * 16u + col) =
-            make_float2(tot[j][nt][0] * sc[2u * nt], tot[j][nt][1] * sc[2u * nt + 1u]);
-        *reinterpret_cast<float2 *>(pt + (gq + 8u) * 16u + col) =
-            make_float2(tot[j][nt][2] * sc[2u * nt], tot[j][nt][3] * sc[2u * nt + 1u]);
+        *reinterpret_cast<float2 *>(rt + gq * 16u + col) = make_float2(tot[j][nt][0], tot[j][nt][1]);
+        *reinterpret_cast<float2 *>(rt + (gq + 8u) * 16u + col) = make_float2(tot[j][nt][2], tot[j][nt][3]);
       }
     }
-    // stages done: all up to sb when this was the warp's last batch, else those
-    // before the stage its next batch starts in
-    const uint32_t done = te == g1 ? sb + 1u : te * b.ns / kStageSegs;
-    for (; next < done; ++next) release(next);
+    named_bar(1, NCT);
+    for (uint32_t v = tid; v < nq * 256u; v += NCT) {
+      const uint32_t j = v >> 8, e = v & 255u;
+      float a = 0.f;
+#pragma unroll
+      for (uint32_t w = 0; w < kMvConsumers; ++w) a += red[(w * 4u + j) * 256u + e];
+      part[((size_t)b.c * part_tiles + b.t0 + 4u * q + j) * 256u + e] = a * colv[e & 15u];
+    }
+    named_bar(1, NCT);  // red reuse
   }
-  for (; next < nstg; ++next) {
-    wait_full(next);
-    release(next);
-  }
-  (void)n_items;
 }
 
 // Reduction of a row group's partials and the epilogue, after the C CTAs of
@@ -456,6 +436,15 @@ __device__ __forceinline__ void batch_reduce(const BatchRun &b, uint32_t C, cons
 }
 
 enum : uint32_t { kBkQkv = 0, kBkO = 1, kBkGu = 2, kBkDown = 3 };
+
+// aux bytes of an attention phase: every warp's P of its unit (hi and lo,
+// [8 heads][chunk] fp16), or a merge slice's chunk weights [max_chunks][8]
+// followed by [32][8] partial maxima / sums (also [2][128] output halves).
+__host__ __device__ inline uint32_t batch_attn_bytes(uint32_t chunk, uint32_t max_chunks) {
+  const uint32_t units = kMvConsumers * 2u * 8u * chunk * 2u;
+  const uint32_t merge = (max_chunks * 8u + 8u + kMvConsumers * 32u * 4u) * 4u;
+  return units > merge ? units : merge;
+}
 
 // Attention unit u of a batched step: units are ordered by column, KV head,
 // chunk; cu0 holds each column's first unit.
@@ -570,23 +559,33 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_batch_kernel(const __gri
     if (lane == 0) {
       RingPos rp;
       bool live = true;
-      auto rows = [&](const __half *src, uint32_t n) {  // one stage of n cached K or V rows
-        if (!live) return;
-        live = ring_claim(R, rp, n * D * 2u, err, err);
-        if (!live) return;
-        if (n) bulk_g2s(R.ring + rp.slot * R.slot, src, n * D * 2u, &R.full[rp.slot]);
-        rp.next(R.nst);
-      };
       for (uint32_t ph = 0; ph < nb && live; ++ph) {
         const uint32_t l = ph / kPhasesPerLayer, kind = ph - l * kPhasesPerLayer;
         const StepLayer &Ly = layers[l];
         if (kind == kPhAttn) {
-          for (uint32_t u = blockIdx.x; u < n_units; u += gridDim.x) {
-            const BatchUnit a = batch_unit(u, cu0, cnch, cpos, cff, S, p.chunk);
-            const BatchCol &cl = scol[a.n];
-            const size_t off = (size_t)l * cl.layer_elems + ((size_t)a.kvh * cl.ctx + a.r0) * D;
-            rows(cl.kc + off, a.staged);
-            rows(cl.vc + off, a.staged);
+          // one stage per unit of this CTA: its cached K rows, then its V rows
+          for (uint32_t i = 0; live; ++i) {
+            bool more = true;
+            for (uint32_t w = 0; w < kMvConsumers && live; ++w) {
+              const uint32_t u = (i * gridDim.x + blockIdx.x) * kMvConsumers + w;
+              if (u >= n_units) {
+                more = false;
+                break;
+              }
+              const BatchUnit a = batch_unit(u, cu0, cnch, cpos, cff, S, p.chunk);
+              const BatchCol &cl = scol[a.n];
+              const size_t off = (size_t)l * cl.layer_elems + ((size_t)a.kvh * cl.ctx + a.r0) * D;
+              const uint32_t bytes = a.staged * D * 2u;
+              live = ring_claim(R, rp, 2u * bytes, err, err);
+              if (!live) break;
+              if (bytes) {
+                uint8_t *dst = R.ring + rp.slot * R.slot;
+                bulk_g2s(dst, cl.kc + off, bytes, &R.full[rp.slot]);
+                bulk_g2s(dst + p.chunk * D * 2u, cl.vc + off, bytes, &R.full[rp.slot]);
+              }
+              rp.next(R.nst);
+            }
+            if (!more) break;
           }
           continue;
         }
@@ -689,11 +688,11 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_batch_kernel(const __gri
       if (tid < kBatchMaxCols) p.ssb[(b.r * sp.C + b.c) * kBatchMaxCols + tid] =
           reinterpret_cast<const float *>(aux + O.colv)[kBatchMaxCols + tid];
       batch_consume<Q8>(R, rp, b, g, aux, O, S, p.part, p.part_tiles, cw, lane, err, err, ok);
-      // every partial of the CTA is written: one arrival at the row group
+      // every partial (and the slice's sums of squares) of the CTA is written:
+      // one arrival at the row group
       named_bar(1, NCT);
       if (tid == 0) grid_arrive(p.rgc + k * kBatchMaxRowGroups + b.r);
     }
-    for (uint32_t i = 0; i < batch_stages(b); ++i) rp.next(R.nst);
     if (!b.live) return;
     // wait for the C CTAs of the row group, then reduce this CTA's share
     if (tid == 0 && !grid_wait(p.rgc + k * kBatchMaxRowGroups + b.r,
@@ -728,14 +727,14 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_batch_kernel(const __gri
             p.q[(size_t)n * H + head * D + i + hd] = c2;
           } else {
             __half *dst = cl.kc + (size_t)l * cl.layer_elems + ((size_t)head * cl.ctx + pos) * D;
-            dst[i] = __float2half_rn(a);
-            dst[i + hd] = __float2half_rn(c2);
+            dst[kv_swz(pos, i, D)] = __float2half_rn(a);
+            dst[kv_swz(pos, i + hd, D)] = __float2half_rn(c2);
           }
         } else {
           const uint32_t v = R0 - H - KV, kvh = v / D, j = v % D;
           __half *dst = cl.vc + (size_t)l * cl.layer_elems + ((size_t)kvh * cl.ctx + pos) * D;
-          dst[j] = __float2half_rn(a);
-          dst[j + 8u] = __float2half_rn(c2);
+          dst[kv_swz(pos, j, D)] = __float2half_rn(a);
+          dst[kv_swz(pos, j + 8u, D)] = __float2half_rn(c2);
         }
       } else if (k == kBkGu) {
         // matvec_swiglu.comp:67: gate row t * 8 + p (rows R0 / R1 hold gate / up)
@@ -754,220 +753,234 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_batch_kernel(const __gri
   };
 
   // One attention phase at layer l (attn_scores / softmax / attn_values,
-  // split-K): this CTA's units, then its merge slices.
+  // split-K). A unit (column, KV head, chunk of p.chunk positions) is one
+  // ring stage (its cached K rows, then its V rows) and belongs to one warp,
+  // which runs scores, the chunk softmax and the values on the tensor cores
+  // and writes the unit's (o, max, sum) partial: the 8 warps of a CTA work on
+  // 8 units at once. Unit u goes to CTA (u / 8) % grid, warp u % 8. Then the
+  // merge slices, one per (column, KV head, 16 dimensions).
   auto attention = [&](uint32_t ph, uint32_t l) {
     wait_phase(ph);
-    constexpr uint32_t KS = D / 16u;              // K-steps of a head row
-    const uint32_t HT = (G + 7u) / 8u;            // tiles of 8 heads
-    const uint32_t SST = p.chunk + 4u;            // row stride of sS (padded)
-    uint2 *sQB = reinterpret_cast<uint2 *>(aux);  // [HT][KS][2][32] q fragments
-    float *sS = reinterpret_cast<float *>(aux + HT * KS * 2u * 32u * 8u);  // [G][SST]
-    constexpr uint32_t W2 = D / 2u;               // 32-bit words of a row
-    for (uint32_t u = blockIdx.x; u < n_units; u += gridDim.x) {
-      const BatchUnit a = batch_unit(u, cu0, cnch, cpos, cff, S, p.chunk);
-      const BatchCol &cl = scol[a.n];
-      const size_t lo = (size_t)l * cl.layer_elems + (size_t)a.kvh * cl.ctx * D;
-      const __half *kg = cl.kc + lo, *vg = cl.vc + lo;
-      // rows this launch wrote (positions >= cff): from L2; the first word of
-      // each thread is loaded here, so its round trip overlaps the q loads
-      const uint32_t nfw = (a.len - a.staged) * W2, fr = a.r0 + a.staged;
-      uint32_t kw0 = 0, vw0 = 0;
-      if (tid < nfw) {
-        kw0 = __ldcg(reinterpret_cast<const unsigned int *>(kg + (size_t)fr * D) + tid);
-        vw0 = __ldcg(reinterpret_cast<const unsigned int *>(vg + (size_t)fr * D) + tid);
-      }
-      for (uint32_t e = tid; e < HT * KS * 32u; e += NCT) {
-        const uint32_t ln = e & 31u, ks = (e >> 5) % KS, ht = (e >> 5) / KS;
-        const uint32_t g = ht * 8u + (ln >> 2), d0 = ks * 16u + (ln & 3u) * 2u;
-        float v[4] = {0.f, 0.f, 0.f, 0.f};
-        if (g < G) {
-          const float *qg = p.q + (size_t)a.n * p.H + ((size_t)a.kvh * G + g) * D + d0;
-          v[0] = __ldcg(qg);
-          v[1] = __ldcg(qg + 1);
-          v[2] = __ldcg(qg + 8);
-          v[3] = __ldcg(qg + 9);
+    constexpr uint32_t KS = D / 16u;  // K-steps of a head row, and 16-dimension blocks
+    constexpr uint32_t W2 = D / 2u;   // 32-bit words of a row
+    const uint32_t CH = p.chunk, gq = lane >> 2, tq = lane & 3u;
+    __half *psh = reinterpret_cast<__half *>(aux) + cw * (2u * 8u * CH);  // P of the warp's unit: [8 heads][CH]
+    __half *psl = psh + 8u * CH;                                          // its lo halves
+    for (uint32_t i = 0;; ++i) {
+      bool more = true;
+      for (uint32_t w = 0; w < kMvConsumers; ++w) {
+        const uint32_t u = (i * gridDim.x + blockIdx.x) * kMvConsumers + w;
+        if (u >= n_units) {
+          more = false;
+          break;
         }
-        uint32_t hw[2], lw[2];
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-          const __half h0 = __float2half_rn(v[2 * j]), h1 = __float2half_rn(v[2 * j + 1]);
-          hw[j] = pack_half2(h0, h1);
-          lw[j] = pack_half2(__float2half_rn(v[2 * j] - __half2float(h0)), __float2half_rn(v[2 * j + 1] - __half2float(h1)));
+        if (!mbar_wait_bounded(&R.full[rp.slot], rp.phase, err)) {
+          set_error(err, kErrConsumerWait);
+          ok = false;
         }
-        sQB[((ht * KS + ks) * 2u + 0u) * 32u + ln] = make_uint2(hw[0], hw[1]);
-        sQB[((ht * KS + ks) * 2u + 1u) * 32u + ln] = make_uint2(lw[0], lw[1]);
-      }
-      const uint32_t sK = rp.slot, pK = rp.phase;
-      rp.next(R.nst);
-      const uint32_t sV = rp.slot, pV = rp.phase;
-      rp.next(R.nst);
-      if (!mbar_wait_bounded(&R.full[sK], pK, err) || !mbar_wait_bounded(&R.full[sV], pV, err)) {
-        set_error(err, kErrConsumerWait);
-        ok = false;
-      }
-      __half *kS = reinterpret_cast<__half *>(R.ring + sK * R.slot);
-      __half *vS = reinterpret_cast<__half *>(R.ring + sV * R.slot);
-      const uint32_t len16 = (a.len + 15u) & ~15u;
-      if (tid < nfw) {
-        reinterpret_cast<uint32_t *>(kS + a.staged * D)[tid] = kw0;
-        reinterpret_cast<uint32_t *>(vS + a.staged * D)[tid] = vw0;
-      }
-      for (uint32_t i = tid + NCT; i < nfw; i += NCT) {
-        reinterpret_cast<uint32_t *>(kS + a.staged * D)[i] =
-            __ldcg(reinterpret_cast<const unsigned int *>(kg + (size_t)fr * D) + i);
-        reinterpret_cast<uint32_t *>(vS + a.staged * D)[i] =
-            __ldcg(reinterpret_cast<const unsigned int *>(vg + (size_t)fr * D) + i);
-      }
-      // V rows past the chunk's end meet zero weights; make them zero too
-      for (uint32_t i = a.len * W2 + tid; i < len16 * W2; i += NCT) reinterpret_cast<uint32_t *>(vS)[i] = 0u;
-      named_bar(1, NCT);
-      // scores (attn_scores.comp:27-44) on the tensor cores: warp per (16 positions, 8 heads)
-      for (uint32_t it = cw; it < (len16 / 16u) * HT; it += kMvConsumers) {
-        const uint32_t pt = it / HT, ht = it % HT;
-        float c[4] = {0.f, 0.f, 0.f, 0.f}, cl2[4] = {0.f, 0.f, 0.f, 0.f};
-        const __half *kb = kS + (pt * 16u + (lane & 15u)) * D + (lane >> 4) * 8u;
-#pragma unroll 4
-        for (uint32_t ks = 0; ks < KS; ++ks) {
-          uint32_t af[4];
-          ldmatrix_x4(af, kb + ks * 16u);
-          const uint2 bh = sQB[((ht * KS + ks) * 2u + 0u) * 32u + lane];
-          const uint2 bl = sQB[((ht * KS + ks) * 2u + 1u) * 32u + lane];
-          mma_f16(c, af, bh.x, bh.y);
-          mma_f16(cl2, af, bl.x, bl.y);
-        }
-        const uint32_t t = pt * 16u + (lane >> 2), g = ht * 8u + (lane & 3u) * 2u;
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const uint32_t tt = t + (j >> 1) * 8u, gg = g + (j & 1);
-          if (tt < a.len && gg < G) sS[gg * SST + tt] = __fmul_rn(__fadd_rn(c[j], cl2[j]), p.attn_scale);
-        }
-      }
-      named_bar(1, NCT);
-      const size_t pslot = ((size_t)a.n * p.kv_heads + a.kvh) * p.max_chunks + a.c;  // (column, KV head, chunk)
-      // chunk softmax (softmax.comp): warp per head
-      for (uint32_t g0 = cw; g0 < G; g0 += kMvConsumers) {
-        float *sg = sS + g0 * SST;
-        float m = -INFINITY;
-        for (uint32_t t = lane; t < a.len; t += 32) m = fmaxf(m, sg[t]);
-        m = warp_max(m);
-        float lsum = 0.f;
-        for (uint32_t t = lane; t < a.len; t += 32) {
-          const float e = expf(sg[t] - m);
-          sg[t] = e;
-          lsum += e;
-        }
-        lsum = warp_sum(lsum);
-        if (lane == 0) p.apart_ml[pslot * G + g0] = make_float2(m, lsum);
-      }
-      named_bar(1, NCT);
-      // values (attn_values.comp) as (V^T)(P^T): warp per (16 dims, 8 heads)
-      for (uint32_t it = cw; it < KS * HT; it += kMvConsumers) {
-        const uint32_t dt = it / HT, ht = it % HT;
-        float c[4] = {0.f, 0.f, 0.f, 0.f}, cl2[4] = {0.f, 0.f, 0.f, 0.f};
-        const uint32_t gb = ht * 8u + (lane >> 2);
-        const float *pg = sS + (gb < G ? gb : 0u) * SST;
-        const __half *vb = vS + (((lane >> 4) & 1u) * 8u + (lane & 7u)) * D + dt * 16u + ((lane >> 3) & 1u) * 8u;
-        for (uint32_t kk = 0; kk < len16 / 16u; ++kk) {
-          uint32_t af[4];
-          ldmatrix_x4_trans(af, vb + kk * 16u * D);
-          float w[4];
-          const uint32_t t0w = kk * 16u + (lane & 3u) * 2u;
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const uint32_t tt = t0w + (j & 1) + (j >> 1) * 8u;
-            w[j] = (gb < G && tt < a.len) ? pg[tt] : 0.f;
+        if (w == cw) {
+          const BatchUnit a = batch_unit(u, cu0, cnch, cpos, cff, S, CH);
+          const BatchCol &cl = scol[a.n];
+          const size_t lo = (size_t)l * cl.layer_elems + (size_t)a.kvh * cl.ctx * D;
+          __half *kS = reinterpret_cast<__half *>(R.ring + rp.slot * R.slot), *vS = kS + CH * D;
+          // rows this launch wrote (positions >= cff) come from L2
+          const uint32_t fr = a.r0 + a.staged, nfw = (a.len - a.staged) * W2;
+          const unsigned int *kg = reinterpret_cast<const unsigned int *>(cl.kc + lo + (size_t)fr * D);
+          const unsigned int *vg = reinterpret_cast<const unsigned int *>(cl.vc + lo + (size_t)fr * D);
+          for (uint32_t e = lane; e < nfw; e += 32u) {
+            reinterpret_cast<uint32_t *>(kS + a.staged * D)[e] = __ldcg(kg + e);
+            reinterpret_cast<uint32_t *>(vS + a.staged * D)[e] = __ldcg(vg + e);
           }
-          uint32_t bh[2], bl[2];
+          const uint32_t len16 = (a.len + 15u) & ~15u, npt = len16 / 16u;
+          // V rows past the chunk's end meet zero weights; make them zero too
+          for (uint32_t e = a.len * W2 + lane; e < len16 * W2; e += 32u) reinterpret_cast<uint32_t *>(vS)[e] = 0u;
+          // q of head gq of the group as B fragments (rows 2tq, 2tq+1 | 2tq+8, 2tq+9
+          // of each K-step), split into fp16 hi + lo; heads >= G are zero
+          uint32_t qh[KS][2], ql[KS][2];
+          const float *qg = p.q + (size_t)a.n * p.H + ((size_t)a.kvh * G + (gq < G ? gq : 0u)) * D + 2u * tq;
 #pragma unroll
-          for (int j = 0; j < 2; ++j) {
-            const __half h0 = __float2half_rn(w[2 * j]), h1 = __float2half_rn(w[2 * j + 1]);
-            bh[j] = pack_half2(h0, h1);
-            bl[j] = pack_half2(__float2half_rn(w[2 * j] - __half2float(h0)), __float2half_rn(w[2 * j + 1] - __half2float(h1)));
+          for (uint32_t ks = 0; ks < KS; ++ks) {
+            float v[4] = {0.f, 0.f, 0.f, 0.f};
+            if (gq < G) {
+              v[0] = __ldcg(qg + ks * 16u);
+              v[1] = __ldcg(qg + ks * 16u + 1u);
+              v[2] = __ldcg(qg + ks * 16u + 8u);
+              v[3] = __ldcg(qg + ks * 16u + 9u);
+            }
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+              const __half h0 = __float2half_rn(v[2 * j]), h1 = __float2half_rn(v[2 * j + 1]);
+              qh[ks][j] = pack_half2(h0, h1);
+              ql[ks][j] = pack_half2(__float2half_rn(v[2 * j] - __half2float(h0)),
+                                     __float2half_rn(v[2 * j + 1] - __half2float(h1)));
+            }
           }
-          mma_f16(c, af, bh[0], bh[1]);
-          mma_f16(cl2, af, bl[0], bl[1]);
-        }
-        const uint32_t d = dt * 16u + (lane >> 2), g = ht * 8u + (lane & 3u) * 2u;
+          __syncwarp();
+          // scores (attn_scores.comp:27-44): S[t][g] = K[t] . q[g] * scale, 16 positions per MMA tile
+          float sc[4][4];
+          float m0 = -INFINITY, m1 = -INFINITY;
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const uint32_t dd = d + (j >> 1) * 8u, gg = g + (j & 1);
-          if (gg < G) p.apart[(pslot * G + gg) * D + dd] = __fadd_rn(c[j], cl2[j]);
+          for (uint32_t pt = 0; pt < 4; ++pt) {
+            if (pt >= npt) break;
+            float c[4] = {0.f, 0.f, 0.f, 0.f}, c2[4] = {0.f, 0.f, 0.f, 0.f};
+            const uint32_t kt = pt * 16u + (lane & 15u);  // this lane's K row (chunk-permuted, kv_swz)
+            const __half *kb = kS + kt * D;
+#pragma unroll
+            for (uint32_t ks = 0; ks < KS; ++ks) {
+              uint32_t af[4];
+              ldmatrix_x4(af, kb + kv_swz(a.r0 + kt, (lane >> 4) * 8u + ks * 16u, D));
+              mma_f16(c, af, qh[ks][0], qh[ks][1]);
+              mma_f16(c2, af, ql[ks][0], ql[ks][1]);
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const uint32_t t = pt * 16u + gq + (j >> 1) * 8u;
+              sc[pt][j] = t < a.len ? __fmul_rn(__fadd_rn(c[j], c2[j]), p.attn_scale) : -INFINITY;
+            }
+            m0 = fmaxf(m0, fmaxf(sc[pt][0], sc[pt][2]));
+            m1 = fmaxf(m1, fmaxf(sc[pt][1], sc[pt][3]));
+          }
+          // chunk softmax (softmax.comp) of heads 2tq and 2tq + 1 over the positions
+          // of the 8 lanes that share tq
+#pragma unroll
+          for (int o = 4; o < 32; o <<= 1) {
+            m0 = fmaxf(m0, __shfl_xor_sync(0xffffffffu, m0, o));
+            m1 = fmaxf(m1, __shfl_xor_sync(0xffffffffu, m1, o));
+          }
+          float l0 = 0.f, l1 = 0.f;
+#pragma unroll
+          for (uint32_t pt = 0; pt < 4; ++pt) {
+            if (pt >= npt) break;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float e = sc[pt][j] == -INFINITY ? 0.f : expf(sc[pt][j] - ((j & 1) ? m1 : m0));
+              if (j & 1) l1 += e; else l0 += e;
+              const uint32_t t = pt * 16u + gq + (j >> 1) * 8u, g = 2u * tq + (j & 1);
+              const __half h = __float2half_rn(e);
+              psh[g * CH + t] = g < G ? h : __float2half_rn(0.f);
+              psl[g * CH + t] = g < G ? __float2half_rn(e - __half2float(h)) : __float2half_rn(0.f);
+            }
+          }
+#pragma unroll
+          for (int o = 4; o < 32; o <<= 1) {
+            l0 += __shfl_xor_sync(0xffffffffu, l0, o);
+            l1 += __shfl_xor_sync(0xffffffffu, l1, o);
+          }
+          __syncwarp();
+          // values (attn_values.comp): O[d][g] = sum_t V[t][d] P[t][g] as (V^T)(P^T)
+          const size_t pslot = ((size_t)a.n * p.kv_heads + a.kvh) * p.max_chunks + a.c;
+          float *po = p.apart + pslot * D * G;
+          const uint32_t vt = ((lane >> 4) & 1u) * 8u + (lane & 7u);  // this lane's V row in each 16 (kv_swz)
+#pragma unroll 2
+          for (uint32_t dt = 0; dt < KS; ++dt) {
+            float o[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (uint32_t kk = 0; kk < 4; ++kk) {
+              if (kk >= npt) break;
+              uint32_t af[4];
+              ldmatrix_x4_trans(af, vS + (kk * 16u + vt) * D +
+                                        kv_swz(a.r0 + kk * 16u + vt, dt * 16u + ((lane >> 3) & 1u) * 8u, D));
+              const uint32_t pb = gq * CH + kk * 16u + 2u * tq;
+              mma_f16(o, af, *reinterpret_cast<const uint32_t *>(psh + pb), *reinterpret_cast<const uint32_t *>(psh + pb + 8u));
+              mma_f16(o, af, *reinterpret_cast<const uint32_t *>(psl + pb), *reinterpret_cast<const uint32_t *>(psl + pb + 8u));
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const uint32_t d = dt * 16u + gq + (j >> 1) * 8u, g = 2u * tq + (j & 1);
+              if (g < G) po[d * G + g] = o[j];
+            }
+          }
+          if (gq == 0) {
+            if (2u * tq < G) p.apart_ml[pslot * G + 2u * tq] = make_float2(m0, l0);
+            if (2u * tq + 1u < G) p.apart_ml[pslot * G + 2u * tq + 1u] = make_float2(m1, l1);
+          }
+          // the unit's partials are written: one arrival at its (column, KV head)
+          __syncwarp();
+          if (lane == 0) grid_arrive(p.ready + a.n * p.kv_heads + a.kvh);
         }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&R.empty[rp.slot]);
+        rp.next(R.nst);
       }
-      named_bar(1, NCT);
-      if (lane == 0) {
-        mbar_arrive(&R.empty[sK]);
-        mbar_arrive(&R.empty[sV]);
-      }
-      if (tid == 0) grid_arrive(p.ready + a.n * p.kv_heads + a.kvh);
-      named_bar(1, NCT);  // sQB / sS reuse
+      if (!more) break;
     }
-    // merge slices, one per (column, query head), from the end of the grid:
-    // o = sum_c exp(m_c - M) o_c / sum_c exp(m_c - M) l_c over the chunks
-    for (uint32_t m = gridDim.x - 1u - blockIdx.x; m < S * p.heads; m += gridDim.x) {
-      const uint32_t n = m / p.heads, h = m - n * p.heads, kvh = h / G, g0 = h - kvh * G;
+    // merge slices (column n, KV head, dimensions 16 db .. 16 db + 15):
+    // o = sum_c exp(m_c - M) o_c / sum_c exp(m_c - M) l_c over the unit chunks
+    float *sW = reinterpret_cast<float *>(aux);            // [max_chunks][8] chunk weights
+    float *sL = sW + p.max_chunks * 8u;                    // [8] 1 / sum of weights x sums per head
+    float *sP = sL + 8u;                                   // [32][8] partial maxima / sums, then the parts' outputs
+    for (uint32_t m = gridDim.x - 1u - blockIdx.x; m < S * p.kv_heads * KS; m += gridDim.x) {
+      const uint32_t n = m / (p.kv_heads * KS), rem = m - n * p.kv_heads * KS, kvh = rem / KS, db = rem - kvh * KS;
       const uint32_t nch = cnch[n];
-      if (tid == 0 && !grid_wait(p.ready + n * p.kv_heads + kvh, srdy[n * p.kv_heads + kvh] +
-                                                                     (unsigned long long)(l + 1u) * nch, err))
+      if (tid == 0 && !grid_wait(p.ready + n * p.kv_heads + kvh,
+                                 srdy[n * p.kv_heads + kvh] + (unsigned long long)(l + 1u) * nch, err))
         set_error(err, kErrGridWait);
       named_bar(1, NCT);
-      constexpr uint32_t NCOL = D / 4u, NGR = NCT / NCOL, MR = 8u;
-      static_assert(NCT % NCOL == 0, "whole chunk groups");
-      float *sW = reinterpret_cast<float *>(aux);
-      float4 *sO = reinterpret_cast<float4 *>(aux + step_merge_w_bytes(p.max_chunks));
-      const uint32_t col = tid % NCOL, grp = tid / NCOL;
-      const size_t hb = ((size_t)n * p.kv_heads + kvh) * p.max_chunks * G + g0;  // slot of chunk 0
-      const float4 *ob = reinterpret_cast<const float4 *>(p.apart + hb * D) + col;
-      auto row = [&](uint32_t c) { return __ldcg(ob + (size_t)c * G * NCOL); };
-      float4 v[MR];
-#pragma unroll
-      for (uint32_t i = 0; i < MR; ++i) {
-        const uint32_t c = grp + i * NGR;
-        v[i] = c < nch ? row(c) : make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-      if (cw == 0) {
-        float M = -INFINITY;
-        for (uint32_t c = lane; c < nch; c += 32u) M = fmaxf(M, __ldcg(&p.apart_ml[hb + (size_t)c * G]).x);
-        M = warp_max(M);
-        float Ls = 0.f;
-        for (uint32_t c = lane; c < nch; c += 32u) {
-          const float2 m2 = __ldcg(&p.apart_ml[hb + (size_t)c * G]);
-          const float w = m2.x == -INFINITY ? 0.f : expf(m2.x - M);
-          sW[c] = w;
-          Ls = fmaf(w, m2.y, Ls);
-        }
-        Ls = warp_sum(Ls);
-        if (lane == 0) sW[p.max_chunks] = 1.0f / Ls;
-      }
+      const size_t hb = ((size_t)n * p.kv_heads + kvh) * p.max_chunks;
+      const uint32_t g = tid & 7u, part = tid >> 3;  // 32 parts of the chunks per head
+      float M = -INFINITY;
+      if (g < G)
+        for (uint32_t c = part; c < nch; c += 32u) M = fmaxf(M, __ldcg(&p.apart_ml[(hb + c) * G + g]).x);
+      sP[part * 8u + g] = M;
       named_bar(1, NCT);
-      float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
-      auto acc = [&](uint32_t c, const float4 &r) {
-        const float w = sW[c];
-        o.x = fmaf(w, r.x, o.x);
-        o.y = fmaf(w, r.y, o.y);
-        o.z = fmaf(w, r.z, o.z);
-        o.w = fmaf(w, r.w, o.w);
+      M = -INFINITY;
+#pragma unroll 8
+      for (uint32_t q2 = 0; q2 < 32u; ++q2) M = fmaxf(M, sP[q2 * 8u + g]);
+      float Lp = 0.f;
+      if (g < G)
+        for (uint32_t c = part; c < nch; c += 32u) {
+          const float2 ml = __ldcg(&p.apart_ml[(hb + c) * G + g]);
+          const float w = ml.x == -INFINITY ? 0.f : expf(ml.x - M);
+          sW[c * 8u + g] = w;
+          Lp = fmaf(w, ml.y, Lp);
+        }
+      named_bar(1, NCT);
+      sP[part * 8u + g] = Lp;
+      named_bar(1, NCT);
+      if (tid < 8u) {
+        float L = 0.f;
+        for (uint32_t q2 = 0; q2 < 32u; ++q2) L += sP[q2 * 8u + tid];
+        sL[tid] = 1.0f / L;
+      }
+      named_bar(1, NCT);  // sP reuse
+      // outputs: thread (dimension 16 db + dl, heads hq*VW .. hq*VW + VW - 1, chunk part)
+      // loads VW heads of one dimension at once, 4 chunks in flight; the parts
+      // are added in order
+      const uint32_t VW = G >= 4u ? 4u : G, TPR = 16u * (G / VW), NPART = NCT / TPR;
+      const uint32_t rr = tid % TPR, cp = tid / TPR, dl = rr / (G / VW), hq = rr % (G / VW);
+      const float *ob = p.apart + (hb * D + db * 16u + dl) * G + hq * VW;
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      auto add = [&](uint32_t c) {
+        const float *src = ob + (size_t)c * D * G;
+        const float *w = sW + c * 8u + hq * VW;
+        if (VW == 4u) {
+          const float4 x = __ldcg(reinterpret_cast<const float4 *>(src));
+          acc[0] = fmaf(w[0], x.x, acc[0]);
+          acc[1] = fmaf(w[1], x.y, acc[1]);
+          acc[2] = fmaf(w[2], x.z, acc[2]);
+          acc[3] = fmaf(w[3], x.w, acc[3]);
+        } else {
+          for (uint32_t v = 0; v < VW; ++v) acc[v] = fmaf(w[v], __ldcg(src + v), acc[v]);
+        }
       };
-#pragma unroll
-      for (uint32_t i = 0; i < MR; ++i)
-        if (grp + i * NGR < nch) acc(grp + i * NGR, v[i]);
-      for (uint32_t c = grp + MR * NGR; c < nch; c += NGR) acc(c, row(c));
-      sO[grp * NCOL + col] = o;
-      named_bar(1, NCT);
-      if (tid < NCOL) {
-        float4 t = sO[tid];
-        for (uint32_t gi = 1; gi < NGR; ++gi) {
-          const float4 u2 = sO[gi * NCOL + tid];
-          t.x += u2.x;
-          t.y += u2.y;
-          t.z += u2.z;
-          t.w += u2.w;
-        }
-        const float inv = sW[p.max_chunks];
-        reinterpret_cast<float4 *>(p.attn + (size_t)n * p.H + ((size_t)kvh * G + g0) * D)[tid] =
-            make_float4(t.x * inv, t.y * inv, t.z * inv, t.w * inv);
+      uint32_t c = cp;
+      for (; c + 3u * NPART < nch; c += 4u * NPART) {
+        add(c);
+        add(c + NPART);
+        add(c + 2u * NPART);
+        add(c + 3u * NPART);
       }
+      for (; c < nch; c += NPART) add(c);
+      float *so = sP;  // [NPART][16 dims x G heads]
+      for (uint32_t v = 0; v < VW; ++v) so[cp * 16u * G + dl * G + hq * VW + v] = acc[v];
       named_bar(1, NCT);
+      if (tid < 16u * G) {
+        const uint32_t dd = db * 16u + tid / G, gd = tid % G;
+        float o = 0.f;
+        for (uint32_t q2 = 0; q2 < NPART; ++q2) o += so[q2 * 16u * G + tid];
+        p.attn[(size_t)n * p.H + ((size_t)kvh * G + gd) * D + dd] = o * sL[gd];
+      }
+      named_bar(1, NCT);  // sW / sP reuse
     }
     arrive();
   };

@@ -712,6 +712,7 @@ void build_program(vg_stream *s, bool token_input, bool logits, std::vector<Laun
     ap.scale = 1.0f / sqrtf((float)D);
     ap.fixed_pos = 0xFFFFFFFFu;
     ap.ctrl = ctrl;
+    ap.swz = 1;  // the stream's cache holds chunk-permuted rows (kv_swz)
     prog.push_back({[=](cudaStream_t st, bool pdl) {
       return launch_ex(afn, dim3(ap.nsplit, ap.kv_heads), dim3(kAttnThreads), asmem, st, pdl, kAttnCluster, ap);
     }, "attention", l, 2ull * c.kv_dim * 2, true});
@@ -1051,6 +1052,7 @@ std::string plan_batch(vg_model *m, BatchWork &w) {
   if (!coop) return "the device has no cooperative launch";
   const uint32_t D = c.head_dim, G = c.head_count / c.head_count_kv, H = c.embedding_length;
   if (c.head_count_kv > 8) return strf("%u KV heads (at most 8)", c.head_count_kv);
+  if (G > 8) return strf("%u query heads per KV head (at most 8)", G);
   if (c.head_count * D != H) return "the query width differs from the hidden width";
   w.fn = type == GGML_Q8_0 ? pick_batch_dpl<true>(D) : pick_batch_dpl<false>(D);
   if (!w.fn) return strf("head_dim %u", D);
@@ -1070,13 +1072,14 @@ std::string plan_batch(vg_model *m, BatchWork &w) {
     part_tiles = std::max(part_tiles, g.tiles());
   }
   p.slot = kStageSegs * segb;
-  p.chunk = std::min<uint32_t>(64u, p.slot / (2u * D)) & ~15u;
-  if (p.chunk == 0) return strf("a stage slot of %u bytes holds no 16 rows of head_dim %u", p.slot, D);
+  // positions per attention unit: 16-row MMA tiles of K and V rows, both in one stage slot
+  p.chunk = std::min<uint32_t>(64u, p.slot / (4u * D)) & ~15u;
+  if (p.chunk == 0) return strf("a stage slot of %u bytes holds no 16 K and V rows of head_dim %u", p.slot, D);
   p.max_chunks = (c.context_length + p.chunk - 1) / p.chunk;
   const uint32_t grid = (uint32_t)m->ctx->sms;
   if (grid > kBatchMaxRowGroups) return strf("%u SMs (the row-group counters cover %u)", grid, kBatchMaxRowGroups);
   constexpr uint32_t kMaxAux = 72u * 1024u;  // operand region: leaves the ring 8 or more stages
-  uint32_t aux = step_attn_bytes(G, D, p.chunk, p.max_chunks), maxc = 1;
+  uint32_t aux = batch_attn_bytes(p.chunk, p.max_chunks), maxc = 1;
   for (uint32_t k = 0; k < kBatchKinds; ++k) {
     const TileGeom &g = p.g[k];
     p.split[k] = choose_split(g, kBatchMaxCols, grid, kMaxAux);
@@ -1645,13 +1648,19 @@ int vg_stream_write_kv(vg_stream *s, const uint16_t *k, const uint16_t *v, uint3
     if (n > s->max_ctx) fail(VG_EFULL, strf("%u positions exceed the KV cache of %u", n, s->max_ctx));
     CK(cudaSetDevice(s->m->ctx->device));
     CK(cudaStreamSynchronize(s->st));
+    // reference layout [layer][pos][kv_dim] -> [layer][kv_head][ctx][head_dim],
+    // each row's chunks permuted as kv_swz stores them
     const uint32_t D = c.head_dim;
+    std::vector<uint16_t> blk((size_t)n * D);
     for (uint32_t l = 0; l < c.block_count && n; ++l)
       for (uint32_t h = 0; h < c.head_count_kv; ++h) {
         const size_t dst = ((size_t)l * c.head_count_kv + h) * s->max_ctx * D;
-        const size_t src = (size_t)l * n * c.kv_dim + (size_t)h * D;
-        CK(cudaMemcpy2D(s->kc + dst, D * 2, k + src, c.kv_dim * 2, D * 2, n, cudaMemcpyHostToDevice));
-        CK(cudaMemcpy2D(s->vc + dst, D * 2, v + src, c.kv_dim * 2, D * 2, n, cudaMemcpyHostToDevice));
+        for (int which = 0; which < 2; ++which) {
+          const uint16_t *src = (which ? v : k) + (size_t)l * n * c.kv_dim + (size_t)h * D;
+          for (uint32_t pos = 0; pos < n; ++pos)
+            for (uint32_t e = 0; e < D; ++e) blk[(size_t)pos * D + kv_swz(pos, e, D)] = src[(size_t)pos * c.kv_dim + e];
+          CK(cudaMemcpy((which ? s->vc : s->kc) + dst, blk.data(), blk.size() * 2, cudaMemcpyHostToDevice));
+        }
       }
     CK(cudaMemcpy(s->ctrl + kCtrlPos, &n, 4, cudaMemcpyHostToDevice));
     s->pos = n;
@@ -1668,12 +1677,16 @@ int vg_stream_read_kv(vg_stream *s, uint16_t *k, uint16_t *v, uint32_t n) {
     CK(cudaSetDevice(s->m->ctx->device));
     sync_stream(s, 60ull * 1000000000ull, false);
     const uint32_t D = c.head_dim;
+    std::vector<uint16_t> blk((size_t)n * D);
     for (uint32_t l = 0; l < c.block_count && n; ++l)
       for (uint32_t h = 0; h < c.head_count_kv; ++h) {
         const size_t src = ((size_t)l * c.head_count_kv + h) * s->max_ctx * D;
-        const size_t dst = (size_t)l * n * c.kv_dim + (size_t)h * D;
-        CK(cudaMemcpy2D(k + dst, c.kv_dim * 2, s->kc + src, D * 2, D * 2, n, cudaMemcpyDeviceToHost));
-        CK(cudaMemcpy2D(v + dst, c.kv_dim * 2, s->vc + src, D * 2, D * 2, n, cudaMemcpyDeviceToHost));
+        for (int which = 0; which < 2; ++which) {
+          CK(cudaMemcpy(blk.data(), (which ? s->vc : s->kc) + src, blk.size() * 2, cudaMemcpyDeviceToHost));
+          uint16_t *dst = (which ? v : k) + (size_t)l * n * c.kv_dim + (size_t)h * D;
+          for (uint32_t pos = 0; pos < n; ++pos)
+            for (uint32_t e = 0; e < D; ++e) dst[(size_t)pos * c.kv_dim + e] = blk[(size_t)pos * D + kv_swz(pos, e, D)];
+        }
       }
     return VG_OK;
   });

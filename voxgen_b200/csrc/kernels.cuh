@@ -94,6 +94,18 @@ struct TileGeom {
   }
 };
 
+// KV-cache rows in HBM are stored with their 16-byte chunks (8 fp16 each)
+// XOR-permuted by the row's position: chunk c of row r sits at chunk
+// c ^ (r & m), m = min(head_dim / 8, 8) - 1. A bulk copy of consecutive rows
+// then lands in shared memory so that the 8 rows an ldmatrix reads at one
+// chunk column fall in 8 different bank groups (plain rows of 128 or 256
+// bytes put all 8 in the same banks). kv_swz gives the stored element index
+// of element e of the row at position r.
+__host__ __device__ __forceinline__ uint32_t kv_swz(uint32_t r, uint32_t e, uint32_t head_dim) {
+  const uint32_t m = (head_dim >= 64u ? 8u : head_dim / 8u) - 1u;
+  return ((((e >> 3) ^ (r & m)) << 3) | (e & 7u));
+}
+
 struct MvParams {
   const uint8_t *w;       // segmented tiles
   TileGeom g;
@@ -293,14 +305,14 @@ __device__ __forceinline__ void mv_epilogue(const MvParams &p, uint32_t R, float
         p.out[head * hd + i + half_d] = b;
       } else {
         __half *dst = p.kc + ((size_t)head * p.ctx + pos) * hd;  // store_kv.comp:21-22, RNE
-        dst[i] = __float2half_rn(a);
-        dst[i + half_d] = __float2half_rn(b);
+        dst[kv_swz(pos, i, hd)] = __float2half_rn(a);
+        dst[kv_swz(pos, i + half_d, hd)] = __float2half_rn(b);
       }
     } else {
       const uint32_t v = R - p.q_rows - p.kv_rows, kvh = v / hd, j = v % hd;
       __half *dst = p.vc + ((size_t)kvh * p.ctx + pos) * hd;
-      dst[j] = __float2half_rn(a);
-      dst[j + 8u] = __float2half_rn(b);
+      dst[kv_swz(pos, j, hd)] = __float2half_rn(a);
+      dst[kv_swz(pos, j + 8u, hd)] = __float2half_rn(b);
     }
   }
 }
@@ -953,6 +965,7 @@ struct AttnParams {
   float scale;             // 1 / sqrt(head_dim)
   uint32_t fixed_pos;      // position to use, or 0xFFFFFFFF to read ctrl
   uint32_t *ctrl;
+  uint32_t swz;            // 1: rows stored chunk-permuted (kv_swz, a stream's cache); 0: plain rows
 };
 
 __host__ __device__ inline uint32_t attention_smem_bytes(uint32_t G, uint32_t head_dim, uint32_t chunk_cap) {
@@ -1035,7 +1048,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
   // scores: warp per position; lane holds DPL dims of K; query heads in groups of 8
   for (uint32_t t = warp; t < len; t += nwarps) {
     float kf[DPL];
-    const __half *kr = sK + t * D + lane * DPL;
+    const __half *kr = sK + t * D + (p.swz ? kv_swz(t0 + t, lane * DPL, D) : lane * DPL);
 #pragma unroll
     for (int j = 0; j < DPL; ++j) kf[j] = __half2float(kr[j]);
     for (uint32_t gb = 0; gb < G; gb += 8) {
@@ -1076,7 +1089,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(const __grid_co
     for (int j = 0; j < DPL; ++j) o[j] = 0.f;
     for (uint32_t t = 0; t < len; ++t) {
       const float pw = sg[t];
-      const __half *vr = sV + t * D + lane * DPL;
+      const __half *vr = sV + t * D + (p.swz ? kv_swz(t0 + t, lane * DPL, D) : lane * DPL);
 #pragma unroll
       for (int j = 0; j < DPL; ++j) o[j] = fmaf(pw, __half2float(vr[j]), o[j]);
     }

@@ -614,11 +614,12 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_step_kernel(const __grid
         for (uint32_t it = cw; it < (len16 / 16u) * HT; it += kMvConsumers) {
           const uint32_t pt = it / HT, ht = it % HT;
           float c[4] = {0.f, 0.f, 0.f, 0.f}, cl[4] = {0.f, 0.f, 0.f, 0.f};  // hi and lo chains
-          const __half *kb = kS + (pt * 16u + (lane & 15u)) * D + (lane >> 4) * 8u;
+          const uint32_t kt = pt * 16u + (lane & 15u);  // this lane's K row (chunk-permuted, kv_swz)
+          const __half *kb = kS + kt * D;
 #pragma unroll 4
           for (uint32_t ks = 0; ks < KS; ++ks) {
             uint32_t af[4];
-            ldmatrix_x4(af, kb + ks * 16u);
+            ldmatrix_x4(af, kb + kv_swz(a.r0 + kt, (lane >> 4) * 8u + ks * 16u, D));
             const uint2 bh = sQB[((ht * KS + ks) * 2u + 0u) * 32u + lane];
             const uint2 bl = sQB[((ht * KS + ks) * 2u + 1u) * 32u + lane];
             mma_f16(c, af, bh.x, bh.y);
@@ -659,10 +660,11 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_step_kernel(const __grid
           float c[4] = {0.f, 0.f, 0.f, 0.f}, cl[4] = {0.f, 0.f, 0.f, 0.f};  // hi and lo chains
           const uint32_t gb = ht * 8u + (lane >> 2);  // head of this lane's B column
           const float *pg = sS + (gb < G ? gb : 0u) * SST;
-          const __half *vb = vS + (((lane >> 4) & 1u) * 8u + (lane & 7u)) * D + dt * 16u + ((lane >> 3) & 1u) * 8u;
+          const uint32_t vt = ((lane >> 4) & 1u) * 8u + (lane & 7u);  // this lane's V row in each 16 (kv_swz)
+          const uint32_t ve = dt * 16u + ((lane >> 3) & 1u) * 8u;
           for (uint32_t kk = 0; kk < len16 / 16u; ++kk) {
             uint32_t af[4];
-            ldmatrix_x4_trans(af, vb + kk * 16u * D);
+            ldmatrix_x4_trans(af, vS + (kk * 16u + vt) * D + kv_swz(a.r0 + kk * 16u + vt, ve, D));
             float w[4];
             const uint32_t t0w = kk * 16u + (lane & 3u) * 2u;
 #pragma unroll
