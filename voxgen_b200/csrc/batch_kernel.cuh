@@ -304,10 +304,10 @@ __device__ __forceinline__ void batch_consume(const MvRing &R, RingPos &rp, cons
   constexpr uint32_t NCT = kMvConsumers * 32;
   const uint32_t SEGB = g.seg_bytes(), tid = cw * 32u + lane;
   const uint32_t gq = lane >> 2, tq = lane & 3u;
-  const bool two = S > 8u;  // the second n8 tile (columns 8-15) carries live columns
   const float *colv = reinterpret_cast<const float *>(aux + O.colv);
   const uint8_t *hi = aux + O.hi, *lo = aux + O.lo;
   float *red = reinterpret_cast<float *>(aux + O.red);
+  (void)S;  // both n8 tiles are always computed; columns >= S hold zeros
   for (uint32_t q = 0; q < batch_groups(b); ++q) {
     const uint32_t nq = min(4u, b.nt - 4u * q);
     float tot[4][2][4];
@@ -325,64 +325,83 @@ __device__ __forceinline__ void batch_consume(const MvRing &R, RingPos &rp, cons
       }
       const uint8_t *st = R.ring + rp.slot * R.slot;
       const uint32_t kk = sgi * kSegSteps + cw;  // K-step within the slice
+      // the 4 tiles' work is issued in lock-step so their MMA chains overlap; a
+      // group of fewer tiles repeats its last tile, whose sums are not kept
+      const uint8_t *sg[4];
+#pragma unroll
+      for (uint32_t j = 0; j < 4; ++j) sg[j] = st + min(j, nq - 1u) * SEGB + cw * kStepBytes;
       if constexpr (Q8) {
         const uint32_t bo = ((kk * kBatchMaxCols + gq) * 4u + tq) * 16u;
         const uint4 bh0 = *reinterpret_cast<const uint4 *>(hi + bo), bl0 = *reinterpret_cast<const uint4 *>(lo + bo);
-        uint4 bh1 = make_uint4(0u, 0u, 0u, 0u), bl1 = bh1;
-        if (two) {
-          bh1 = *reinterpret_cast<const uint4 *>(hi + bo + 8u * 64u);
-          bl1 = *reinterpret_cast<const uint4 *>(lo + bo + 8u * 64u);
+        const uint4 bh1 = *reinterpret_cast<const uint4 *>(hi + bo + 8u * 64u);
+        const uint4 bl1 = *reinterpret_cast<const uint4 *>(lo + bo + 8u * 64u);
+        uint32_t a[4][4];
+        float2 d[4];
+#pragma unroll
+        for (uint32_t j = 0; j < 4; ++j) {
+          ldmatrix_x4(a[j], sg[j] + lane * 16u);
+          d[j] = __half22float2(*reinterpret_cast<const __half2 *>(sg[j] - cw * kStepBytes + kSegQsBytes + gq * 32u + cw * 4u));
+        }
+        float c[4][2][4];
+        uint32_t A[4][4];
+        // K columns 0-15 of the step (int8 A fragment registers 0 and 1)
+#pragma unroll
+        for (uint32_t j = 0; j < 4; ++j) {
+          i8x4_to_h2x2(a[j][0], A[j][0], A[j][2]);
+          i8x4_to_h2x2(a[j][1], A[j][1], A[j][3]);
         }
 #pragma unroll
         for (uint32_t j = 0; j < 4; ++j) {
-          if (j >= nq) break;
-          const uint8_t *sg = st + j * SEGB;
-          uint32_t a[4], A1[4], A2[4];
-          ldmatrix_x4(a, sg + cw * kStepBytes + lane * 16u);
-          i8x4_to_h2x2(a[0], A1[0], A1[2]);
-          i8x4_to_h2x2(a[1], A1[1], A1[3]);
-          i8x4_to_h2x2(a[2], A2[0], A2[2]);
-          i8x4_to_h2x2(a[3], A2[1], A2[3]);
-          const float2 d = __half22float2(*reinterpret_cast<const __half2 *>(sg + kSegQsBytes + gq * 32u + cw * 4u));
-          float c[4];
-          mma_f16_zero(c, A1, bh0.x, bh0.y);
-          mma_f16(c, A1, bl0.x, bl0.y);
-          mma_f16(c, A2, bh0.z, bh0.w);
-          mma_f16(c, A2, bl0.z, bl0.w);
-          tot[j][0][0] = fmaf(c[0], d.x, tot[j][0][0]);
-          tot[j][0][1] = fmaf(c[1], d.x, tot[j][0][1]);
-          tot[j][0][2] = fmaf(c[2], d.y, tot[j][0][2]);
-          tot[j][0][3] = fmaf(c[3], d.y, tot[j][0][3]);
-          if (two) {
-            mma_f16_zero(c, A1, bh1.x, bh1.y);
-            mma_f16(c, A1, bl1.x, bl1.y);
-            mma_f16(c, A2, bh1.z, bh1.w);
-            mma_f16(c, A2, bl1.z, bl1.w);
-            tot[j][1][0] = fmaf(c[0], d.x, tot[j][1][0]);
-            tot[j][1][1] = fmaf(c[1], d.x, tot[j][1][1]);
-            tot[j][1][2] = fmaf(c[2], d.y, tot[j][1][2]);
-            tot[j][1][3] = fmaf(c[3], d.y, tot[j][1][3]);
-          }
+          mma_f16_zero(c[j][0], A[j], bh0.x, bh0.y);
+          mma_f16_zero(c[j][1], A[j], bh1.x, bh1.y);
         }
+#pragma unroll
+        for (uint32_t j = 0; j < 4; ++j) {
+          mma_f16(c[j][0], A[j], bl0.x, bl0.y);
+          mma_f16(c[j][1], A[j], bl1.x, bl1.y);
+        }
+        // K columns 16-31 (registers 2 and 3)
+#pragma unroll
+        for (uint32_t j = 0; j < 4; ++j) {
+          i8x4_to_h2x2(a[j][2], A[j][0], A[j][2]);
+          i8x4_to_h2x2(a[j][3], A[j][1], A[j][3]);
+        }
+#pragma unroll
+        for (uint32_t j = 0; j < 4; ++j) {
+          mma_f16(c[j][0], A[j], bh0.z, bh0.w);
+          mma_f16(c[j][1], A[j], bh1.z, bh1.w);
+        }
+#pragma unroll
+        for (uint32_t j = 0; j < 4; ++j) {
+          mma_f16(c[j][0], A[j], bl0.z, bl0.w);
+          mma_f16(c[j][1], A[j], bl1.z, bl1.w);
+        }
+#pragma unroll
+        for (uint32_t j = 0; j < 4; ++j)
+#pragma unroll
+          for (uint32_t nt = 0; nt < 2; ++nt) {
+            tot[j][nt][0] = fmaf(c[j][nt][0], d[j].x, tot[j][nt][0]);
+            tot[j][nt][1] = fmaf(c[j][nt][1], d[j].x, tot[j][nt][1]);
+            tot[j][nt][2] = fmaf(c[j][nt][2], d[j].y, tot[j][nt][2]);
+            tot[j][nt][3] = fmaf(c[j][nt][3], d[j].y, tot[j][nt][3]);
+          }
       } else {
         const uint32_t bo = ((kk * kBatchMaxCols + gq) * 4u + tq) * 8u;
         const uint2 bh0 = *reinterpret_cast<const uint2 *>(hi + bo), bl0 = *reinterpret_cast<const uint2 *>(lo + bo);
-        uint2 bh1 = make_uint2(0u, 0u), bl1 = bh1;
-        if (two) {
-          bh1 = *reinterpret_cast<const uint2 *>(hi + bo + 8u * 32u);
-          bl1 = *reinterpret_cast<const uint2 *>(lo + bo + 8u * 32u);
+        const uint2 bh1 = *reinterpret_cast<const uint2 *>(hi + bo + 8u * 32u);
+        const uint2 bl1 = *reinterpret_cast<const uint2 *>(lo + bo + 8u * 32u);
+        uint32_t a[4][4];
+#pragma unroll
+        for (uint32_t j = 0; j < 4; ++j) ldmatrix_x4(a[j], sg[j] + lane * 16u);
+#pragma unroll
+        for (uint32_t j = 0; j < 4; ++j) {
+          mma_f16(tot[j][0], a[j], bh0.x, bh0.y);
+          mma_f16(tot[j][1], a[j], bh1.x, bh1.y);
         }
 #pragma unroll
         for (uint32_t j = 0; j < 4; ++j) {
-          if (j >= nq) break;
-          uint32_t a[4];
-          ldmatrix_x4(a, st + j * SEGB + cw * kStepBytes + lane * 16u);
-          mma_f16(tot[j][0], a, bh0.x, bh0.y);
-          mma_f16(tot[j][0], a, bl0.x, bl0.y);
-          if (two) {
-            mma_f16(tot[j][1], a, bh1.x, bh1.y);
-            mma_f16(tot[j][1], a, bl1.x, bl1.y);
-          }
+          mma_f16(tot[j][0], a[j], bl0.x, bl0.y);
+          mma_f16(tot[j][1], a[j], bl1.x, bl1.y);
         }
       }
       __syncwarp();
@@ -423,19 +442,31 @@ __device__ __forceinline__ void batch_reduce(const BatchRun &b, uint32_t C, cons
                                              const float *rs, uint32_t S, uint32_t tid, Epi epi) {
   const uint32_t half = tid >> 7, pr = (tid >> 4) & 7u, n = tid & 15u;
   const size_t stride = (size_t)part_tiles * 256u;
-  for (uint32_t i = half; b.c + i * C < b.nt; i += 2u) {
+  // two tiles per iteration, their loads in flight together
+  for (uint32_t i = half; b.c + i * C < b.nt; i += 4u) {
     const uint32_t t = b.t0 + b.c + i * C;
-    const float *pt = part + (size_t)t * 256u + pr * 16u + n;
-    float a = 0.f, c2 = 0.f;
+    const bool two = b.c + (i + 2u) * C < b.nt;
+    const uint32_t t2 = two ? t + 2u * C : t;
+    const float *pt = part + (size_t)t * 256u + pr * 16u + n, *pu = part + (size_t)t2 * 256u + pr * 16u + n;
+    float a = 0.f, c2 = 0.f, a2 = 0.f, c3 = 0.f;
     for (uint32_t cg = 0; cg < C; ++cg) {
       a += __ldcg(pt + cg * stride);
       c2 += __ldcg(pt + cg * stride + 128u);
+      a2 += __ldcg(pu + cg * stride);
+      c3 += __ldcg(pu + cg * stride + 128u);
     }
-    if (n < S) epi(t * kTileRows + pr, n, a * rs[n], c2 * rs[n]);
+    if (n < S) {
+      epi(t * kTileRows + pr, n, a * rs[n], c2 * rs[n]);
+      if (two) epi(t2 * kTileRows + pr, n, a2 * rs[n], c3 * rs[n]);
+    }
   }
 }
 
 enum : uint32_t { kBkQkv = 0, kBkO = 1, kBkGu = 2, kBkDown = 3 };
+
+// Positions of a batched attention unit for head_dim D: 16-row MMA tiles of K
+// and V rows that fit one stage slot together (a slot holds 16 KiB or more).
+__host__ __device__ constexpr uint32_t batch_chunk(uint32_t D) { return D >= 256u ? 16u : D >= 128u ? 32u : 64u; }
 
 // aux bytes of an attention phase: every warp's P of its unit (hi and lo,
 // [8 heads][chunk] fp16), or a merge slice's chunk weights [max_chunks][8]
@@ -763,7 +794,8 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_batch_kernel(const __gri
     wait_phase(ph);
     constexpr uint32_t KS = D / 16u;  // K-steps of a head row, and 16-dimension blocks
     constexpr uint32_t W2 = D / 2u;   // 32-bit words of a row
-    const uint32_t CH = p.chunk, gq = lane >> 2, tq = lane & 3u;
+    constexpr uint32_t CH = batch_chunk(D), NPT = CH / 16u;  // positions of a unit, 16-row tiles
+    const uint32_t gq = lane >> 2, tq = lane & 3u;
     __half *psh = reinterpret_cast<__half *>(aux) + cw * (2u * 8u * CH);  // P of the warp's unit: [8 heads][CH]
     __half *psl = psh + 8u * CH;                                          // its lo halves
     for (uint32_t i = 0;; ++i) {
@@ -791,9 +823,9 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_batch_kernel(const __gri
             reinterpret_cast<uint32_t *>(kS + a.staged * D)[e] = __ldcg(kg + e);
             reinterpret_cast<uint32_t *>(vS + a.staged * D)[e] = __ldcg(vg + e);
           }
-          const uint32_t len16 = (a.len + 15u) & ~15u, npt = len16 / 16u;
-          // V rows past the chunk's end meet zero weights; make them zero too
-          for (uint32_t e = a.len * W2 + lane; e < len16 * W2; e += 32u) reinterpret_cast<uint32_t *>(vS)[e] = 0u;
+          // V rows past the unit's end meet zero weights; make them zero too (all
+          // NPT tiles are computed, the scores of rows past the end are masked)
+          for (uint32_t e = a.len * W2 + lane; e < CH * W2; e += 32u) reinterpret_cast<uint32_t *>(vS)[e] = 0u;
           // q of head gq of the group as B fragments (rows 2tq, 2tq+1 | 2tq+8, 2tq+9
           // of each K-step), split into fp16 hi + lo; heads >= G are zero
           uint32_t qh[KS][2], ql[KS][2];
@@ -802,10 +834,12 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_batch_kernel(const __gri
           for (uint32_t ks = 0; ks < KS; ++ks) {
             float v[4] = {0.f, 0.f, 0.f, 0.f};
             if (gq < G) {
-              v[0] = __ldcg(qg + ks * 16u);
-              v[1] = __ldcg(qg + ks * 16u + 1u);
-              v[2] = __ldcg(qg + ks * 16u + 8u);
-              v[3] = __ldcg(qg + ks * 16u + 9u);
+              const float2 x = __ldcg(reinterpret_cast<const float2 *>(qg + ks * 16u));
+              const float2 y = __ldcg(reinterpret_cast<const float2 *>(qg + ks * 16u + 8u));
+              v[0] = x.x;
+              v[1] = x.y;
+              v[2] = y.x;
+              v[3] = y.y;
             }
 #pragma unroll
             for (int j = 0; j < 2; ++j) {
@@ -816,29 +850,36 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_batch_kernel(const __gri
             }
           }
           __syncwarp();
-          // scores (attn_scores.comp:27-44): S[t][g] = K[t] . q[g] * scale, 16 positions per MMA tile
-          float sc[4][4];
+          // scores (attn_scores.comp:27-44): S[t][g] = K[t] . q[g] * scale, 16 positions
+          // per MMA tile, the tiles' chains interleaved
+          float sc[NPT][4];
           float m0 = -INFINITY, m1 = -INFINITY;
+          {
+            float c[NPT][4], c2[NPT][4];
 #pragma unroll
-          for (uint32_t pt = 0; pt < 4; ++pt) {
-            if (pt >= npt) break;
-            float c[4] = {0.f, 0.f, 0.f, 0.f}, c2[4] = {0.f, 0.f, 0.f, 0.f};
-            const uint32_t kt = pt * 16u + (lane & 15u);  // this lane's K row (chunk-permuted, kv_swz)
-            const __half *kb = kS + kt * D;
+            for (uint32_t pt = 0; pt < NPT; ++pt)
 #pragma unroll
-            for (uint32_t ks = 0; ks < KS; ++ks) {
-              uint32_t af[4];
-              ldmatrix_x4(af, kb + kv_swz(a.r0 + kt, (lane >> 4) * 8u + ks * 16u, D));
-              mma_f16(c, af, qh[ks][0], qh[ks][1]);
-              mma_f16(c2, af, ql[ks][0], ql[ks][1]);
+              for (int j = 0; j < 4; ++j) c[pt][j] = c2[pt][j] = 0.f;
+#pragma unroll
+            for (uint32_t ks = 0; ks < KS; ++ks)
+#pragma unroll
+              for (uint32_t pt = 0; pt < NPT; ++pt) {
+                const uint32_t kt = pt * 16u + (lane & 15u);  // this lane's K row (chunk-permuted, kv_swz)
+                uint32_t af[4];
+                ldmatrix_x4(af, kS + kt * D + kv_swz(a.r0 + kt, (lane >> 4) * 8u + ks * 16u, D));
+                mma_f16(c[pt], af, qh[ks][0], qh[ks][1]);
+                mma_f16(c2[pt], af, ql[ks][0], ql[ks][1]);
+              }
+#pragma unroll
+            for (uint32_t pt = 0; pt < NPT; ++pt) {
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const uint32_t t = pt * 16u + gq + (j >> 1) * 8u;
+                sc[pt][j] = t < a.len ? __fmul_rn(__fadd_rn(c[pt][j], c2[pt][j]), p.attn_scale) : -INFINITY;
+              }
+              m0 = fmaxf(m0, fmaxf(sc[pt][0], sc[pt][2]));
+              m1 = fmaxf(m1, fmaxf(sc[pt][1], sc[pt][3]));
             }
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const uint32_t t = pt * 16u + gq + (j >> 1) * 8u;
-              sc[pt][j] = t < a.len ? __fmul_rn(__fadd_rn(c[j], c2[j]), p.attn_scale) : -INFINITY;
-            }
-            m0 = fmaxf(m0, fmaxf(sc[pt][0], sc[pt][2]));
-            m1 = fmaxf(m1, fmaxf(sc[pt][1], sc[pt][3]));
           }
           // chunk softmax (softmax.comp) of heads 2tq and 2tq + 1 over the positions
           // of the 8 lanes that share tq
@@ -849,8 +890,7 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_batch_kernel(const __gri
           }
           float l0 = 0.f, l1 = 0.f;
 #pragma unroll
-          for (uint32_t pt = 0; pt < 4; ++pt) {
-            if (pt >= npt) break;
+          for (uint32_t pt = 0; pt < NPT; ++pt) {
 #pragma unroll
             for (int j = 0; j < 4; ++j) {
               const float e = sc[pt][j] == -INFINITY ? 0.f : expf(sc[pt][j] - ((j & 1) ? m1 : m0));
@@ -871,23 +911,31 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_batch_kernel(const __gri
           const size_t pslot = ((size_t)a.n * p.kv_heads + a.kvh) * p.max_chunks + a.c;
           float *po = p.apart + pslot * D * G;
           const uint32_t vt = ((lane >> 4) & 1u) * 8u + (lane & 7u);  // this lane's V row in each 16 (kv_swz)
-#pragma unroll 2
+          uint32_t pbh[NPT][2], pbl[NPT][2];  // P^T B fragments, the same for every dimension tile
+#pragma unroll
+          for (uint32_t kk = 0; kk < NPT; ++kk) {
+            const uint32_t pb = gq * CH + kk * 16u + 2u * tq;
+            pbh[kk][0] = *reinterpret_cast<const uint32_t *>(psh + pb);
+            pbh[kk][1] = *reinterpret_cast<const uint32_t *>(psh + pb + 8u);
+            pbl[kk][0] = *reinterpret_cast<const uint32_t *>(psl + pb);
+            pbl[kk][1] = *reinterpret_cast<const uint32_t *>(psl + pb + 8u);
+          }
+#pragma unroll(KS > 8u ? 2 : 4)
           for (uint32_t dt = 0; dt < KS; ++dt) {
             float o[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-            for (uint32_t kk = 0; kk < 4; ++kk) {
-              if (kk >= npt) break;
+            for (uint32_t kk = 0; kk < NPT; ++kk) {
               uint32_t af[4];
               ldmatrix_x4_trans(af, vS + (kk * 16u + vt) * D +
                                         kv_swz(a.r0 + kk * 16u + vt, dt * 16u + ((lane >> 3) & 1u) * 8u, D));
-              const uint32_t pb = gq * CH + kk * 16u + 2u * tq;
-              mma_f16(o, af, *reinterpret_cast<const uint32_t *>(psh + pb), *reinterpret_cast<const uint32_t *>(psh + pb + 8u));
-              mma_f16(o, af, *reinterpret_cast<const uint32_t *>(psl + pb), *reinterpret_cast<const uint32_t *>(psl + pb + 8u));
+              mma_f16(o, af, pbh[kk][0], pbh[kk][1]);
+              mma_f16(o, af, pbl[kk][0], pbl[kk][1]);
             }
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const uint32_t d = dt * 16u + gq + (j >> 1) * 8u, g = 2u * tq + (j & 1);
-              if (g < G) po[d * G + g] = o[j];
+            // rows d, d + 8 of heads 2tq, 2tq + 1 (G is even)
+            if (2u * tq < G) {
+              const uint32_t d = dt * 16u + gq;
+              *reinterpret_cast<float2 *>(po + d * G + 2u * tq) = make_float2(o[0], o[1]);
+              *reinterpret_cast<float2 *>(po + (d + 8u) * G + 2u * tq) = make_float2(o[2], o[3]);
             }
           }
           if (gq == 0) {

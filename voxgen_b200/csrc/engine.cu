@@ -1052,7 +1052,7 @@ std::string plan_batch(vg_model *m, BatchWork &w) {
   if (!coop) return "the device has no cooperative launch";
   const uint32_t D = c.head_dim, G = c.head_count / c.head_count_kv, H = c.embedding_length;
   if (c.head_count_kv > 8) return strf("%u KV heads (at most 8)", c.head_count_kv);
-  if (G > 8) return strf("%u query heads per KV head (at most 8)", G);
+  if (G > 8 || G % 2) return strf("%u query heads per KV head (an even count up to 8)", G);
   if (c.head_count * D != H) return "the query width differs from the hidden width";
   w.fn = type == GGML_Q8_0 ? pick_batch_dpl<true>(D) : pick_batch_dpl<false>(D);
   if (!w.fn) return strf("head_dim %u", D);
@@ -1073,8 +1073,8 @@ std::string plan_batch(vg_model *m, BatchWork &w) {
   }
   p.slot = kStageSegs * segb;
   // positions per attention unit: 16-row MMA tiles of K and V rows, both in one stage slot
-  p.chunk = std::min<uint32_t>(64u, p.slot / (4u * D)) & ~15u;
-  if (p.chunk == 0) return strf("a stage slot of %u bytes holds no 16 K and V rows of head_dim %u", p.slot, D);
+  p.chunk = batch_chunk(D);
+  if (4u * p.chunk * D > p.slot) return strf("a stage slot of %u bytes holds no %u K and V rows of head_dim %u", p.slot, p.chunk, D);
   p.max_chunks = (c.context_length + p.chunk - 1) / p.chunk;
   const uint32_t grid = (uint32_t)m->ctx->sms;
   if (grid > kBatchMaxRowGroups) return strf("%u SMs (the row-group counters cover %u)", grid, kBatchMaxRowGroups);
