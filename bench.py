@@ -51,6 +51,10 @@ WORKLOADS = {
     # ResidualLM + FSQ + fusion after BaseLM (src/acoustic.rs:851-1035), VoxCPM2's shape
     "residual": dict(acoustic="res_cfg2", prefill=0, ctx=4096,
                      desc="ResidualLM 8L H2048 16x128 GQA 2 KV F6144 F16 + FSQ 512 + fusion"),
+    # batched prefill (vg_prefill_tokens): config[1]'s 128-token prompt, and a longer prompt at
+    # config[2]'s shape; one step is one whole prompt from position 0
+    "prefill": dict(preset="cfg1", prompt=128, desc="prefill of a 128-token prompt, BaseLM 24L H1024 Q8_0"),
+    "prefill_cfg2": dict(preset="cfg2", prompt=512, desc="prefill of a 512-token prompt, BaseLM 28L H2048 Q8_0"),
     # BASELINE cfg4: many streams per GPU, each with its own KV cache (runtime.rs's engines)
     "cfg4": dict(preset="cfg2", streams=16, ctx=4096, slack=256, prefill=2080,
                  desc="16 streams per GPU, BaseLM 28L H2048 Q8_0, ragged KV ~U[64,4096]"),
@@ -557,12 +561,124 @@ def run_batch(args, rank, world, local):
     replicas.shutdown(pg)
 
 
+def run_prefill(args, rank, world, local):
+    """Prompt tokens per second through vg_prefill_tokens: one step is a whole prompt from
+    position 0, runs of up to 16 positions per launch of the batched kernel (one weight pass
+    each). Device-timed with events on the engine's stream; e2e passes the prompt from host
+    memory through the public call and reads the final hidden state back. The same prompt decoded
+    one token per step (the batched kernel switched off for a second copy of the model) is timed
+    beside it."""
+    import ctypes
+
+    import torch
+
+    from voxgen_b200 import api, replicas, synth
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    pg = replicas.init("nccl", world, timeout_s=600, device=dev)
+
+    def barrier():
+        replicas.barrier(pg)
+
+    wl = WORKLOADS[args.workload]
+    spec = synth.preset(wl["preset"])
+    path = ensure_model(spec, rank, world, barrier)
+    n, K, W = wl["prompt"], args.steps, args.warmup
+    toks = np.ascontiguousarray(synth.token_ids(spec, n, seed_index=3500 + rank), np.uint32)
+    tp = toks.ctypes.data_as(ctypes.c_void_p)
+    ctx = api.Context(local)
+    L = api.lib()
+
+    def timed(model, reps, e2e):
+        eng = api.BaseLmEngine(model, n + 8)
+        stream = torch.cuda.ExternalStream(eng.cuda_stream, device=dev)
+        out = np.empty(model.info["embedding_length"], np.float32)
+        for _ in range(W):
+            eng.reset()
+            ctx.check(L.vg_prefill_tokens(eng.h, tp, n, 0))
+        eng.sync()
+        barrier()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(reps):
+            eng.reset()
+            ctx.check(L.vg_prefill_tokens(eng.h, tp, n, 0))
+            if e2e:
+                out[:] = eng.output()
+        b.record(stream)
+        eng.sync(timeout_s=600)
+        torch.cuda.synchronize()
+        barrier()
+        ms = replicas.max_over_ranks(a.elapsed_time(b), pg, dev)
+        eng.close()
+        return ms
+
+    model = api.Model(ctx, path)
+    info = model.info
+    cols = model.batch_columns
+    clocks = ClockSampler(local)
+    ms = timed(model, K, False)
+    clk = clocks.stop()
+    e_ms = timed(model, max(1, min(K, 20)), True)
+    model.close()
+    os.environ["VOXGEN_BATCH_KERNEL"] = "0"     # the same prompt, one decode step per token
+    seq_model = api.Model(ctx, path)
+    seq_reps = max(1, min(K, 5))
+    seq_ms = timed(seq_model, seq_reps, False)
+    seq_model.close()
+    del os.environ["VOXGEN_BATCH_KERNEL"]
+    passes = -(-n // cols) if cols else n
+    kv = info["block_count"] * info["kv_dim"] * 2 * 2
+    wbytes = info["layer_weight_bytes"] + info["norm_weight_bytes"]
+    byt = passes * wbytes + sum(kv * (p + 1) + kv for p in range(n)) + n * info["embedding_length"] * 2
+    step_ms = ms / K
+    peak, peak_kind = measured_peaks()
+    ach = byt / (step_ms * 1e-3) / 1e9
+    line = {
+        "metric": "prefill tok/s", "value": round(world * n * K / (ms / 1e3), 2), "unit": "tok/s", "n_gpus": world,
+        "steps": K, "warmup": W, "ms_per_step": round(step_ms, 5), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"{args.workload}: {wl['desc']}", "prompt_tokens": n, "positions_per_pass": cols,
+                   "weight_passes_per_prompt": passes, "streams_per_gpu": 1,
+                   "parallelism": f"replicas x{world} (weights replicated, no collectives)",
+                   "l2": f"inputs larger than L2: {wbytes / 1e9:.2f} GB of weights per pass",
+                   "input": "seeded token ids"},
+        "roofline": {"kernel": "decode_batch_kernel (up to 16 positions per launch)", "bound": "hbm",
+                     "achieved": round(ach, 1), "peak": peak, "unit": "GB/s", "frac": round(ach / peak, 4),
+                     "traffic": None, "bytes_per_launch": int(byt / passes),
+                     "avg_launch_ms": round(step_ms / passes, 5), "peak_source": f"{peak_kind} hbm_gbs"},
+        "one_token_per_step": {"value": round(world * n * seq_reps / (seq_ms / 1e3), 2),
+                               "unit": "tok/s", "note": "the same prompt through one decode step per token"},
+        "e2e": {"value": round(world * n * max(1, min(K, 20)) / (e_ms / 1e3), 2), "unit": "tok/s",
+                "h2d_bytes_per_step": 4 * n + 960 * passes, "d2h_bytes_per_step": info["embedding_length"] * 4},
+        "gpu_launches": K * passes,
+        "clocks": clk,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline_sample(args, spec, path, {"ctx": n + 80, "prefill": 0})
+        line["cpu_baseline"]["sample"] += "; a prompt is prefilled one decode step per token"
+    ctx.close()
+    if rank == 0:
+        emit(line)
+    replicas.barrier(pg)
+    replicas.shutdown(pg)
+
+
 def main():
     args = parse()
     quiet_stdout()
     rank, world, local = dist_env()
     if args.workload == "cfg4" and args.impl == "ours":
         run_batch(args, rank, world, local)
+        return
+    if args.workload.startswith("prefill"):
+        if args.impl == "reference":
+            if rank == 0:
+                emit({"impl": "reference", "unavailable":
+                      "the prefill workloads have no reference CPU arm (the reference arm covers BaseLM decode)"})
+            return
+        run_prefill(args, rank, world, local)
         return
     if args.workload == "residual":
         if args.impl == "reference":
