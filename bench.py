@@ -530,7 +530,9 @@ def run_batch(args, rank, world, local):
             "workload": f"{args.workload}: {wl['desc']}", "weights": "Q8_0", "streams_per_gpu": S,
             "kv_lengths": [int(x) for x in lens], "step": f"one token for each of the {S} streams",
             "parallelism": f"replicas x{world} (weights replicated, streams partitioned, no collectives)",
-            "l2": f"inputs larger than L2: {info['layer_weight_bytes'] / 1e9:.2f} GB of weights per stream token",
+            "l2": (f"inputs larger than L2: {info['layer_weight_bytes'] / 1e9:.2f} GB of weights per batched step"
+                   if batched else
+                   f"inputs larger than L2: {info['layer_weight_bytes'] / 1e9:.2f} GB of weights per stream token"),
             "input": "seeded token ids",
         },
         "roofline": {"kernel": kname, "bound": "hbm", "achieved": round(launch_ach, 1),
