@@ -80,6 +80,13 @@ def lib() -> C.CDLL:
         L.vgo_swiglu.argtypes = [I, P, P, U32, U32, fp, fp]
         L.vgo_rope.argtypes = [fp, fp, fp, U32, U32, U32, U32, F32, F32]
         L.vgo_attention.argtypes = [fp, P, P, U32, U32, U32, U32, U32, fp, fp]
+        # the RX 7900 XTX mode's variants (the _xtx7900 shaders' summation order)
+        L.vgo_set_xtx.argtypes = [P, I]
+        L.vgo_matvec_xtx.argtypes = L.vgo_matvec.argtypes
+        L.vgo_rmsnorm_xtx.argtypes = L.vgo_rmsnorm.argtypes
+        L.vgo_residual_rmsnorm_xtx.argtypes = L.vgo_residual_rmsnorm.argtypes
+        L.vgo_swiglu_xtx.argtypes = L.vgo_swiglu.argtypes
+        L.vgo_attention_xtx.argtypes = L.vgo_attention.argtypes
         _lib = L
     return _lib
 
@@ -145,7 +152,8 @@ class OracleModel:
 class OracleState:
     """A decode session on the oracle: BaseLmEngine's buffers and KV cache on the CPU."""
 
-    def __init__(self, model: OracleModel, max_context: int):
+    def __init__(self, model: OracleModel, max_context: int, xtx: bool = False):
+        """xtx: follow the RX 7900 XTX mode's shaders (their wave32 summation order)."""
         self.model = model
         h = C.c_void_p()
         rc = lib().vgo_state_create(model.h, max_context, C.byref(h))
@@ -153,6 +161,7 @@ class OracleState:
             raise OracleError(rc, "state create failed")
         self.h = h
         self.max_context = max_context
+        lib().vgo_set_xtx(h, int(xtx))
 
     def close(self):
         if self.h:
@@ -226,10 +235,12 @@ def float_to_half(f: float) -> int:
     return lib().vgo_float_to_half(f)
 
 
-def matvec(dtype: int, raw: np.ndarray, rows: int, cols: int, x: np.ndarray, alpha: float = 1.0):
+def matvec(dtype: int, raw: np.ndarray, rows: int, cols: int, x: np.ndarray, alpha: float = 1.0,
+           xtx: bool = False):
     y = np.empty(rows, np.float32)
     x = np.ascontiguousarray(x, np.float32)
-    lib().vgo_matvec(dtype, vptr(np.ascontiguousarray(raw)), rows, cols, fptr(x), fptr(y), alpha)
+    (lib().vgo_matvec_xtx if xtx else lib().vgo_matvec)(dtype, vptr(np.ascontiguousarray(raw)), rows, cols,
+                                                        fptr(x), fptr(y), alpha)
     return y
 
 
@@ -239,23 +250,24 @@ def embedding(dtype: int, raw: np.ndarray, cols: int, token: int, alpha: float =
     return y
 
 
-def rmsnorm(x: np.ndarray, w: np.ndarray, eps: float):
+def rmsnorm(x: np.ndarray, w: np.ndarray, eps: float, xtx: bool = False):
     y = np.empty_like(x)
-    lib().vgo_rmsnorm(fptr(x), fptr(w), x.size, eps, fptr(y))
+    (lib().vgo_rmsnorm_xtx if xtx else lib().vgo_rmsnorm)(fptr(x), fptr(w), x.size, eps, fptr(y))
     return y
 
 
 def residual_rmsnorm(hidden: np.ndarray, branch: np.ndarray, w: np.ndarray, eps: float,
-                     scale: float):
+                     scale: float, xtx: bool = False):
     h = hidden.copy()
     y = np.empty_like(h)
-    lib().vgo_residual_rmsnorm(fptr(h), fptr(branch), fptr(w), h.size, eps, scale, fptr(y))
+    (lib().vgo_residual_rmsnorm_xtx if xtx else lib().vgo_residual_rmsnorm)(fptr(h), fptr(branch), fptr(w), h.size,
+                                                                          eps, scale, fptr(y))
     return h, y
 
 
-def swiglu(dtype: int, rg: np.ndarray, ru: np.ndarray, rows: int, cols: int, x: np.ndarray):
+def swiglu(dtype: int, rg: np.ndarray, ru: np.ndarray, rows: int, cols: int, x: np.ndarray, xtx: bool = False):
     y = np.empty(rows, np.float32)
-    lib().vgo_swiglu(dtype, vptr(rg), vptr(ru), rows, cols, fptr(x), fptr(y))
+    (lib().vgo_swiglu_xtx if xtx else lib().vgo_swiglu)(dtype, vptr(rg), vptr(ru), rows, cols, fptr(x), fptr(y))
     return y
 
 
@@ -269,11 +281,12 @@ def rope(q: np.ndarray, k: np.ndarray, ext: np.ndarray, position: int, heads: in
 
 
 def attention(q: np.ndarray, k_cache: np.ndarray, v_cache: np.ndarray, heads: int,
-              kv_heads: int, head_dim: int, position: int):
+              kv_heads: int, head_dim: int, position: int, xtx: bool = False):
     """One layer; caches are [ctx][kv_dim] fp16 bits (reference layout)."""
     ctx = k_cache.shape[0]
     scores = np.zeros(heads * ctx, np.float32)
     out = np.empty(heads * head_dim, np.float32)
-    lib().vgo_attention(fptr(q), vptr(k_cache), vptr(v_cache), heads, kv_heads, head_dim, ctx,
+    (lib().vgo_attention_xtx if xtx else lib().vgo_attention)(fptr(q), vptr(k_cache), vptr(v_cache), heads, kv_heads,
+                                                              head_dim, ctx,
                         position, fptr(scores), fptr(out))
     return out, scores.reshape(heads, ctx)

@@ -23,6 +23,8 @@ HERE = Path(__file__).resolve().parent
 LIB = HERE / "_ref" / "libvoxgen_ref.so"
 
 F16, Q8_0 = 1, 8   # dtype_code, src/baselm.rs:1249-1255
+# the shaders the XTX mode swaps for their _xtx7900 variants (same bindings and push constants)
+_XTX = {"rmsnorm", "residual_rmsnorm", "qkv_matvec", "matvec_swiglu", "matvec", "attn_scores", "softmax"}
 
 _lib: Optional[C.CDLL] = None
 
@@ -82,8 +84,11 @@ def effective_scale(v: float) -> float:   # src/baselm.rs:1262-1264
 class RefEngine:
     """One BaseLM decode session on the reference shaders (fp32 buffers, fp16 KV words)."""
 
-    def __init__(self, path, max_context: int):
+    def __init__(self, path, max_context: int, xtx: bool = False):
+        """xtx: record the RX 7900 XTX mode's shaders (the _xtx7900 variants that
+        GpuContext::select_spirv picks, baselm.rs:515-546 and :1241) instead of the normal ones."""
         from oracle import oracle as O
+        self.xtx = xtx
         from voxgen_b200 import gguf
         self.summary = gguf.read_gguf(path)
         om = O.OracleModel(path)   # geometry and metadata scalars (BaseLmConfig::from_gguf)
@@ -105,6 +110,9 @@ class RefEngine:
         self.kv_k = np.zeros(g["layers"] * max_context * KV // 2, np.uint32)
         self.kv_v = np.zeros_like(self.kv_k)
         self.position = 0
+
+    def shader(self, name: str) -> str:
+        return f"{name}_xtx7900" if self.xtx and name in _XTX else name
 
     def t(self, name: str):
         return self.summary.tensors[name]
@@ -132,15 +140,15 @@ class RefEngine:
 
     # ---- dispatch helpers (src/baselm.rs:1054-1202) ----
     def rms(self, w: str) -> None:
-        dispatch("rmsnorm", [self.model, self.hidden, self.norm], push("IIf", self.off(w), self.g["H"], self.eps), [1])
+        dispatch(self.shader("rmsnorm"), [self.model, self.hidden, self.norm], push("IIf", self.off(w), self.g["H"], self.eps), [1])
 
     def residual_rms(self, w: str) -> None:
-        dispatch("residual_rmsnorm", [self.model, self.hidden, self.branch, self.norm],
+        dispatch(self.shader("residual_rmsnorm"), [self.model, self.hidden, self.branch, self.norm],
                  push("IIff", self.off(w), self.g["H"], self.eps, effective_scale(self.res_scale)), [1])
 
     def matvec(self, w: str, x: np.ndarray, y: np.ndarray, rows: int, cols: int, alpha: float) -> None:
         assert self.t(w).dims == (cols, rows)
-        dispatch("matvec", [self.model, x, y], push("IIIIIf", self.off(w), rows, cols, self.dtype(w), 0, alpha), [rows])
+        dispatch(self.shader("matvec"), [self.model, x, y], push("IIIIIf", self.off(w), rows, cols, self.dtype(w), 0, alpha), [rows])
 
     def record_transformer(self, position: int, logits: bool) -> None:
         g = self.g
@@ -151,7 +159,7 @@ class RefEngine:
         for l in range(g["layers"]):
             n = lambda s: f"blk.{l}.{s}"
             qw, kw, vw = n("attn_q.weight"), n("attn_k.weight"), n("attn_v.weight")
-            dispatch("qkv_matvec", [self.model, self.norm, self.q, self.k, self.v],
+            dispatch(self.shader("qkv_matvec"), [self.model, self.norm, self.q, self.k, self.v],
                      push("IIIIIIIIII", self.off(qw), self.off(kw), self.off(vw), H, KV, H,
                           self.dtype(qw), self.dtype(kw), self.dtype(vw), 0), [H + 2 * KV])
             dispatch("rope", [self.model, self.q, self.k],
@@ -159,13 +167,13 @@ class RefEngine:
                      [heads + kvh])
             dispatch("store_kv", [self.k, self.v, self.kv_k, self.kv_v], push("IIII", l, position, self.ctx, KV), [1])
             attn = push("IIIIII", l, self.ctx, position, D, heads // kvh, kvh)
-            dispatch("attn_scores", [self.q, self.kv_k, self.scores], attn, [position + 1, heads])
-            dispatch("softmax", [self.scores], push("II", self.ctx, position), [heads])
+            dispatch(self.shader("attn_scores"), [self.q, self.kv_k, self.scores], attn, [position + 1, heads])
+            dispatch(self.shader("softmax"), [self.scores], push("II", self.ctx, position), [heads])
             dispatch("attn_values", [self.scores, self.kv_v, self.attention], attn, [heads])
             self.matvec(n("attn_output.weight"), self.attention, self.branch, H, H, 1.0)
             self.residual_rms(n("ffn_norm.weight"))
             gw, uw = n("ffn_gate.weight"), n("ffn_up.weight")
-            dispatch("matvec_swiglu", [self.model, self.norm, self.gate],
+            dispatch(self.shader("matvec_swiglu"), [self.model, self.norm, self.gate],
                      push("IIIIII", self.off(gw), self.off(uw), F, H, self.dtype(gw), 0), [F])
             self.matvec(n("ffn_down.weight"), self.gate, self.branch, H, F, 1.0)
             nxt = f"blk.{l + 1}.attn_norm.weight" if l + 1 < g["layers"] else "output_norm.weight"

@@ -44,6 +44,11 @@ DEFAULT_REFERENCE = ORACLE.parent.parent / "reference"
 SHADERS = ["embedding", "rmsnorm", "residual_rmsnorm", "qkv_matvec", "rope", "store_kv",
            "attn_scores", "softmax", "attn_values", "matvec", "matvec_swiglu",
            "linear_bias", "fsq_quantize", "fusion_linear"]
+# The RX 7900 XTX mode swaps these for their _xtx7900 variants (GpuContext::select_spirv at
+# baselm.rs:515-546 and :1241): the same bindings and push constants, wave32 subgroup reductions.
+XTX_SHADERS = ["rmsnorm", "residual_rmsnorm", "qkv_matvec", "matvec_swiglu", "matvec",
+               "attn_scores", "softmax"]
+SHADERS += [f"{s}_xtx7900" for s in XTX_SHADERS]
 
 _BUF = re.compile(r"layout\s*\(([^)]*)\)\s*((?:(?:readonly|writeonly|coherent|restrict|volatile)\s+)*)"
                   r"buffer\s+(\w+)\s*\{\s*(\w+)\s+(\w+)\s*\[\s*\]\s*;\s*\}\s*(\w+)\s*;")
@@ -60,6 +65,7 @@ def translate(name: str, src: str) -> str:
     """C++ for one shader: the rewritten declarations and the unchanged body in namespace
     vgref_<name>, plus its exported dispatch function."""
     text = re.sub(r"^\s*#version[^\n]*\n", "", src, flags=re.M)
+    text = re.sub(r"^\s*#extension[^\n]*\n", "", text, flags=re.M)
     m = _LOCAL.search(text)
     if not m:
         raise ValueError(f"{name}: no local_size_x")

@@ -22,7 +22,14 @@
 struct vec2 {
   float x, y;
   vec2() = default;
+  explicit vec2(float a) : x(a), y(a) {}
   vec2(float a, float b) : x(a), y(b) {}
+  vec2 operator+(const vec2 &o) const { return vec2(x + o.x, y + o.y); }
+  vec2 &operator+=(const vec2 &o) {
+    x += o.x;
+    y += o.y;
+    return *this;
+  }
 };
 
 extern "C" {
@@ -76,3 +83,12 @@ inline uvec3 vgref_global_id(uint local_size_x) {
 #define gl_WorkGroupID (::vgref::group_id())
 #define gl_NumWorkGroups (::vgref::num_groups())
 #define shared static thread_local
+
+// Subgroups (GL_KHR_shader_subgroup_basic / _arithmetic) of 32 invocations:
+// the _xtx7900 shaders' wave32 reductions (see workgroup.h for the order).
+#define gl_SubgroupSize 32u
+#define gl_SubgroupInvocationID (::vgref::local_id().x & 31u)
+#define gl_SubgroupID (::vgref::local_id().x >> 5)
+#define gl_NumSubgroups ((vgref_local_size + 31u) / 32u)
+inline float subgroupAdd(float v) { return vgref::subgroup_add(v); }
+inline float subgroupMax(float v) { return vgref::subgroup_max(v); }

@@ -62,6 +62,8 @@ struct Fiber {
   void *sp = nullptr;
   uvec3 lid{0, 0, 0};
   bool done = false;
+  uint32_t bar = 0;   // workgroup barriers this invocation has reached
+  uint32_t sgop = 0;  // subgroup operations this invocation has entered
   std::vector<uint8_t> stack;
 };
 
@@ -69,6 +71,7 @@ struct Worker {
   void *sched_sp = nullptr;
   std::vector<Fiber> fibers;
   uint32_t cur = 0;
+  float sg[2][1024];  // subgroup operands, double-buffered by operation parity
   void (*fn)() = nullptr;
   uvec3 wg{0, 0, 0}, nwg{1, 1, 1};
 };
@@ -115,6 +118,8 @@ void run_group(Worker &w) {
   for (uint32_t i = 0; i < n; ++i) {
     w.fibers[i].done = false;
     w.fibers[i].lid = uvec3{i, 0, 0};
+    w.fibers[i].sgop = 0;
+    w.fibers[i].bar = 0;
   }
   bool live = true;
   while (live) {
@@ -133,10 +138,57 @@ void run_group(Worker &w) {
 const uvec3 &local_id() { return tw->fibers[tw->cur].lid; }
 const uvec3 &group_id() { return tw->wg; }
 const uvec3 &num_groups() { return tw->nwg; }
+// An invocation at barrier() runs on only once every live invocation of the
+// workgroup has reached it (so subgroup operations inside subgroup-uniform
+// branches, which switch fibers a different number of times, cannot skew
+// the workgroup's barriers).
 void barrier() {
   Worker *w = tw;
-  vgref_switch(&w->fibers[w->cur].sp, w->sched_sp);
+  const uint32_t target = ++w->fibers[w->cur].bar;
+  for (;;) {
+    bool all = true;
+    for (const Fiber &o : w->fibers)
+      if (!o.done && o.bar < target) {
+        all = false;
+        break;
+      }
+    if (all) return;
+    vgref_switch(&w->fibers[w->cur].sp, w->sched_sp);
+  }
 }
+
+// Every invocation of the subgroup deposits its operand and switches fibers
+// until the other 31 have deposited theirs, then reduces the 32 operands.
+// Consecutive operations use the two buffers in turn: an invocation can enter
+// operation k + 2 only after all of its subgroup entered k + 1, that is after
+// they read operation k's operands.
+namespace {
+template <bool MAX>
+float subgroup_reduce(float v) {
+  Worker *w = tw;
+  const uint32_t me = w->cur, lane = w->fibers[me].lid.x, base = lane & ~31u;
+  const uint32_t buf = w->fibers[me].sgop++ & 1u, target = w->fibers[me].sgop;
+  w->sg[buf][lane] = v;
+  for (;;) {
+    bool all = true;
+    for (uint32_t i = base; i < base + 32u && i < w->fibers.size(); ++i)
+      if (!w->fibers[i].done && w->fibers[i].sgop < target) {
+        all = false;
+        break;
+      }
+    if (all) break;
+    vgref_switch(&w->fibers[me].sp, w->sched_sp);
+  }
+  float t[32];
+  const float *src = w->sg[buf] + base;
+  for (int i = 0; i < 32; ++i) t[i] = src[i];
+  for (int s = 1; s < 32; s <<= 1)
+    for (int i = 0; i < 32; i += 2 * s) t[i] = MAX ? (t[i] < t[i + s] ? t[i + s] : t[i]) : t[i] + t[i + s];
+  return t[0];
+}
+}  // namespace
+float subgroup_add(float v) { return subgroup_reduce<false>(v); }
+float subgroup_max(float v) { return subgroup_reduce<true>(v); }
 
 void set_threads(int n) { g_threads = n; }
 

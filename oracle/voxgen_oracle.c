@@ -324,6 +324,187 @@ void vgo_attention(const float *q, const uint16_t *k_cache, const uint16_t *v_ca
 }
 
 /* ------------------------------------------------------------------------ */
+/* RX 7900 XTX mode: the _xtx7900 shader variants (baselm.rs:515-546, :1241). */
+/* A lane sums its strided share in order; a workgroup reduction is a wave32   */
+/* subgroup sum per wave, the waves' sums in shared memory, then one more      */
+/* subgroup sum in wave 0 over waves[i] (i < number of waves, else 0). The     */
+/* order inside a subgroup sum is not fixed by GLSL; it is taken as the        */
+/* balanced pairwise tree over the 32 invocations (what a shuffle-xor          */
+/* butterfly computes), the same assumption as the shader emulation that pins  */
+/* this restatement.                                                           */
+/* ------------------------------------------------------------------------ */
+static float xtx_tree32(float *t, int is_max) {
+  for (int st = 1; st < 32; st <<= 1)
+    for (int i = 0; i < 32; i += 2 * st) t[i] = is_max ? (t[i] < t[i + st] ? t[i + st] : t[i]) : t[i] + t[i + st];
+  return t[0];
+}
+/* reduce_sum / red / rmax of the xtx shaders over nl (128 or 256) lane values */
+static float xtx_reduce(const float *lanes, uint32_t nl, int is_max) {
+  float waves[8], t[32];
+  const uint32_t nw = nl / 32u;
+  for (uint32_t w = 0; w < nw; ++w) {
+    for (int i = 0; i < 32; ++i) t[i] = lanes[w * 32u + i];
+    waves[w] = xtx_tree32(t, is_max);
+  }
+  for (uint32_t i = 0; i < 32u; ++i) t[i] = i < nw ? waves[i] : (is_max ? -3.402823466e+38f : 0.0f);
+  return xtx_tree32(t, is_max);
+}
+/* One lane's sum of a row (matvec_xtx7900.comp:14-15): columns 4 lane .. 4 lane + 3,
+ * then + 1024; Q8_0 as d * (q0 x0 + q1 x1 + q2 x2 + q3 x3), F16 element by element. */
+static float xtx_lane(int dtype, const uint8_t *w, uint32_t cols, uint32_t row, const float *x,
+                      uint32_t lane) {
+  float s = 0.0f;
+  for (uint32_t c = lane * 4u; c < cols; c += 1024u) {
+    if (dtype == GGML_F16) {
+      const uint8_t *rb = w + (size_t)row * cols * 2u + (size_t)c * 2u;
+      s += ld_f16(rb) * x[c];
+      if (c + 1u < cols) s += ld_f16(rb + 2) * x[c + 1u];
+      if (c + 2u < cols) s += ld_f16(rb + 4) * x[c + 2u];
+      if (c + 3u < cols) s += ld_f16(rb + 6) * x[c + 3u];
+    } else {
+      const uint8_t *base = w + ((size_t)row * (cols / 32u) + c / 32u) * 34u;
+      const float d = ld_f16(base);
+      const int8_t *q = (const int8_t *)(base + 2u + (c & 31u));
+      s += d * ((float)q[0] * x[c] + (float)q[1] * x[c + 1u] + (float)q[2] * x[c + 2u] +
+                (float)q[3] * x[c + 3u]);
+    }
+  }
+  return s;
+}
+static float xtx_dot(int dtype, const uint8_t *w, uint32_t cols, uint32_t row, const float *x) {
+  float lanes[256];
+  for (uint32_t lane = 0; lane < 256u; ++lane) lanes[lane] = xtx_lane(dtype, w, cols, row, x, lane);
+  return xtx_reduce(lanes, 256u, 0);
+}
+
+/* matvec_xtx7900.comp: y[row] = total * alpha. */
+void vgo_matvec_xtx(int dtype, const uint8_t *w, uint32_t rows, uint32_t cols, const float *x,
+                    float *y, float alpha) {
+#pragma omp parallel for schedule(static) num_threads(vgo_get_threads())
+  for (long r = 0; r < (long)rows; ++r) y[r] = xtx_dot(dtype, w, cols, (uint32_t)r, x) * alpha;
+}
+
+/* qkv_matvec_xtx7900.comp: the same row sums, written without alpha. */
+static void qkv_matvec_xtx(int dtype_q, const uint8_t *wq, int dtype_k, const uint8_t *wk,
+                           int dtype_v, const uint8_t *wv, uint32_t q_rows, uint32_t kv_rows,
+                           uint32_t cols, const float *x, float *q, float *k, float *v) {
+  const long total = (long)q_rows + 2L * kv_rows;
+#pragma omp parallel for schedule(static) num_threads(vgo_get_threads())
+  for (long cr = 0; cr < total; ++cr) {
+    const uint32_t r = (uint32_t)cr;
+    if (r < q_rows) q[r] = xtx_dot(dtype_q, wq, cols, r, x);
+    else if (r < q_rows + kv_rows) k[r - q_rows] = xtx_dot(dtype_k, wk, cols, r - q_rows, x);
+    else v[r - q_rows - kv_rows] = xtx_dot(dtype_v, wv, cols, r - q_rows - kv_rows, x);
+  }
+}
+
+/* matvec_swiglu_xtx7900.comp: gate and up summed together per lane (vec2), Q8_0 as
+ * the sum of four (d q x) terms added to the lane's sum; y = (g / (1 + exp(-g))) * u. */
+void vgo_swiglu_xtx(int dtype, const uint8_t *wg, const uint8_t *wu, uint32_t rows, uint32_t cols,
+                    const float *x, float *y) {
+#pragma omp parallel for schedule(static) num_threads(vgo_get_threads())
+  for (long r = 0; r < (long)rows; ++r) {
+    float lg[256], lu[256];
+    for (uint32_t lane = 0; lane < 256u; ++lane) {
+      float sg = 0.0f, su = 0.0f;
+      for (uint32_t c = lane * 4u; c < cols; c += 1024u) {
+        if (dtype == GGML_F16) {
+          const uint8_t *gr = wg + ((size_t)r * cols + c) * 2u, *ur = wu + ((size_t)r * cols + c) * 2u;
+          for (uint32_t j = 0; j < 4u; ++j) {
+            if (c + j >= cols) break;
+            const float xj = x[c + j];
+            sg += ld_f16(gr + 2u * j) * xj;
+            su += ld_f16(ur + 2u * j) * xj;
+          }
+        } else {
+          const size_t blk = ((size_t)r * (cols / 32u) + c / 32u) * 34u;
+          const float gd = ld_f16(wg + blk), ud = ld_f16(wu + blk);
+          const int8_t *gq = (const int8_t *)(wg + blk + 2u + (c & 31u));
+          const int8_t *uq = (const int8_t *)(wu + blk + 2u + (c & 31u));
+          float tg = gd * (float)gq[0] * x[c], tu = ud * (float)uq[0] * x[c];
+          for (uint32_t j = 1; j < 4u; ++j) {
+            tg = tg + gd * (float)gq[j] * x[c + j];
+            tu = tu + ud * (float)uq[j] * x[c + j];
+          }
+          sg += tg;
+          su += tu;
+        }
+      }
+      lg[lane] = sg;
+      lu[lane] = su;
+    }
+    const float g = xtx_reduce(lg, 256u, 0), u = xtx_reduce(lu, 256u, 0);
+    y[r] = (g / (1.0f + expf(-g))) * u;
+  }
+}
+
+/* rmsnorm_xtx7900.comp / residual_rmsnorm_xtx7900.comp: lane-strided sums of
+ * squares (stride 256), the wave reduction, then x * inv_rms * w. */
+static float xtx_sumsq(const float *x, uint32_t n) {
+  float lanes[256];
+  for (uint32_t lane = 0; lane < 256u; ++lane) {
+    float s = 0.0f;
+    for (uint32_t k = lane; k < n; k += 256u) s += x[k] * x[k];
+    lanes[lane] = s;
+  }
+  return xtx_reduce(lanes, 256u, 0);
+}
+void vgo_rmsnorm_xtx(const float *x, const float *w, uint32_t n, float eps, float *y) {
+  const float inv = 1.0f / sqrtf(xtx_sumsq(x, n) / (float)n + eps);
+  for (uint32_t i = 0; i < n; ++i) y[i] = x[i] * inv * w[i];
+}
+void vgo_residual_rmsnorm_xtx(float *hidden, const float *branch, const float *w, uint32_t n,
+                              float eps, float scale, float *y) {
+  for (uint32_t i = 0; i < n; ++i) hidden[i] = hidden[i] + scale * branch[i];
+  const float inv = 1.0f / sqrtf(xtx_sumsq(hidden, n) / (float)n + eps);
+  for (uint32_t i = 0; i < n; ++i) y[i] = hidden[i] * inv * w[i];
+}
+
+/* attn_scores_xtx7900.comp (128 lanes, lane = dimension, head_dim <= 128) +
+ * softmax_xtx7900.comp (256 lanes, max then sum of exp) + attn_values.comp. */
+void vgo_attention_xtx(const float *q, const uint16_t *k_cache, const uint16_t *v_cache,
+                       uint32_t heads, uint32_t kv_heads, uint32_t head_dim, uint32_t ctx,
+                       uint32_t position, float *scores, float *out) {
+  const uint32_t kv_dim = kv_heads * head_dim, q_per_kv = heads / kv_heads;
+  const float scale = 1.0f / sqrtf((float)head_dim);
+#pragma omp parallel for collapse(2) schedule(static) num_threads(vgo_get_threads())
+  for (long qh = 0; qh < (long)heads; ++qh)
+    for (long t = 0; t <= (long)position; ++t) {
+      float lanes[128];
+      const uint32_t kvh = (uint32_t)qh / q_per_kv;
+      for (uint32_t lane = 0; lane < 128u; ++lane)
+        lanes[lane] = lane < head_dim ? q[qh * head_dim + lane] *
+                                            vgo_half_to_float(k_cache[(size_t)t * kv_dim + kvh * head_dim + lane])
+                                      : 0.0f;
+      scores[qh * ctx + t] = xtx_reduce(lanes, 128u, 0) * scale;
+    }
+  for (uint32_t head = 0; head < heads; ++head) {
+    float *s = scores + (size_t)head * ctx, lanes[256];
+    for (uint32_t lane = 0; lane < 256u; ++lane) {
+      float m = -3.402823466e+38f;
+      for (uint32_t t = lane; t <= position; t += 256u) m = m < s[t] ? s[t] : m;
+      lanes[lane] = m;
+    }
+    const float gmax = xtx_reduce(lanes, 256u, 1);
+    for (uint32_t lane = 0; lane < 256u; ++lane) {
+      float sum = 0.0f;
+      for (uint32_t t = lane; t <= position; t += 256u) sum += expf(s[t] - gmax);
+      lanes[lane] = sum;
+    }
+    const float inv_sum = 1.0f / xtx_reduce(lanes, 256u, 0);
+    for (uint32_t t = 0; t <= position; ++t) s[t] = expf(s[t] - gmax) * inv_sum;
+  }
+#pragma omp parallel for collapse(2) schedule(static) num_threads(vgo_get_threads())
+  for (long qh = 0; qh < (long)heads; ++qh)
+    for (long d = 0; d < (long)head_dim; ++d) {
+      const uint32_t kvh = (uint32_t)qh / q_per_kv;
+      float acc = 0.0f;
+      for (uint32_t t = 0; t <= position; ++t)
+        acc += scores[qh * ctx + t] * vgo_half_to_float(v_cache[(size_t)t * kv_dim + kvh * head_dim + d]);
+      out[qh * head_dim + d] = acc;
+    }
+}
+/* ------------------------------------------------------------------------ */
 /* GGUF reader: restates load_summary (src/gguf.rs:222-286).                 */
 /* ------------------------------------------------------------------------ */
 typedef struct {
@@ -653,8 +834,11 @@ struct vgo_state {
   uint32_t ctx, position;
   float *hidden, *norm, *q, *k, *v, *attention, *gate, *branch, *logits, *scores;
   uint16_t *kv_k, *kv_v; /* [layer][ctx][kv_dim] */
+  int xtx;               /* record the RX 7900 XTX mode's shader variants */
   char err[256];
 };
+
+void vgo_set_xtx(vgo_state *s, int on) { s->xtx = on != 0; }
 
 int vgo_state_create(const vgo_model *m, uint32_t max_context, vgo_state **out) {
   *out = NULL;
@@ -732,11 +916,14 @@ static int record_transformer(vgo_state *s, int compute_logits) {
     return -4;
   }
   const float *ext = tf32(m, m->rope_factors);
-  vgo_rmsnorm(s->hidden, tf32(m, m->attn_norm[0]), m->H, m->eps, s->norm);
+  /* the XTX mode swaps rmsnorm, residual_rmsnorm, qkv_matvec, matvec_swiglu,
+   * matvec, attn_scores and softmax for their _xtx7900 variants */
+  const int x = s->xtx;
+  (x ? vgo_rmsnorm_xtx : vgo_rmsnorm)(s->hidden, tf32(m, m->attn_norm[0]), m->H, m->eps, s->norm);
   for (uint32_t l = 0; l < m->L; ++l) {
-    qkv_matvec((int)m->wq[l]->type, tdata(m, m->wq[l]), (int)m->wk[l]->type, tdata(m, m->wk[l]),
-               (int)m->wv[l]->type, tdata(m, m->wv[l]), m->H, m->kv_dim, m->H, s->norm, s->q,
-               s->k, s->v);
+    (x ? qkv_matvec_xtx : qkv_matvec)((int)m->wq[l]->type, tdata(m, m->wq[l]), (int)m->wk[l]->type,
+                                      tdata(m, m->wk[l]), (int)m->wv[l]->type, tdata(m, m->wv[l]), m->H,
+                                      m->kv_dim, m->H, s->norm, s->q, s->k, s->v);
     vgo_rope(s->q, s->k, ext, pos, m->heads, m->kv_heads, m->head_dim, m->theta, m->scaling);
     /* store_kv.comp:16-24 */
     uint16_t *kl = s->kv_k + (size_t)l * s->ctx * m->kv_dim;
@@ -745,19 +932,22 @@ static int record_transformer(vgo_state *s, int compute_logits) {
       kl[(size_t)pos * m->kv_dim + j] = vgo_float_to_half(s->k[j]);
       vl[(size_t)pos * m->kv_dim + j] = vgo_float_to_half(s->v[j]);
     }
-    vgo_attention(s->q, kl, vl, m->heads, m->kv_heads, m->head_dim, s->ctx, pos, s->scores,
-                  s->attention);
-    vgo_matvec((int)m->wo[l]->type, tdata(m, m->wo[l]), m->H, m->H, s->attention, s->branch, 1.0f);
-    vgo_residual_rmsnorm(s->hidden, s->branch, tf32(m, m->ffn_norm[l]), m->H, m->eps, rs, s->norm);
-    vgo_swiglu((int)m->wg[l]->type, tdata(m, m->wg[l]), tdata(m, m->wu[l]), m->F, m->H, s->norm,
-               s->gate);
-    vgo_matvec((int)m->wd[l]->type, tdata(m, m->wd[l]), m->H, m->F, s->gate, s->branch, 1.0f);
+    (x ? vgo_attention_xtx : vgo_attention)(s->q, kl, vl, m->heads, m->kv_heads, m->head_dim, s->ctx, pos,
+                                            s->scores, s->attention);
+    (x ? vgo_matvec_xtx : vgo_matvec)((int)m->wo[l]->type, tdata(m, m->wo[l]), m->H, m->H, s->attention,
+                                      s->branch, 1.0f);
+    (x ? vgo_residual_rmsnorm_xtx : vgo_residual_rmsnorm)(s->hidden, s->branch, tf32(m, m->ffn_norm[l]), m->H,
+                                                          m->eps, rs, s->norm);
+    (x ? vgo_swiglu_xtx : vgo_swiglu)((int)m->wg[l]->type, tdata(m, m->wg[l]), tdata(m, m->wu[l]), m->F, m->H,
+                                      s->norm, s->gate);
+    (x ? vgo_matvec_xtx : vgo_matvec)((int)m->wd[l]->type, tdata(m, m->wd[l]), m->H, m->F, s->gate,
+                                      s->branch, 1.0f);
     const float *next = l + 1 < m->L ? tf32(m, m->attn_norm[l + 1]) : tf32(m, m->out_norm);
-    vgo_residual_rmsnorm(s->hidden, s->branch, next, m->H, m->eps, rs, s->norm);
+    (x ? vgo_residual_rmsnorm_xtx : vgo_residual_rmsnorm)(s->hidden, s->branch, next, m->H, m->eps, rs, s->norm);
   }
   if (compute_logits)
-    vgo_matvec((int)m->out->type, tdata(m, m->out), m->vocab, m->H, s->norm, s->logits,
-               eff(m->logit_scale));
+    (x ? vgo_matvec_xtx : vgo_matvec)((int)m->out->type, tdata(m, m->out), m->vocab, m->H, s->norm,
+                                      s->logits, eff(m->logit_scale));
   return 0;
 }
 

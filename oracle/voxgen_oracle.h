@@ -58,6 +58,19 @@ const float *vgo_buffer(const vgo_state *s, const char *name);
 const char *vgo_last_error(const vgo_state *s);
 
 void vgo_set_threads(int n);
+/* The RX 7900 XTX mode (the _xtx7900 shader variants' summation order) for
+ * every later step of this state. */
+void vgo_set_xtx(vgo_state *s, int on);
+void vgo_matvec_xtx(int dtype, const uint8_t *w, uint32_t rows, uint32_t cols, const float *x,
+                    float *y, float alpha);
+void vgo_swiglu_xtx(int dtype, const uint8_t *wg, const uint8_t *wu, uint32_t rows, uint32_t cols,
+                    const float *x, float *y);
+void vgo_rmsnorm_xtx(const float *x, const float *w, uint32_t n, float eps, float *y);
+void vgo_residual_rmsnorm_xtx(float *hidden, const float *branch, const float *w, uint32_t n,
+                              float eps, float scale, float *y);
+void vgo_attention_xtx(const float *q, const uint16_t *k_cache, const uint16_t *v_cache,
+                       uint32_t heads, uint32_t kv_heads, uint32_t head_dim, uint32_t ctx,
+                       uint32_t position, float *scores, float *out);
 int vgo_get_threads(void);
 
 /* ---- shader-level restatements (raw GGUF tensor bytes) ---- */

@@ -2,7 +2,9 @@
 shaders (compiled as C++ by oracle/ref_shim, run on the CPU) on the seeded synthetic models
 "pin" (Q8_0) and "pin_f16" (F16, untied output, non-unit scales).
 
-Run where the reference checkout is available:  python tests/golden/make_ref_pin.py
+Run where the reference checkout is available:  python tests/golden/make_ref_pin.py [--xtx]
+With --xtx the same session runs the RX 7900 XTX mode's shader variants (the _xtx7900 files,
+subgroup sums emulated as a pairwise tree over 32 invocations) into ref_shader_pin_xtx.npz.
 The session is run_session below: 20 prefilled KV positions, two steps from external embeddings,
 then two token steps with logits. The file also records each model file's SHA-256, so a change
 of the synthetic-model generator is caught instead of silently comparing different weights.
@@ -21,6 +23,7 @@ if str(ROOT) not in sys.path:
 from voxgen_b200 import synth  # noqa: E402
 
 OUT = Path(__file__).resolve().parent / "ref_shader_pin.npz"
+OUT_XTX = Path(__file__).resolve().parent / "ref_shader_pin_xtx.npz"
 CONTEXT = 48
 
 
@@ -39,20 +42,21 @@ def run_session(spec, eng):
     return outs
 
 
-def main():
+def main(xtx: bool = False):
     from oracle import ref as R
     arrays = {}
     with tempfile.TemporaryDirectory() as d:
         for name in ("pin", "pin_f16"):
             spec = synth.preset(name)
             path = synth.model_path(spec, Path(d))
-            outs = run_session(spec, R.RefEngine(path, CONTEXT))
+            outs = run_session(spec, R.RefEngine(path, CONTEXT, xtx=xtx))
             arrays[f"{name}_hidden"] = np.stack([h for h, _ in outs])
             arrays[f"{name}_logits"] = np.stack([lg for _, lg in outs if lg is not None])
             arrays[f"{name}_sha256"] = np.array(hashlib.sha256(path.read_bytes()).hexdigest())
-    np.savez_compressed(OUT, **arrays)
-    print(f"wrote {OUT}")
+    out = OUT_XTX if xtx else OUT
+    np.savez_compressed(out, **arrays)
+    print(f"wrote {out}")
 
 
 if __name__ == "__main__":
-    main()
+    main("--xtx" in sys.argv[1:])

@@ -16,11 +16,13 @@ def _ordinal(bits):
 class Pair:
     """The same session on the CUDA engine and on the oracle."""
 
-    def __init__(self, ctx, path, max_context):
+    def __init__(self, ctx, path, max_context, xtx=False):
+        """xtx: the oracle follows the reference's RX 7900 XTX mode (its _xtx7900 shaders'
+        summation order) instead of the normal shaders."""
         self.model = api.Model(ctx, path)
         self.eng = api.BaseLmEngine(self.model, max_context)
         self.om = O.OracleModel(path)
-        self.ost = O.OracleState(self.om, max_context)
+        self.ost = O.OracleState(self.om, max_context, xtx=xtx)
 
     def write_kv(self, k, v):
         self.eng.write_kv(k, v)

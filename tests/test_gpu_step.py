@@ -244,3 +244,19 @@ def test_decode_batch_matches_single_streams(ctx, model_dir, monkeypatch):
     for e in engines + solo:
         e.close()
     m.close()
+
+
+@pytest.mark.parametrize("name,prefill", [("pin", 300), ("cfg2", 1500)])
+def test_matches_xtx_mode_oracle(ctx, model_dir, name, prefill):
+    """The same tolerance against the reference's RX 7900 XTX mode (the _xtx7900 shaders'
+    wave32 summation order, restated by the oracle and pinned to those shaders in
+    test_cpu_ref_pin_xtx.py): one CUDA result is within tolerance of a reference run in either
+    mode."""
+    spec = synth.preset(name)
+    p = Pair(ctx, spec_path(model_dir, name), prefill + 8, xtx=True)
+    k, v = synth.kv_prefill(spec, prefill)
+    p.write_kv(k, v)
+    for i, t in enumerate(synth.token_ids(spec, 3, seed_index=88)):
+        p.step_token(t)
+        p.compare(f"{name} XTX-mode step {i}")
+    p.close()
