@@ -71,6 +71,10 @@ struct Worker {
   void *sched_sp = nullptr;
   std::vector<Fiber> fibers;
   uint32_t cur = 0;
+  uint32_t nlive = 0;          // invocations of the workgroup still running
+  uint32_t bar_n[4] = {};      // arrivals at barrier k, in slot k % 4
+  uint32_t sg_n[32][4] = {};   // deposits of subgroup s for its operation k, in slot [s][k % 4]
+  bool sg_used = false;        // sg_n holds counts of the previous workgroup
   float sg[2][1024];  // subgroup operands, double-buffered by operation parity
   void (*fn)() = nullptr;
   uvec3 wg{0, 0, 0}, nwg{1, 1, 1};
@@ -88,6 +92,7 @@ int g_threads = 0;
     Fiber &f = w->fibers[w->cur];
     w->fn();
     f.done = true;
+    --w->nlive;
     vgref_switch(&f.sp, w->sched_sp);
   }
 }
@@ -121,6 +126,12 @@ void run_group(Worker &w) {
     w.fibers[i].sgop = 0;
     w.fibers[i].bar = 0;
   }
+  w.nlive = n;
+  std::memset(w.bar_n, 0, sizeof w.bar_n);
+  if (w.sg_used) {
+    std::memset(w.sg_n, 0, sizeof w.sg_n);
+    w.sg_used = false;
+  }
   bool live = true;
   while (live) {
     live = false;
@@ -142,19 +153,15 @@ const uvec3 &num_groups() { return tw->nwg; }
 // workgroup has reached it (so subgroup operations inside subgroup-uniform
 // branches, which switch fibers a different number of times, cannot skew
 // the workgroup's barriers).
+// Invocations are at most one barrier apart (none passes barrier k before all
+// reached it), so four arrival slots suffice: arriving at k clears slot k + 2,
+// whose last use, barrier k - 2, every invocation has passed.
 void barrier() {
   Worker *w = tw;
-  const uint32_t target = ++w->fibers[w->cur].bar;
-  for (;;) {
-    bool all = true;
-    for (const Fiber &o : w->fibers)
-      if (!o.done && o.bar < target) {
-        all = false;
-        break;
-      }
-    if (all) return;
-    vgref_switch(&w->fibers[w->cur].sp, w->sched_sp);
-  }
+  const uint32_t k = ++w->fibers[w->cur].bar;
+  w->bar_n[(k + 2u) & 3u] = 0;
+  ++w->bar_n[k & 3u];
+  while (w->bar_n[k & 3u] < w->nlive) vgref_switch(&w->fibers[w->cur].sp, w->sched_sp);
 }
 
 // Every invocation of the subgroup deposits its operand and switches fibers
@@ -166,19 +173,14 @@ namespace {
 template <bool MAX>
 float subgroup_reduce(float v) {
   Worker *w = tw;
-  const uint32_t me = w->cur, lane = w->fibers[me].lid.x, base = lane & ~31u;
-  const uint32_t buf = w->fibers[me].sgop++ & 1u, target = w->fibers[me].sgop;
+  const uint32_t me = w->cur, lane = w->fibers[me].lid.x, base = lane & ~31u, sgi = lane >> 5;
+  const uint32_t k = w->fibers[me].sgop++, buf = k & 1u;
+  const uint32_t width = w->fibers.size() - base < 32u ? (uint32_t)w->fibers.size() - base : 32u;
   w->sg[buf][lane] = v;
-  for (;;) {
-    bool all = true;
-    for (uint32_t i = base; i < base + 32u && i < w->fibers.size(); ++i)
-      if (!w->fibers[i].done && w->fibers[i].sgop < target) {
-        all = false;
-        break;
-      }
-    if (all) break;
-    vgref_switch(&w->fibers[me].sp, w->sched_sp);
-  }
+  w->sg_used = true;
+  w->sg_n[sgi][(k + 2u) & 3u] = 0;
+  ++w->sg_n[sgi][k & 3u];
+  while (w->sg_n[sgi][k & 3u] < width) vgref_switch(&w->fibers[me].sp, w->sched_sp);
   float t[32];
   const float *src = w->sg[buf] + base;
   for (int i = 0; i < 32; ++i) t[i] = src[i];
