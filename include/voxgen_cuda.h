@@ -297,7 +297,7 @@ int vg_stream_profile_step(vg_stream *stream, uint32_t token, int want_logits,
 int vg_decode_batch(vg_stream *const *streams, int n, const uint32_t *tokens);
 /* 16 when vg_decode_batch and vg_prefill_tokens can use the batched step
  * kernel for this model (one weight format for every projection, cooperative
- * launch, head_dim 32-256, at most 8 KV heads, query width = hidden width,
+ * launch, head_dim 32, 64 or 128, at most 8 KV heads, query width = hidden width,
  * VOXGEN_BATCH_KERNEL not 0), else 0 with the reason in vg_last_error. The
  * first call plans the kernel and allocates its workspace (about 70 MB at the
  * BaseLM backbone's shape with a 32768-position context). */

@@ -466,7 +466,7 @@ enum : uint32_t { kBkQkv = 0, kBkO = 1, kBkGu = 2, kBkDown = 3 };
 
 // Positions of a batched attention unit for head_dim D: 16-row MMA tiles of K
 // and V rows that fit one stage slot together (a slot holds 16 KiB or more).
-__host__ __device__ constexpr uint32_t batch_chunk(uint32_t D) { return D >= 256u ? 16u : D >= 128u ? 32u : 64u; }
+__host__ __device__ constexpr uint32_t batch_chunk(uint32_t D) { return D >= 128u ? 32u : 64u; }
 
 // aux bytes of an attention phase: every warp's P of its unit (hi and lo,
 // [8 heads][chunk] fp16), or a merge slice's chunk weights [max_chunks][8]

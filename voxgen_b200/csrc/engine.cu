@@ -994,8 +994,9 @@ BatchFn pick_batch_dpl(uint32_t head_dim) {
     case 32: return decode_batch_kernel<Q8, 1>;
     case 64: return decode_batch_kernel<Q8, 2>;
     case 128: return decode_batch_kernel<Q8, 4>;
-    case 256: return decode_batch_kernel<Q8, 8>;
   }
+  // a warp's attention unit at head_dim 256 would spill its output tile; such
+  // models step each stream with its own launch
   return nullptr;
 }
 
@@ -1055,7 +1056,7 @@ std::string plan_batch(vg_model *m, BatchWork &w) {
   if (G > 8 || G % 2) return strf("%u query heads per KV head (an even count up to 8)", G);
   if (c.head_count * D != H) return "the query width differs from the hidden width";
   w.fn = type == GGML_Q8_0 ? pick_batch_dpl<true>(D) : pick_batch_dpl<false>(D);
-  if (!w.fn) return strf("head_dim %u", D);
+  if (!w.fn) return strf("head_dim %u (the batched kernel takes 32, 64 or 128)", D);
   BatchParams &p = w.p;
   p = BatchParams{};
   const Layer &L0 = m->layers[0];
