@@ -283,7 +283,7 @@ __device__ __forceinline__ bool batch_produce(const MvRing &R, const uint8_t *w,
       if (!ring_claim(R, rp, nq * SEGB, abort_flag, err)) return false;
       uint8_t *dst = R.ring + rp.slot * R.slot;
       for (uint32_t j = 0; j < nq; ++j)
-        bulk_g2s(dst + j * SEGB, w + ((uint64_t)(b.t0 + 4u * q + j) * NS + b.s0 + sgi) * SEGB, SEGB, &R.full[rp.slot]);
+        bulk_g2s_stream(dst + j * SEGB, w + ((uint64_t)(b.t0 + 4u * q + j) * NS + b.s0 + sgi) * SEGB, SEGB, &R.full[rp.slot]);
       rp.next(R.nst);
     }
   }
@@ -611,8 +611,8 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_batch_kernel(const __gri
               if (!live) break;
               if (bytes) {
                 uint8_t *dst = R.ring + rp.slot * R.slot;
-                bulk_g2s(dst, cl.kc + off, bytes, &R.full[rp.slot]);
-                bulk_g2s(dst + p.chunk * D * 2u, cl.vc + off, bytes, &R.full[rp.slot]);
+                bulk_g2s_stream(dst, cl.kc + off, bytes, &R.full[rp.slot]);
+                bulk_g2s_stream(dst + p.chunk * D * 2u, cl.vc + off, bytes, &R.full[rp.slot]);
               }
               rp.next(R.nst);
             }

@@ -159,6 +159,21 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
       : "memory");
 }
 
+// The same copy with an L2 evict-first policy, for data read once per step
+// (weights, cached K/V rows): it leaves L2 to the partial sums and vectors
+// that other CTAs read back within the step. The batched step kernel streams
+// with it (its split-K and attention partials otherwise stay dirty in L2 until
+// the weight stream evicts them to DRAM); the single-stream kernel, whose
+// partials are few, measured no gain from it.
+__device__ __forceinline__ void bulk_g2s_stream(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+  asm volatile(
+      "{\n\t.reg .b64 pol;\n\t"
+      "createpolicy.fractional.L2::evict_first.b64 pol, 1.0;\n\t"
+      "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], pol;\n\t}"
+      ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
 // Programmatic dependent launch (PDL).
 __device__ __forceinline__ void pdl_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
