@@ -433,10 +433,11 @@ def run_residual(args, rank, world, local):
 def run_batch(args, rank, world, local):
     """cfg4: S streams per GPU over one model, each with its own KV cache prefilled to a seeded
     ragged length ~U[64, 4096]. A step advances every stream by one token through
-    vg_decode_batch (each stream's step on its own CUDA stream; the weights are read once per
-    stream). value = tokens of all streams on all ranks / device time (events on every engine
-    stream, max over streams and ranks). e2e copies the S token ids from host memory and reads
-    the S output hidden states back every step."""
+    vg_decode_batch: one launch of the batched step kernel reads the weights once for all the
+    streams (or, for a model that kernel does not take, one step-kernel launch per stream).
+    value = tokens of all streams on all ranks / device time (events on every engine stream, max
+    over streams and ranks). e2e copies the S token ids from host memory and reads the S output
+    hidden states back every step, with one wait for all of them (vg_copy_outputs)."""
     import torch
 
     from voxgen_b200 import api, replicas, synth
@@ -479,8 +480,7 @@ def run_batch(args, rank, world, local):
         for row in rows:
             api.decode_batch(engs, [int(t) for t in row])   # S token ids from host memory
             if read_back:
-                for e in engs:
-                    e.output()                                # D2H of each stream's hidden state
+                api.outputs(engs)                             # D2H of every stream's hidden state, one wait
         for st, ev in zip(streams, ends):
             ev.record(st)
         for e in engs:

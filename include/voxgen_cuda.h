@@ -252,6 +252,15 @@ int vg_stream_output(const vg_stream *stream, const float **device_hidden);
 int vg_stream_logits(const vg_stream *stream, const float **device_logits);
 /* Waits for the stream's work (bounded) and copies n floats to host memory. */
 int vg_copy_output(vg_stream *stream, float *host, size_t n);
+/* The final hidden states of n streams after a batched step, stream i's first
+ * n_each floats into host[i * n_each ..]: every device-to-host copy is enqueued
+ * before the first wait, so a caller stepping many streams (vg_decode_batch)
+ * pays one round trip instead of n. Each stream's device error flag comes back
+ * with its copy and is cleared; VG_EDEVICE names the first stream that had one
+ * (the other streams' outputs are still copied). No counterpart in the
+ * reference, which reads each engine's result separately
+ * (BaseLmEngine::collect_result, src/baselm.rs:1204-1231). */
+int vg_copy_outputs(vg_stream *const *streams, int n, float *host, size_t n_each);
 int vg_copy_logits(vg_stream *stream, float *host, size_t n);
 /* Bounded wait for all enqueued work: VG_ETIMEDOUT after timeout_ns, and
  * VG_EDEVICE when a kernel raised the device error flag (which is cleared). */

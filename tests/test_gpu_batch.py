@@ -114,3 +114,18 @@ def test_batch_then_reset_and_errors(ctx, model_dir):
     assert err.value.code == -6
     assert [e.position for e in s.eng] == [1, 1, 40]
     s.close()
+
+
+def test_copy_outputs_reads_every_stream(ctx, model_dir):
+    """vg_copy_outputs after batched steps: the n hidden states with one wait, equal bit for bit
+    to each stream's own vg_copy_output, and within tolerance of the oracle."""
+    spec = synth.preset("tiny")
+    s = Streams(ctx, spec, spec_path(model_dir, "tiny"), [3, 0, 17, 40, 9], 64)
+    for r, row in enumerate(synth.token_ids(spec, 10, seed_index=4400).reshape(2, 5)):
+        s.batch_step(row)
+        got = api.outputs(s.eng)
+        assert got.shape == (5, spec.hidden)
+        for i, (e, o) in enumerate(zip(s.eng, s.ost)):
+            assert np.array_equal(got[i].view(np.uint32), e.output().view(np.uint32)), f"stream {i}"
+            assert_close(got[i], o.output(), what=f"batched read of stream {i} after step {r}")
+    s.close()

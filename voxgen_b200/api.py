@@ -34,7 +34,7 @@ EXPORTS = [
     "vg_stream_destroy", "vg_stream_reset", "vg_stream_position", "vg_stream_cuda_stream", "vg_stream_kernel_mode",
     "vg_stream_write_kv", "vg_stream_read_kv", "vg_decode_token", "vg_decode_embedding",
     "vg_decode_embedding_device", "vg_prefill_tokens", "vg_stream_output", "vg_stream_logits",
-    "vg_copy_output", "vg_copy_logits", "vg_stream_sync", "vg_step_result_get", "vg_benchmark",
+    "vg_copy_output", "vg_copy_outputs", "vg_copy_logits", "vg_stream_sync", "vg_step_result_get", "vg_benchmark",
     "vg_stream_profile_step", "vg_decode_batch", "vg_k_packed_bytes", "vg_k_repack", "vg_k_matvec", "vg_k_embedding",
     "vg_k_residual_rmsnorm", "vg_k_attention", "vg_k_attention_noalloc",
     "vg_residual_load_gguf", "vg_residual_step", "vg_residual_step_host", "vg_residual_state",
@@ -120,6 +120,7 @@ def lib() -> C.CDLL:
         "vg_decode_embedding_device": ([P, P, I], I), "vg_prefill_tokens": ([P, P, U32, I], I),
         "vg_stream_output": ([P, PP], I), "vg_stream_logits": ([P, PP], I),
         "vg_copy_output": ([P, P, SZ], I), "vg_copy_logits": ([P, P, SZ], I),
+        "vg_copy_outputs": ([P, I, P, SZ], I),
         "vg_stream_sync": ([P, U64], I),
         "vg_step_result_get": ([P, U32, C.POINTER(StepResult), C.POINTER(TopLogit)], I),
         "vg_benchmark": ([P, U32, U32, U32, I, C.POINTER(BenchmarkResult)], I),
@@ -431,6 +432,18 @@ def decode_batch(engines: Sequence[BaseLmEngine], tokens: Sequence[int]) -> None
     rc = lib().vg_decode_batch(arr, len(engines), _ptr(t))
     if rc:
         engines[0]._check(rc)
+
+
+def outputs(engines: Sequence[BaseLmEngine]) -> np.ndarray:
+    """The final hidden states of several sessions, [n, H], with one wait for all the copies
+    (vg_copy_outputs): the read-back of a batched step."""
+    H = engines[0].H
+    out = np.empty((len(engines), H), np.float32)
+    arr = (C.c_void_p * len(engines))(*[e.h for e in engines])
+    rc = lib().vg_copy_outputs(arr, len(engines), _ptr(out), H)
+    if rc:
+        engines[0]._check(rc)
+    return out
 
 
 class ResidualEngine(BaseLmEngine):

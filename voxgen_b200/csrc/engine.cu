@@ -1963,6 +1963,50 @@ int vg_copy_output(vg_stream *s, float *host, size_t n) {
   return copy_out(s, s->out_norm, host, n, s->m->cfg.embedding_length);
 }
 
+int vg_copy_outputs(vg_stream *const *streams, int n, float *host, size_t n_each) {
+  if (!streams || n <= 0 || (!host && n_each)) return VG_EINVAL;
+  for (int i = 0; i < n; ++i)
+    if (!live(streams[i])) return VG_ESTATE;
+  vg_ctx *ctx = streams[0]->m->ctx;
+  return guard(ctx, [&] {
+    for (int i = 0; i < n; ++i)
+      if (n_each > streams[i]->m->cfg.embedding_length)
+        fail(VG_EINVAL, strf("stream %d: requested %zu floats, its output holds %u", i, n_each,
+                             streams[i]->m->cfg.embedding_length));
+    // every copy is enqueued before the first wait, so the n round trips overlap
+    for (int i = 0; i < n; ++i) {
+      vg_stream *s = streams[i];
+      CK(cudaSetDevice(s->m->ctx->device));
+      const size_t bytes = (size_t)((uint8_t *)(s->ctrl + kCtrlWords) - (uint8_t *)s->out_norm);
+      CK(cudaMemcpyAsync(s->pin_out, s->out_norm, bytes, cudaMemcpyDeviceToHost, s->st));
+      CK(cudaEventRecord(s->ev_done, s->st));
+    }
+    for (int i = 0; i < n; ++i) {
+      const int rc = host_wait(streams[i]->ev_done, 30ull * 1000000000ull);
+      if (rc) fail(rc, strf("stream %d: output copy did not finish within the timeout", i));
+    }
+    int first_bad = -1;
+    uint32_t bad_flag = 0;
+    for (int i = 0; i < n; ++i) {
+      vg_stream *s = streams[i];
+      uint32_t flag;
+      std::memcpy(&flag, s->pin_out + ((uint8_t *)(s->ctrl + kCtrlErr) - (uint8_t *)s->out_norm), 4);
+      if (flag) {
+        CK(cudaSetDevice(s->m->ctx->device));
+        CK(cudaMemset(s->ctrl + kCtrlErr, 0, 4));
+        if (first_bad < 0) {
+          first_bad = i;
+          bad_flag = flag;
+        }
+      }
+      std::memcpy(host + (size_t)i * n_each, s->pin_out, n_each * 4);
+    }
+    if (first_bad >= 0)
+      fail(VG_EDEVICE, strf("stream %d: a kernel raised device error flag 0x%x", first_bad, bad_flag));
+    return VG_OK;
+  });
+}
+
 int vg_copy_logits(vg_stream *s, float *host, size_t n) {
   if (!live(s)) return VG_ESTATE;
   if (!host && n) return VG_EINVAL;
