@@ -16,7 +16,7 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libvoxgen_b200.so"
 SOURCES = [CSRC / "engine.cu", CSRC / "gguf_loader.cpp"]
-HEADERS = [CSRC / "kernels.cuh", CSRC / "step_kernel.cuh", CSRC / "ptx.cuh", CSRC / "gguf_loader.h", ROOT / "include" / "voxgen_cuda.h"]
+HEADERS = sorted(CSRC.glob("*.cuh")) + sorted(CSRC.glob("*.h")) + sorted((ROOT / "include").glob("*.h"))
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ["-O3", "-std=c++17", "-lineinfo", "--expt-relaxed-constexpr", "-Xcompiler", "-fPIC",
