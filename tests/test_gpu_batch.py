@@ -80,11 +80,13 @@ def test_batch_16_ragged_streams(ctx, model_dir, name):
     s.close()
 
 
-@pytest.mark.parametrize("name,n", [("tiny", 3), ("tiny", 9), ("tiny_f16", 16), ("pin", 5), ("pin_f16", 16), ("cfg1", 16)])
+@pytest.mark.parametrize("name,n", [("tiny", 3), ("tiny", 9), ("tiny_f16", 16), ("pin", 5), ("pin_f16", 16), ("cfg1", 16),
+                                    ("g6", 16), ("g6", 4)])
 def test_batch_small_models(ctx, model_dir, name, n):
     """Fewer columns than 16 (one or two n8 tiles), streams at position 0 and at chunk boundaries,
-    ragged matrix widths (F = 608: the last column group reaches into the padding), GQA 4,
-    head_dim 32 / 64 / 128, F16 and Q8_0, several batched steps."""
+    ragged matrix widths (F = 608: the last column group reaches into the padding), GQA 2, 4
+    and 6, head_dim 32 / 64 / 128, F16 and Q8_0, merge slices 16 and 32 dimensions wide, several
+    batched steps."""
     spec = synth.preset(name)
     lens = [0, 63, 64, 65, 127, 128, 129, 200, 1, 300, 17, 33, 250, 301, 99, 5][:n]
     s = Streams(ctx, spec, spec_path(model_dir, name), lens, 320)
@@ -92,6 +94,19 @@ def test_batch_small_models(ctx, model_dir, name, n):
     for r, row in enumerate(toks):
         s.batch_step(row)
         s.compare(f"{name} x{n} batched step {r}")
+    s.close()
+
+
+def test_batch_long_contexts(ctx, model_dir):
+    """Streams past 4096 positions: more than 128 attention chunks per (stream, KV head), so the
+    merge's (max, sum) pass reads chunks beyond the ones each thread keeps in registers."""
+    spec = synth.preset("pin")
+    lens = [4190, 10, 4300]
+    s = Streams(ctx, spec, spec_path(model_dir, "pin"), lens, 4400)
+    toks = synth.token_ids(spec, 6, seed_index=4400).reshape(2, 3)
+    for r, row in enumerate(toks):
+        s.batch_step(row)
+        s.compare(f"pin long contexts batched step {r}")
     s.close()
 
 

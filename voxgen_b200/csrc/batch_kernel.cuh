@@ -82,6 +82,7 @@ struct BatchParams {
   float rope_scaling, eps, res_scale, emb_scale, attn_scale;
   uint32_t H, F, heads, kv_heads, head_dim;
   uint32_t chunk, max_chunks;  // attention positions per unit; partial slots per (column, KV head)
+  uint32_t merge_dw;           // dimensions of a merge slice (batch_merge_width)
   // shared-memory plan (BatchSmem)
   uint32_t nst, slot, aux_bytes;
 };
@@ -470,11 +471,24 @@ __host__ __device__ constexpr uint32_t batch_chunk(uint32_t D) { return D >= 128
 
 // aux bytes of an attention phase: every warp's P of its unit (hi and lo,
 // [8 heads][chunk] fp16), or a merge slice's chunk weights [max_chunks][8]
-// followed by [32][8] partial maxima / sums (also [2][128] output halves).
+// followed by [32][8] partial maxima, [32][8] partial sums and the parts'
+// outputs (at most 4 floats per thread).
 __host__ __device__ inline uint32_t batch_attn_bytes(uint32_t chunk, uint32_t max_chunks) {
   const uint32_t units = kMvConsumers * 2u * 8u * chunk * 2u;
-  const uint32_t merge = (max_chunks * 8u + 8u + kMvConsumers * 32u * 4u) * 4u;
+  const uint32_t merge = (max_chunks * 8u + 2u * 256u + kMvConsumers * 32u * 4u) * 4u;
   return units > merge ? units : merge;
+}
+
+// Dimensions of a merge slice for S columns: the narrowest of 16, 32, ...,
+// head_dim whose (column, KV head, slice) count fits the grid, so each CTA
+// merges one slice at most, as long as a slice's threads (width x group / 4
+// heads loaded at once) fit the CTA.
+__host__ __device__ inline uint32_t batch_merge_width(uint32_t S, uint32_t kv_heads, uint32_t D, uint32_t G,
+                                                      uint32_t grid) {
+  const uint32_t gv = G % 4u == 0 ? G / 4u : G / 2u;
+  uint32_t dw = 16u;
+  while (dw < D && 2u * dw * gv <= kMvConsumers * 32u && S * kv_heads * (D / dw) > grid) dw *= 2u;
+  return dw;
 }
 
 // Attention unit u of a batched step: units are ordered by column, KV head,
@@ -952,83 +966,111 @@ __global__ void __launch_bounds__(kMvThreads, 1) decode_batch_kernel(const __gri
       }
       if (!more) break;
     }
-    // merge slices (column n, KV head, dimensions 16 db .. 16 db + 15):
-    // o = sum_c exp(m_c - M) o_c / sum_c exp(m_c - M) l_c over the unit chunks
-    float *sW = reinterpret_cast<float *>(aux);            // [max_chunks][8] chunk weights
-    float *sL = sW + p.max_chunks * 8u;                    // [8] 1 / sum of weights x sums per head
-    float *sP = sL + 8u;                                   // [32][8] partial maxima / sums, then the parts' outputs
-    for (uint32_t m = gridDim.x - 1u - blockIdx.x; m < S * p.kv_heads * KS; m += gridDim.x) {
-      const uint32_t n = m / (p.kv_heads * KS), rem = m - n * p.kv_heads * KS, kvh = rem / KS, db = rem - kvh * KS;
+    // merge slices (column n, KV head, dimensions DW db .. DW db + DW - 1, DW =
+    // p.merge_dw, chosen per launch so that the slices fit the grid):
+    // o = sum_c exp(m_c - M) o_c / sum_c exp(m_c - M) l_c over the unit chunks.
+    // Each thread loads its first chunks' outputs before the weights are known,
+    // and keeps its (max, sum) pairs in registers for the second pass.
+    const uint32_t DW = p.merge_dw, NSL = D / DW;
+    // thread (dimension DW db + dl, heads hq*VW .. hq*VW + VW - 1, chunk part cp)
+    // loads VW heads of one dimension at once; the parts are added in order
+    const uint32_t VW = G % 4u == 0 ? 4u : 2u, GV = G / VW, TPR = DW * GV, NPART = NCT / TPR;
+    const uint32_t rr = tid % TPR, cp = tid / TPR, dl = rr / GV, hq = rr % GV;
+    const uint32_t g = tid & 7u, part = tid >> 3;  // the (max, sum) pass: 32 parts of the chunks per head
+    float *sW = reinterpret_cast<float *>(aux);    // [max_chunks][8] chunk weights
+    float *sM = sW + p.max_chunks * 8u;            // [32][8] partial maxima
+    float *sS = sM + 256u;                         // [32][8] partial sums
+    float *so = sS + 256u;                         // [NPART][DW x G] the parts' outputs
+    for (uint32_t m = gridDim.x - 1u - blockIdx.x; m < S * p.kv_heads * NSL; m += gridDim.x) {
+      const uint32_t n = m / (p.kv_heads * NSL), rem = m - n * p.kv_heads * NSL, kvh = rem / NSL, db = rem - kvh * NSL;
       const uint32_t nch = cnch[n];
       if (tid == 0 && !grid_wait(p.ready + n * p.kv_heads + kvh,
                                  srdy[n * p.kv_heads + kvh] + (unsigned long long)(l + 1u) * nch, err))
         set_error(err, kErrGridWait);
+      // (the previous slice's last reads of sM / sS / so come before this barrier)
       named_bar(1, NCT);
       const size_t hb = ((size_t)n * p.kv_heads + kvh) * p.max_chunks;
-      const uint32_t g = tid & 7u, part = tid >> 3;  // 32 parts of the chunks per head
+      const float *ob = p.apart + (hb * D + db * DW + dl) * G + hq * VW;
+      auto load = [&](uint32_t c) {
+        const float *src = ob + (size_t)c * D * G;
+        if (VW == 4u) return __ldcg(reinterpret_cast<const float4 *>(src));
+        const float2 x = __ldcg(reinterpret_cast<const float2 *>(src));
+        return make_float4(x.x, x.y, 0.f, 0.f);
+      };
+      constexpr uint32_t MR = 4u, MLR = 4u;
+      float4 v[MR];
+#pragma unroll
+      for (uint32_t i = 0; i < MR; ++i) {
+        const uint32_t c = cp + i * NPART;
+        v[i] = cp < NPART && c < nch ? load(c) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      float2 ml[MLR];
       float M = -INFINITY;
+#pragma unroll
+      for (uint32_t i = 0; i < MLR; ++i) {
+        const uint32_t c = part + 32u * i;
+        ml[i] = g < G && c < nch ? __ldcg(&p.apart_ml[(hb + c) * G + g]) : make_float2(-INFINITY, 0.f);
+        M = fmaxf(M, ml[i].x);
+      }
       if (g < G)
-        for (uint32_t c = part; c < nch; c += 32u) M = fmaxf(M, __ldcg(&p.apart_ml[(hb + c) * G + g]).x);
-      sP[part * 8u + g] = M;
+        for (uint32_t c = part + 32u * MLR; c < nch; c += 32u) M = fmaxf(M, __ldcg(&p.apart_ml[(hb + c) * G + g]).x);
+      sM[part * 8u + g] = M;
       named_bar(1, NCT);
       M = -INFINITY;
 #pragma unroll 8
-      for (uint32_t q2 = 0; q2 < 32u; ++q2) M = fmaxf(M, sP[q2 * 8u + g]);
+      for (uint32_t q2 = 0; q2 < 32u; ++q2) M = fmaxf(M, sM[q2 * 8u + g]);
       float Lp = 0.f;
-      if (g < G)
-        for (uint32_t c = part; c < nch; c += 32u) {
-          const float2 ml = __ldcg(&p.apart_ml[(hb + c) * G + g]);
-          const float w = ml.x == -INFINITY ? 0.f : expf(ml.x - M);
+#pragma unroll
+      for (uint32_t i = 0; i < MLR; ++i) {
+        const uint32_t c = part + 32u * i;
+        if (g < G && c < nch) {
+          const float w = ml[i].x == -INFINITY ? 0.f : expf(ml[i].x - M);
           sW[c * 8u + g] = w;
-          Lp = fmaf(w, ml.y, Lp);
+          Lp = fmaf(w, ml[i].y, Lp);
         }
-      named_bar(1, NCT);
-      sP[part * 8u + g] = Lp;
-      named_bar(1, NCT);
-      if (tid < 8u) {
-        float L = 0.f;
-        for (uint32_t q2 = 0; q2 < 32u; ++q2) L += sP[q2 * 8u + tid];
-        sL[tid] = 1.0f / L;
       }
-      named_bar(1, NCT);  // sP reuse
-      // outputs: thread (dimension 16 db + dl, heads hq*VW .. hq*VW + VW - 1, chunk part)
-      // loads VW heads of one dimension at once, 4 chunks in flight; the parts
-      // are added in order
-      const uint32_t VW = G >= 4u ? 4u : G, TPR = 16u * (G / VW), NPART = NCT / TPR;
-      const uint32_t rr = tid % TPR, cp = tid / TPR, dl = rr / (G / VW), hq = rr % (G / VW);
-      const float *ob = p.apart + (hb * D + db * 16u + dl) * G + hq * VW;
-      float acc[4] = {0.f, 0.f, 0.f, 0.f};
-      auto add = [&](uint32_t c) {
-        const float *src = ob + (size_t)c * D * G;
-        const float *w = sW + c * 8u + hq * VW;
-        if (VW == 4u) {
-          const float4 x = __ldcg(reinterpret_cast<const float4 *>(src));
+      if (g < G)
+        for (uint32_t c = part + 32u * MLR; c < nch; c += 32u) {
+          const float2 m2 = __ldcg(&p.apart_ml[(hb + c) * G + g]);
+          const float w = m2.x == -INFINITY ? 0.f : expf(m2.x - M);
+          sW[c * 8u + g] = w;
+          Lp = fmaf(w, m2.y, Lp);
+        }
+      sS[part * 8u + g] = Lp;
+      named_bar(1, NCT);
+      if (cp < NPART) {
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        auto add = [&](uint32_t c, const float4 &x) {
+          const float *w = sW + c * 8u + hq * VW;
           acc[0] = fmaf(w[0], x.x, acc[0]);
           acc[1] = fmaf(w[1], x.y, acc[1]);
-          acc[2] = fmaf(w[2], x.z, acc[2]);
-          acc[3] = fmaf(w[3], x.w, acc[3]);
-        } else {
-          for (uint32_t v = 0; v < VW; ++v) acc[v] = fmaf(w[v], __ldcg(src + v), acc[v]);
+          if (VW == 4u) {
+            acc[2] = fmaf(w[2], x.z, acc[2]);
+            acc[3] = fmaf(w[3], x.w, acc[3]);
+          }
+        };
+#pragma unroll
+        for (uint32_t i = 0; i < MR; ++i)
+          if (cp + i * NPART < nch) add(cp + i * NPART, v[i]);
+        uint32_t c = cp + MR * NPART;
+        for (; c + 3u * NPART < nch; c += 4u * NPART) {
+          const float4 x0 = load(c), x1 = load(c + NPART), x2 = load(c + 2u * NPART), x3 = load(c + 3u * NPART);
+          add(c, x0);
+          add(c + NPART, x1);
+          add(c + 2u * NPART, x2);
+          add(c + 3u * NPART, x3);
         }
-      };
-      uint32_t c = cp;
-      for (; c + 3u * NPART < nch; c += 4u * NPART) {
-        add(c);
-        add(c + NPART);
-        add(c + 2u * NPART);
-        add(c + 3u * NPART);
+        for (; c < nch; c += NPART) add(c, load(c));
+        for (uint32_t vv = 0; vv < VW; ++vv) so[cp * DW * G + dl * G + hq * VW + vv] = acc[vv];
       }
-      for (; c < nch; c += NPART) add(c);
-      float *so = sP;  // [NPART][16 dims x G heads]
-      for (uint32_t v = 0; v < VW; ++v) so[cp * 16u * G + dl * G + hq * VW + v] = acc[v];
       named_bar(1, NCT);
-      if (tid < 16u * G) {
-        const uint32_t dd = db * 16u + tid / G, gd = tid % G;
-        float o = 0.f;
-        for (uint32_t q2 = 0; q2 < NPART; ++q2) o += so[q2 * 16u * G + tid];
-        p.attn[(size_t)n * p.H + ((size_t)kvh * G + gd) * D + dd] = o * sL[gd];
+      for (uint32_t i = tid; i < DW * G; i += NCT) {
+        const uint32_t dd = db * DW + i / G, gd = i % G;
+        float L = 0.f, o = 0.f;
+        for (uint32_t q2 = 0; q2 < 32u; ++q2) L += sS[q2 * 8u + gd];
+        for (uint32_t q2 = 0; q2 < NPART; ++q2) o += so[q2 * DW * G + i];
+        p.attn[(size_t)n * p.H + ((size_t)kvh * G + gd) * D + dd] = o * (1.0f / L);
       }
-      named_bar(1, NCT);  // sW / sP reuse
     }
     arrive();
   };

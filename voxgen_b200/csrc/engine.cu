@@ -1217,6 +1217,7 @@ void batch_launch(BatchWork &w, const std::vector<BatchCol> &cols, const std::ve
   CK(cudaEventRecord(w.pin_ev[i], w.st));
   BatchParams p = w.p;
   p.S = (uint32_t)cols.size();
+  p.merge_dw = batch_merge_width(p.S, p.kv_heads, p.head_dim, p.heads / p.kv_heads, w.grid);
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(w.grid);
   cfg.blockDim = dim3(kMvThreads);

@@ -79,6 +79,8 @@ PRESETS: Dict[str, ModelSpec] = {
     "pin": ModelSpec("pin", 2, 256, 2, 1, 128, 512, 96, GGML_Q8_0, seed=31),
     "pin_f16": ModelSpec("pin_f16", 2, 256, 2, 1, 128, 512, 96, GGML_F16, seed=32, tied_output=False,
                          embedding_scale=12.0, residual_scale=0.25, logit_scale=0.125),
+    # groups of 6 query heads per KV head (the batched merge then loads 2 heads at a time)
+    "g6": ModelSpec("g6", 2, 1536, 12, 2, 128, 608, 512, GGML_Q8_0, seed=14),
     # projections in two formats (a Q8_0 model whose down projections are F16, which
     # validate_baselm accepts, src/gguf.rs:135-148): a model the persistent step kernel does not
     # take, so it runs the per-kernel program
