@@ -194,12 +194,13 @@ def test_backbone_outlier_channels(ctx, model_dir, name):
     p.close()
 
 
-@pytest.mark.parametrize("name", ["tiny", "tiny_f16", "pin"])
+@pytest.mark.parametrize("name", ["tiny", "tiny_f16", "pin", "g6"])
 def test_attention_merge_long_context(ctx, model_dir, name):
     """Contexts long enough that the attention units outnumber the CTAs left free for the merge
     slices (tiny: 188 units on 148 CTAs, so some CTAs run two units and the last eight run a
     unit and then a slice), and that a slice loads its chunks' rows in more than one batch
-    (pin: 94 chunks of one KV head at head_dim 128, 64 rows per batch)."""
+    (pin: 94 chunks of one KV head at head_dim 128, 64 rows per batch); g6: groups of 6 query
+    heads, which fill 6 of a unit's 8 head columns."""
     spec = synth.preset(name)
     n = 6000
     p = Pair(ctx, spec_path(model_dir, name), n + 8)
