@@ -93,7 +93,7 @@ def test_embedding_shader(dtype):
 
 
 @needs_ref
-@pytest.mark.parametrize("heads,kv_heads", [(16, 2), (2, 1), (4, 4)])
+@pytest.mark.parametrize("heads,kv_heads", [(16, 2), (2, 1), (4, 4), (12, 2)])
 @pytest.mark.parametrize("position", [0, 5, 300])
 def test_rope_and_attention_shaders(heads, kv_heads, position):
     D, ctx = 128, 320
@@ -144,9 +144,10 @@ def _session(name, tmp):
 
 
 @needs_ref
-@pytest.mark.parametrize("name", ["pin", "pin_f16"])
+@pytest.mark.parametrize("name", ["pin", "pin_f16", "g6"])
 def test_decode_steps_bit_exact(tmp_path_factory, name):
-    """Whole decode steps: embedding input, token input with logits, the KV cache."""
+    """Whole decode steps: embedding input, token input with logits, the KV cache (g6: groups of 6
+    query heads per KV head)."""
     spec, path = _session(name, tmp_path_factory.mktemp("pin"))
     ref = R.RefEngine(path, 48)
     om = O.OracleModel(path)
