@@ -1,6 +1,7 @@
 """Generates ref_shader_pin.npz: hidden states and logits computed by the reference's own BaseLM
 shaders (compiled as C++ by oracle/ref_shim, run on the CPU) on the seeded synthetic models
-"pin" (Q8_0) and "pin_f16" (F16, untied output, non-unit scales).
+"pin" (Q8_0), "pin_f16" (F16, untied output, non-unit scales) and "g6" (Q8_0, groups of 6 query
+heads per KV head).
 
 Run where the reference checkout is available:  python tests/golden/make_ref_pin.py [--xtx]
 With --xtx the same session runs the RX 7900 XTX mode's shader variants (the _xtx7900 files,
@@ -25,6 +26,7 @@ from voxgen_b200 import synth  # noqa: E402
 OUT = Path(__file__).resolve().parent / "ref_shader_pin.npz"
 OUT_XTX = Path(__file__).resolve().parent / "ref_shader_pin_xtx.npz"
 CONTEXT = 48
+MODELS = ("pin", "pin_f16", "g6")
 
 
 def run_session(spec, eng):
@@ -46,7 +48,7 @@ def main(xtx: bool = False):
     from oracle import ref as R
     arrays = {}
     with tempfile.TemporaryDirectory() as d:
-        for name in ("pin", "pin_f16"):
+        for name in MODELS:
             spec = synth.preset(name)
             path = synth.model_path(spec, Path(d))
             outs = run_session(spec, R.RefEngine(path, CONTEXT, xtx=xtx))

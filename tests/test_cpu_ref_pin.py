@@ -174,10 +174,10 @@ def test_decode_steps_bit_exact(tmp_path_factory, name):
 def test_oracle_matches_reference_golden(tmp_path_factory):
     """The committed outputs of the reference shaders (tests/golden/make_ref_pin.py) against the
     oracle: the pin without the reference checkout."""
-    from golden.make_ref_pin import run_session
+    from golden.make_ref_pin import MODELS, run_session
     g = np.load(GOLDEN)
     d = tmp_path_factory.mktemp("golden")
-    for name in ("pin", "pin_f16"):
+    for name in MODELS:
         spec = synth.preset(name)
         path = synth.model_path(spec, d)
         import hashlib

@@ -88,7 +88,7 @@ def test_attention_xtx_shaders(D, position):
 
 
 @needs_ref
-@pytest.mark.parametrize("name", ["pin", "pin_f16"])
+@pytest.mark.parametrize("name", ["pin", "pin_f16", "g6"])
 def test_decode_steps_xtx_bit_exact(tmp_path_factory, name):
     """Whole XTX-mode decode steps (embedding and token inputs, logits, KV cache) on the
     emulated shaders and on the oracle."""
@@ -112,10 +112,10 @@ def test_decode_steps_xtx_bit_exact(tmp_path_factory, name):
 def test_oracle_xtx_matches_reference_golden(tmp_path_factory):
     """The committed XTX-mode outputs of the emulated reference shaders against the oracle's
     XTX restatement: the pin without the reference checkout."""
-    from golden.make_ref_pin import CONTEXT, run_session
+    from golden.make_ref_pin import CONTEXT, MODELS, run_session
     g = np.load(GOLDEN)
     d = tmp_path_factory.mktemp("golden_xtx")
-    for name in ("pin", "pin_f16"):
+    for name in MODELS:
         spec = synth.preset(name)
         path = synth.model_path(spec, d)
         assert hashlib.sha256(path.read_bytes()).hexdigest() == str(g[f"{name}_sha256"]), \
