@@ -24,7 +24,7 @@ def test_library_exports_every_header_symbol():
 
 
 def test_inspect_valid_models(model_dir):
-    for name in ("tiny", "tiny_f16", "cfg0"):
+    for name in ("tiny", "tiny_f16", "cfg0", "g6"):
         spec = synth.preset(name)
         info = api.inspect_gguf(spec_path(model_dir, name))
         assert info["embedding_length"] == spec.hidden
